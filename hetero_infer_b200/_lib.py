@@ -1,0 +1,65 @@
+"""ctypes binding of ``libhq4.so`` (the C ABI declared in ``include/hq4.h``).
+
+The binding mirrors how the reference binds its own kernel
+(``hetero/cpu_model.py:33-45``: ``ctypes.CDLL`` plus argtypes of ``c_void_p`` and
+``c_int``).  There is no fallback: if the library is missing the import of any
+op fails with an error naming the build command.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+
+from . import build as _build
+
+_P = ctypes.c_void_p
+_I = ctypes.c_int
+_Z = ctypes.c_size_t
+
+HEADER = os.path.join(_build.INCLUDE, "hq4.h")
+
+# name -> (restype, argtypes); kept in the order of include/hq4.h
+SIGNATURES = {
+    "hq4_version": (_I, []),
+    "hq4_gemv": (_I, [_P] * 5 + [_I] * 4 + [_P]),
+    "hq4_dequant": (_I, [_P] * 4 + [_I] * 4 + [_P]),
+}
+
+ERRORS = {
+    -1: "bad shape (n_in % gs, unsupported gs, or a non-positive size)",
+    -2: "misaligned pointer",
+    -4: "CUDA launch failed",
+    -5: "current device is not sm_100 (B200)",
+}
+
+_lib = None
+
+
+def declared_symbols(header: str = HEADER):
+    """Function names declared in include/hq4.h."""
+    text = open(header).read()
+    return re.findall(r"^\s*(?:int|size_t|void)\s+(hq4_\w+)\s*\(", text, flags=re.M)
+
+
+def load(path: str = None) -> ctypes.CDLL:
+    """Load libhq4.so and attach argtypes; raises if it has not been built."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    path = path or _build.LIB
+    if not os.path.exists(path):
+        raise RuntimeError(f"{path} is missing: build it with `python -m hetero_infer_b200.build` "
+                           "(there is no CPU fallback)")
+    lib = ctypes.CDLL(path)
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = lib
+    return lib
+
+
+def check(rc: int, what: str) -> None:
+    if rc != 0:
+        raise RuntimeError(f"{what} failed with {rc}: {ERRORS.get(rc, 'unknown error')}")

@@ -1,0 +1,516 @@
+// Fused int4 GEMV (decode, one token) and block dequantisation for sm_100a.
+//
+// Device-side replacement for the reference's q4_gemv / q4_dequant
+// (hetero-infer kernel/q4gemv.c:232-301, 303-379).  Same packed layout, same
+// per-group arithmetic:  y[o] = sum_g scale[o,g] * dot_g + bias[o,g] * xsum_g
+// (kernel/q4gemv.c:15-17), with dot_g evaluated on the tensor cores.
+//
+// How one token's GEMV maps onto the hardware
+// -------------------------------------------
+// * A warp works on "tiles" of 16 output rows x 4 lane-groups (KG = 64 or 32
+//   values of K each).  Lane (g = lane/4, t = lane%4) owns lane-group t of the
+//   tile for rows g and g+8 and fetches those two group-rows (KG/2 bytes each)
+//   with one 256-bit (or 128-bit) load each: the weight stream is fully
+//   coalesced, one instruction per group-row.
+// * Nibbles become u8 with three instructions per packed word (mask, shift,
+//   mask) and are the A operand of the integer tensor-core MMA
+//   mma.sync m16n8k32 (u8 x s8 -> s32).  Lane t feeds only its own group's k
+//   positions, so one k-step mixes four groups.
+// * The B operand holds x as a per-group fixed-point integer: with
+//   2^(E-1) <= max|x_group| < 2^E, v = rint(x * 2^(22-E)) has 22 bits plus
+//   sign and is split into three balanced s8 digits (v = d2*2^16 + d1*2^8 +
+//   d0).  Columns 2t / 2t+1 of n-tile 0 carry d2 / d1 of lane-group t and
+//   column 2t of n-tile 1 carries d0, zero elsewhere, so the C registers lane
+//   t holds end the tile as the three exact integer digit-dots of its own
+//   group for rows g and g+8.
+// * The epilogue per group is fp32: dot = (C2*2^16 + C1*2^8 + C0) * 2^(E-22),
+//   acc += scale * dot + bias * xsum, with xsum the group's fp32 sum of x
+//   (kernel/q4gemv.c:244-248).  x is thereby represented to 2^-22 of its group
+//   maximum and every product and integer sum is exact: the result agrees with
+//   the reference float path to fp32 rounding.
+// * Work split: every CTA owns a contiguous run of whole 16-row strips
+//   (balanced to one strip); inside the CTA the (strip, tile) units are split
+//   evenly and contiguously over its 8 warps.  A strip cut between two warps
+//   is reduced through shared memory by the warp holding its last piece,
+//   summing the pieces in warp order: deterministic, and no global scratch,
+//   atomics or fences.
+// * The first D tiles of weights are requested before griddepcontrol.wait,
+//   so with programmatic dependent launch the weight stream starts while the
+//   producer of x is still draining.
+#include <algorithm>
+#include <cstdio>
+
+#include "hq4_common.cuh"
+#include "hq4.h"
+
+namespace hq4 {
+
+constexpr int kGemvThreads = 256;  // 8 warps
+constexpr int kGemvWarps = kGemvThreads / kWarp;
+constexpr int kPrefetch = 3;       // tiles of weights in flight per warp
+
+template <int KG>
+struct M1 {
+    static constexpr int kWords = KG / 8;        // packed words per group-row
+    static constexpr int kKSteps = KG / 8;       // one word per row per k32 step
+    static constexpr int kDigitBytes = KG;       // one s8 digit per value
+    static constexpr int kBRegs = KG / 4;        // B registers per (group, digit)
+    static constexpr int kImgStride = 3 * KG + 16;  // bytes per group: d2|d1|d0|pad
+};
+
+struct GemvM1Params {
+    const uint32_t* w;
+    const uint16_t* sc;
+    const uint16_t* bi;
+    const float* x;
+    float* out;
+    int n_out, n_in;
+    int ng;        // lane-groups per row (n_in / KG)
+    int sg_shift;  // scale index = lane-group >> sg_shift
+    int n_sg;      // scale groups per row (n_in / gs)
+    int n_strips, nq;
+    const float* row_add;   // optional: out[r] += row_add[r]
+    const float* residual;  // optional: out[r] += residual[r]
+};
+
+// Shared memory: [ng x kImgStride image][ng x float2 meta][zero block]
+//                [kGemvWarps x 2 x 16 floats: split-strip partials]
+__host__ __device__ __forceinline__ size_t zero_block_offset(int ng, int stride) {
+    return (size_t)ng * stride + (((size_t)ng * sizeof(float2) + 15) & ~(size_t)15);
+}
+__host__ __device__ __forceinline__ size_t partial_offset(int ng, int stride) {
+    return zero_block_offset(ng, stride) + 64;
+}
+
+__device__ __forceinline__ void store_row(const GemvM1Params& p, int r, float y) {
+    if (r >= p.n_out) return;
+    if (p.row_add) y += p.row_add[r];
+    if (p.residual) y += p.residual[r];
+    p.out[r] = y;
+}
+
+// Sum a strip's lane partials across the 4 lanes t; store it when this warp
+// owns the whole strip, else park it in the warp's head/tail smem slot.
+__device__ __forceinline__ void flush_strip(const GemvM1Params& p, int s, bool full, float* slot,
+                                            float acc0, float acc1, int lane) {
+    acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
+    acc0 += __shfl_xor_sync(0xffffffffu, acc0, 2);
+    acc1 += __shfl_xor_sync(0xffffffffu, acc1, 1);
+    acc1 += __shfl_xor_sync(0xffffffffu, acc1, 2);
+    const int g = lane >> 2, t = lane & 3;
+    if (t != 0) return;
+    if (full) {
+        store_row(p, s * 16 + g, acc0);
+        store_row(p, s * 16 + g + 8, acc1);
+    } else {
+        slot[g] = acc0;
+        slot[g + 8] = acc1;
+    }
+}
+
+// Per-CTA x image: for every lane-group, three s8 digit blocks (d2, d1, d0)
+// of KG bytes, each in k-step order with the values of a packed word
+// permuted as the u8 unpack produces them ({0,2,4,6} then {1,3,5,7}), plus
+// (2^(E-22), xsum) per group.
+template <int KG>
+__device__ __forceinline__ void build_x_image(const float* __restrict__ x, int ng,
+                                              unsigned char* img, float2* meta) {
+    using C = M1<KG>;
+    constexpr int kPer = KG / 4;  // values per thread: 4 threads per lane-group
+    const int ntask = ng * 4;
+    for (int base = 0; base < ntask; base += kGemvThreads) {
+        const int task = base + threadIdx.x;
+        const bool ok = task < ntask;
+        const int G = task >> 2, qq = task & 3;
+        float v[kPer];
+        if (ok) {
+            const float4* xp = reinterpret_cast<const float4*>(x + (size_t)G * KG + qq * kPer);
+#pragma unroll
+            for (int i = 0; i < kPer / 4; i++) {
+                float4 f = xp[i];
+                v[4 * i] = f.x; v[4 * i + 1] = f.y; v[4 * i + 2] = f.z; v[4 * i + 3] = f.w;
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < kPer; i++) v[i] = 0.0f;
+        }
+        float amax = 0.0f, s = 0.0f;
+#pragma unroll
+        for (int i = 0; i < kPer; i++) {
+            amax = fmaxf(amax, fabsf(v[i]));
+            s += v[i];
+        }
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+        s += __shfl_xor_sync(0xffffffffu, s, 1);
+        s += __shfl_xor_sync(0xffffffffu, s, 2);
+        const int E = group_exponent(amax);
+        const float up = exp2i(22 - E);
+        if (ok) {
+            unsigned char* gbase = img + (size_t)G * C::kImgStride;
+#pragma unroll
+            for (int j = 0; j < kPer / 8; j++) {
+                const int word = qq * (kPer / 8) + j;
+                uint32_t d2[2] = {0u, 0u}, d1[2] = {0u, 0u}, d0[2] = {0u, 0u};
+#pragma unroll
+                for (int k = 0; k < 8; k++) {
+                    // byte slot of value k in the unpacked order {0,2,4,6,1,3,5,7}
+                    const int slot = (k & 1) * 4 + (k >> 1);
+                    uint32_t a2, a1, a0;
+                    digits3(__float2int_rn(v[8 * j + k] * up), a2, a1, a0);
+                    d2[slot >> 2] |= a2 << (8 * (slot & 3));
+                    d1[slot >> 2] |= a1 << (8 * (slot & 3));
+                    d0[slot >> 2] |= a0 << (8 * (slot & 3));
+                }
+                *reinterpret_cast<uint2*>(gbase + 0 * KG + word * 8) = make_uint2(d2[0], d2[1]);
+                *reinterpret_cast<uint2*>(gbase + 1 * KG + word * 8) = make_uint2(d1[0], d1[1]);
+                *reinterpret_cast<uint2*>(gbase + 2 * KG + word * 8) = make_uint2(d0[0], d0[1]);
+            }
+            if (qq == 0) meta[G] = make_float2(exp2i(E - 22), s);
+        }
+    }
+}
+
+template <int KG>
+__global__ void __launch_bounds__(kGemvThreads, 2) gemv_m1_kernel(const GemvM1Params p) {
+    using C = M1<KG>;
+    constexpr int D = kPrefetch;
+    extern __shared__ __align__(16) unsigned char smem[];
+    unsigned char* img = smem;
+    float2* meta = reinterpret_cast<float2*>(smem + (size_t)p.ng * C::kImgStride);
+
+    pdl_launch_dependents();
+
+    const int lane = threadIdx.x & 31;
+    const int g = lane >> 2, t = lane & 3;
+    const int wj = threadIdx.x >> 5;
+    // this CTA's strips, and this warp's contiguous share of their units
+    const int s0 = (int)((long long)blockIdx.x * p.n_strips / gridDim.x);
+    const int s1 = (int)((long long)(blockIdx.x + 1) * p.n_strips / gridDim.x);
+    const int cu0 = s0 * p.nq, nunits = (s1 - s0) * p.nq;
+    const int wa = nunits < kGemvWarps ? nunits : kGemvWarps;  // warps with work
+    const int u0 = wj < wa ? cu0 + (int)((long long)wj * nunits / wa) : cu0 + nunits;
+    const int u1 = wj < wa ? cu0 + (int)((long long)(wj + 1) * nunits / wa) : cu0 + nunits;
+    const size_t wpr = (size_t)(p.n_in >> 3);
+    float* partials = reinterpret_cast<float*>(smem + partial_offset(p.ng, C::kImgStride));
+
+    uint32_t wv[D][2][C::kWords];
+    uint32_t sv[D][4];
+
+    // load cursor: strip ls, tile lq; lp points at this lane's row-g group-row
+    int ls = u0 / p.nq, lq = u0 - ls * p.nq;
+    const uint32_t* lp = p.w + (size_t)(ls * 16 + g) * wpr + (size_t)(lq * 4 + t) * C::kWords;
+    auto issue = [&](uint32_t (&wr)[2][C::kWords], uint32_t (&sr)[4], bool live) {
+        const int r0 = ls * 16 + g;
+        const int G = lq * 4 + t;
+        const bool gok = live && G < p.ng;
+        const bool ok0 = gok && r0 < p.n_out, ok1 = gok && r0 + 8 < p.n_out;
+        if constexpr (C::kWords == 8) {
+            if (ok0) ldg256_stream(lp, wr[0]);
+            else
+#pragma unroll
+                for (int i = 0; i < 8; i++) wr[0][i] = 0u;
+            if (ok1) ldg256_stream(lp + 8 * wpr, wr[1]);
+            else
+#pragma unroll
+                for (int i = 0; i < 8; i++) wr[1][i] = 0u;
+        } else {
+            if (ok0) ldg128_stream(lp, wr[0]);
+            else
+#pragma unroll
+                for (int i = 0; i < 4; i++) wr[0][i] = 0u;
+            if (ok1) ldg128_stream(lp + 8 * wpr, wr[1]);
+            else
+#pragma unroll
+                for (int i = 0; i < 4; i++) wr[1][i] = 0u;
+        }
+        const size_t si = (size_t)r0 * p.n_sg + (G >> p.sg_shift);
+        sr[0] = ok0 ? ldg_u16(p.sc + si) : 0u;
+        sr[1] = ok0 ? ldg_u16(p.bi + si) : 0u;
+        sr[2] = ok1 ? ldg_u16(p.sc + si + (size_t)8 * p.n_sg) : 0u;
+        sr[3] = ok1 ? ldg_u16(p.bi + si + (size_t)8 * p.n_sg) : 0u;
+        if (live) {
+            lp += 4 * C::kWords;
+            if (++lq == p.nq) {
+                lq = 0;
+                ++ls;
+                lp = p.w + (size_t)(ls * 16 + g) * wpr + (size_t)t * C::kWords;
+            }
+        }
+    };
+
+#pragma unroll
+    for (int d = 0; d < D; d++) issue(wv[d], sv[d], u0 + d < u1);
+
+    // x image in shared memory (needs the producer of x)
+    pdl_wait();
+    build_x_image<KG>(p.x, p.ng, img, meta);
+    {
+        uint4* z = reinterpret_cast<uint4*>(smem + zero_block_offset(p.ng, C::kImgStride));
+        if (threadIdx.x < KG / 16) z[threadIdx.x] = make_uint4(0, 0, 0, 0);
+    }
+    __syncthreads();
+
+    // B operand: lanes g == 2t read digits d2 (n-tile 0) and d0 (n-tile 1) of
+    // their lane-group, lanes g == 2t+1 read d1 (n-tile 0); every other slot
+    // reads the shared zero block (a broadcast), so no lane branches.
+    const int role = (g >> 1) == t ? (g & 1) + 1 : 0;  // 1: d2+d0, 2: d1, 0: none
+    const unsigned char* zero_blk = smem + zero_block_offset(p.ng, C::kImgStride);
+    const int off0 = role == 1 ? 0 : KG;      // d2 or d1
+    const int off1 = 2 * KG;                  // d0
+
+    int cs = u0 / p.nq, cq = u0 - cs * p.nq;
+    float acc0 = 0.0f, acc1 = 0.0f;
+    for (int ub = u0; ub < u1; ub += D) {
+#pragma unroll
+        for (int d = 0; d < D; d++) {
+            const int u = ub + d;
+            if (u >= u1) break;
+            const int G = cq * 4 + t;
+            const bool gok = G < p.ng;
+            const unsigned char* gb = img + (size_t)(gok ? G : p.ng - 1) * C::kImgStride;
+            const uint4* src0 = reinterpret_cast<const uint4*>(role ? gb + off0 : zero_blk);
+            const uint4* src1 = reinterpret_cast<const uint4*>(role == 1 ? gb + off1 : zero_blk);
+            int c0[4] = {0, 0, 0, 0}, c1[4] = {0, 0, 0, 0};
+            uint4 q0 = make_uint4(0, 0, 0, 0), q1 = q0;
+#pragma unroll
+            for (int ks = 0; ks < C::kKSteps; ks++) {
+                if ((ks & 1) == 0) {
+                    q0 = src0[ks >> 1];
+                    q1 = src1[ks >> 1];
+                }
+                const uint32_t b00 = (ks & 1) ? q0.z : q0.x, b01 = (ks & 1) ? q0.w : q0.y;
+                const uint32_t b10 = (ks & 1) ? q1.z : q1.x, b11 = (ks & 1) ? q1.w : q1.y;
+                uint32_t a0, a1, a2, a3;
+                unpack_u8(wv[d][0][ks], a0, a2);
+                unpack_u8(wv[d][1][ks], a1, a3);
+                mma_u8s8_16832(c0, a0, a1, a2, a3, b00, b01);
+                mma_u8s8_16832(c1, a0, a1, a2, a3, b10, b11);
+            }
+            if (gok) {
+                const float2 m = meta[G];
+                const float dot0 = fmaf((float)c0[0], 65536.0f, fmaf((float)c0[1], 256.0f, (float)c1[0]));
+                const float dot1 = fmaf((float)c0[2], 65536.0f, fmaf((float)c0[3], 256.0f, (float)c1[2]));
+                acc0 = fmaf(h2f(sv[d][0]) * m.x, dot0, acc0);
+                acc0 = fmaf(h2f(sv[d][1]), m.y, acc0);
+                acc1 = fmaf(h2f(sv[d][2]) * m.x, dot1, acc1);
+                acc1 = fmaf(h2f(sv[d][3]), m.y, acc1);
+            }
+            // refill this stage with the tile D ahead
+            issue(wv[d], sv[d], u + D < u1);
+            if (++cq == p.nq) {
+                const bool head = cs * p.nq < u0;  // started before this warp's range
+                flush_strip(p, cs, !head, partials + (wj * 2 + (head ? 0 : 1)) * 16, acc0, acc1, lane);
+                acc0 = acc1 = 0.0f;
+                cq = 0;
+                ++cs;
+            }
+        }
+    }
+    if (cq != 0) {  // range ends inside a strip: slot 0 if it also began in it
+        const int slot = cs * p.nq <= u0 ? 0 : 1;
+        flush_strip(p, cs, false, partials + (wj * 2 + slot) * 16, acc0, acc1, lane);
+    }
+    // split strips: the warp holding a strip's last piece sums the pieces in
+    // warp order
+    __syncthreads();
+    if (u0 < u1) {
+        const int sf = u0 / p.nq;  // first strip of this warp
+        const int first_unit = sf * p.nq, last_unit = first_unit + p.nq - 1;
+        auto warp_of = [&](int u) {  // warp whose (nonempty) range holds unit u
+            return (int)(((long long)(u - cu0 + 1) * wa - 1) / nunits);
+        };
+        const int wf = warp_of(first_unit), wl = warp_of(last_unit);
+        if (wf != wl && wl == wj && t == 0) {
+            float y0 = 0.0f, y1 = 0.0f;
+            for (int k = wf; k <= wl; k++) {
+                const int k_first_strip = (cu0 + (int)((long long)k * nunits / wa)) / p.nq;
+                const float* sl = partials + (k * 2 + (k_first_strip == sf ? 0 : 1)) * 16;
+                y0 += sl[g];
+                y1 += sl[g + 8];
+            }
+            store_row(p, sf * 16 + g, y0);
+            store_row(p, sf * 16 + g + 8, y1);
+        }
+    }
+}
+
+// ---- block dequantisation ------------------------------------------------
+// One thread per packed word; out rows are relative to row0.
+__global__ void dequant_kernel(const uint32_t* __restrict__ w, const uint16_t* __restrict__ sc,
+                               const uint16_t* __restrict__ bi, float* __restrict__ out, int row0,
+                               int rows, int n_in, int gs) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const int wpr = n_in >> 3, n_sg = n_in / gs;
+    const long long total = (long long)rows * wpr;
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (long long)gridDim.x * blockDim.x) {
+        const int rr = (int)(i / wpr), k = (int)(i - (long long)rr * wpr);
+        const int r = row0 + rr;
+        const uint32_t q = w[(size_t)r * wpr + k];
+        const int si = (k * 8) / gs;
+        const float s = h2f(sc[(size_t)r * n_sg + si]);
+        const float b = h2f(bi[(size_t)r * n_sg + si]);
+        float o[8];
+#pragma unroll
+        for (int j = 0; j < 8; j++) o[j] = __fadd_rn(__fmul_rn((float)((q >> (4 * j)) & 0xFu), s), b);
+        float4* dst = reinterpret_cast<float4*>(out + (size_t)rr * n_in + (size_t)k * 8);
+        dst[0] = make_float4(o[0], o[1], o[2], o[3]);
+        dst[1] = make_float4(o[4], o[5], o[6], o[7]);
+    }
+}
+
+// ---- host side -------------------------------------------------------------
+struct GemvPlan {
+    int kg, sg_shift, ng, n_sg, n_strips, nq, grid;
+    size_t smem;
+};
+
+static int sm_count() {
+    static int cached = -1;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+        n = 148;
+    cached = n;
+    return cached;
+}
+
+static int log2_exact(int v) {
+    int s = 0;
+    while ((1 << s) < v) s++;
+    return (1 << s) == v ? s : -1;
+}
+
+// Returns 0 and fills the plan, or HQ4_ERR_SHAPE.
+static int plan_gemv(int n_out, int n_in, int gs, GemvPlan& pl) {
+    if (n_out <= 0 || n_in <= 0 || gs <= 0 || n_in % gs) return HQ4_ERR_SHAPE;
+    if (gs == 32) {
+        pl.kg = 32;
+        pl.sg_shift = 0;
+    } else if (gs % 64 == 0 && log2_exact(gs / 64) >= 0) {
+        pl.kg = 64;
+        pl.sg_shift = log2_exact(gs / 64);
+    } else {
+        return HQ4_ERR_SHAPE;
+    }
+    pl.ng = n_in / pl.kg;
+    pl.n_sg = n_in / gs;
+    pl.n_strips = (n_out + 15) / 16;
+    pl.nq = (pl.ng + 3) / 4;
+    if ((long long)pl.n_strips * pl.nq > (1LL << 30)) return HQ4_ERR_SHAPE;
+    const int stride = pl.kg == 64 ? M1<64>::kImgStride : M1<32>::kImgStride;
+    pl.smem = partial_offset(pl.ng, stride) + (size_t)kGemvWarps * 2 * 16 * sizeof(float);
+    if (pl.smem > 220 * 1024) return HQ4_ERR_SHAPE;  // x image must fit one CTA
+    const int ctas_per_sm = pl.smem <= 100 * 1024 ? 2 : 1;
+    const int max_grid = sm_count() * ctas_per_sm;
+    // whole strips per CTA; enough of them that each warp gets a unit
+    const int min_strips = (kGemvWarps + pl.nq - 1) / pl.nq;
+    pl.grid = std::max(1, std::min(max_grid, pl.n_strips / min_strips));
+    return HQ4_OK;
+}
+
+static int check_device() {
+    static int ok = -1;
+    if (ok < 0) {
+        int dev = 0, major = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+        ok = major == 10 ? 1 : 0;
+    }
+    return ok ? HQ4_OK : HQ4_ERR_DEVICE;
+}
+
+template <int KG>
+static int launch_m1(const GemvPlan& pl, const GemvM1Params& prm, cudaStream_t st) {
+    auto kern = gemv_m1_kernel<KG>;
+    static bool attr_set = false;
+    if (!attr_set) {
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
+        attr_set = true;
+    }
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t lc = {};
+    lc.gridDim = dim3(pl.grid);
+    lc.blockDim = dim3(kGemvThreads);
+    lc.dynamicSmemBytes = pl.smem;
+    lc.stream = st;
+    lc.attrs = attr;
+    lc.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&lc, kern, prm);
+    return e == cudaSuccess ? HQ4_OK : HQ4_ERR_LAUNCH;
+}
+
+int gemv_m1(const uint32_t* w, const uint16_t* scales, const uint16_t* biases, const float* x,
+            float* out, int n_out, int n_in, int gs, const float* row_add, const float* residual,
+            cudaStream_t st) {
+    GemvPlan pl;
+    int rc = plan_gemv(n_out, n_in, gs, pl);
+    if (rc) return rc;
+    if (((uintptr_t)w & 31) || ((uintptr_t)x & 15) || ((uintptr_t)out & 3)) return HQ4_ERR_ALIGN;
+    GemvM1Params prm;
+    prm.w = w;
+    prm.sc = scales;
+    prm.bi = biases;
+    prm.x = x;
+    prm.out = out;
+    prm.n_out = n_out;
+    prm.n_in = n_in;
+    prm.ng = pl.ng;
+    prm.sg_shift = pl.sg_shift;
+    prm.n_sg = pl.n_sg;
+    prm.n_strips = pl.n_strips;
+    prm.nq = pl.nq;
+    prm.row_add = row_add;
+    prm.residual = residual;
+    return pl.kg == 64 ? launch_m1<64>(pl, prm, st) : launch_m1<32>(pl, prm, st);
+}
+
+}  // namespace hq4
+
+using namespace hq4;
+
+extern "C" int hq4_version(void) { return (0 << 16) | 1; }
+
+
+extern "C" int hq4_gemv(const uint32_t* w, const uint16_t* scales, const uint16_t* biases,
+                        const float* x, float* out, int n_out, int n_in, int gs, int m,
+                        void* stream) {
+    if (int rc = check_device()) return rc;
+    if (m <= 0) return HQ4_ERR_SHAPE;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    for (int i = 0; i < m; i++) {
+        int rc = gemv_m1(w, scales, biases, x + (size_t)i * n_in, out + (size_t)i * n_out, n_out,
+                         n_in, gs, nullptr, nullptr, st);
+        if (rc) return rc;
+    }
+    return HQ4_OK;
+}
+
+extern "C" int hq4_dequant(const uint32_t* w, const uint16_t* scales, const uint16_t* biases,
+                           float* out, int row0, int row1, int n_in, int gs, void* stream) {
+    if (int rc = check_device()) return rc;
+    if (n_in <= 0 || gs <= 0 || n_in % gs || gs % 8 || row0 < 0) return HQ4_ERR_SHAPE;
+    const int rows = row1 - row0;
+    if (rows <= 0) return HQ4_OK;
+    if (((uintptr_t)out & 15) || ((uintptr_t)w & 3)) return HQ4_ERR_ALIGN;
+    const long long total = (long long)rows * (n_in / 8);
+    const int threads = 256;
+    const long long want = (total + threads - 1) / threads;
+    const int grid = (int)std::min<long long>(want, (long long)sm_count() * 16);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t lc = {};
+    lc.gridDim = dim3(grid);
+    lc.blockDim = dim3(threads);
+    lc.stream = static_cast<cudaStream_t>(stream);
+    lc.attrs = attr;
+    lc.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&lc, dequant_kernel, w, scales, biases, out, row0, rows, n_in, gs);
+    return e == cudaSuccess ? HQ4_OK : HQ4_ERR_LAUNCH;
+}

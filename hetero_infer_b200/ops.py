@@ -1,0 +1,70 @@
+"""Torch-facing wrappers of the hq4 kernels.
+
+PyTorch provides device memory and the current CUDA stream; the arithmetic is
+all in ``libhq4.so``.  Every op checks that its tensors are CUDA, contiguous and
+of the dtype the C ABI expects, and raises instead of computing anything on the
+CPU.
+"""
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+
+from . import _lib
+
+
+def _stream_ptr(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _need_cuda(t: torch.Tensor, name: str, dtype=None) -> None:
+    if not t.is_cuda:
+        raise RuntimeError(f"{name} must be a CUDA tensor (no CPU fallback)")
+    if not t.is_contiguous():
+        raise RuntimeError(f"{name} must be contiguous")
+    if dtype is not None and t.dtype != dtype:
+        raise RuntimeError(f"{name} must be {dtype}, got {t.dtype}")
+
+
+def q4_gemv(w: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor, x: torch.Tensor,
+            group_size: int = 64, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``out[m, n_out] = x[m, n_in] @ dequant(w).T`` on the GPU (hq4_gemv).
+
+    w: uint32/int32 [n_out, n_in/8]; scales, biases: fp16 [n_out, n_in/gs];
+    x: fp32 [..., n_in]."""
+    lib = _lib.load()
+    _need_cuda(w, "w")
+    if w.dtype not in (torch.int32, torch.uint32):
+        raise RuntimeError("w must hold packed uint32 words")
+    _need_cuda(scales, "scales", torch.float16)
+    _need_cuda(biases, "biases", torch.float16)
+    n_out, n_in = w.shape[0], w.shape[1] * 8
+    xf = x.reshape(-1, n_in)
+    _need_cuda(xf, "x", torch.float32)
+    m = xf.shape[0]
+    if out is None:
+        out = torch.empty((m, n_out), dtype=torch.float32, device=x.device)
+    _need_cuda(out, "out", torch.float32)
+    rc = lib.hq4_gemv(w.data_ptr(), scales.data_ptr(), biases.data_ptr(), xf.data_ptr(),
+                      out.data_ptr(), n_out, n_in, group_size, m, _stream_ptr(x.device))
+    _lib.check(rc, "hq4_gemv")
+    return out.reshape(*x.shape[:-1], n_out)
+
+
+def q4_dequant(w: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor, row0: int, row1: int,
+               group_size: int = 64, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """fp32 expansion of rows [row0, row1) (hq4_dequant)."""
+    lib = _lib.load()
+    _need_cuda(w, "w")
+    _need_cuda(scales, "scales", torch.float16)
+    _need_cuda(biases, "biases", torch.float16)
+    n_in = w.shape[1] * 8
+    rows = max(row1 - row0, 0)
+    if out is None:
+        out = torch.empty((rows, n_in), dtype=torch.float32, device=w.device)
+    _need_cuda(out, "out", torch.float32)
+    rc = lib.hq4_dequant(w.data_ptr(), scales.data_ptr(), biases.data_ptr(), out.data_ptr(),
+                         row0, row1, n_in, group_size, _stream_ptr(w.device))
+    _lib.check(rc, "hq4_dequant")
+    return out

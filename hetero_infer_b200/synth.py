@@ -1,0 +1,143 @@
+"""Seeded synthetic weights in the reference's packed int4 layout.
+
+There is no checkpoint on the GPU box and no network, so every benchmark and
+parity case runs on random weights with the shapes and value distributions the
+benchmark configurations name:
+
+* linear weights: uniform random nibbles 0-15, eight per little-endian uint32
+  along K, low nibble first (MLX affine layout, ``kernel/q4gemv.c:7-11``);
+* per group of ``gs`` along K: an fp16 scale ``|N(0,1)| * 0.01`` and an fp16
+  bias equal to ``-8 * scale`` (exact in fp16);
+* embeddings fp16 ``N(0, 0.02)``, RMSNorm weights ones, q/k/v biases fp16
+  ``N(0, 0.02)`` (qwen2 has them; ``hetero/cpu_model.py:266`` reads them with
+  ``w.get``).
+
+Every tensor draws from its own ``numpy.random.default_rng([seed, crc32(name)])``
+stream, so one tensor (or one layer) can be regenerated alone and the values do
+not depend on which other tensors were generated before it.
+"""
+from __future__ import annotations
+
+import zlib
+from typing import Dict, Iterable, Optional
+
+import numpy as np
+
+QWEN2_7B = {
+    "model_type": "qwen2",
+    "hidden_size": 3584,
+    "num_hidden_layers": 28,
+    "num_attention_heads": 28,
+    "num_key_value_heads": 4,
+    "intermediate_size": 18944,
+    "vocab_size": 152064,
+    "rms_norm_eps": 1e-6,
+    "rope_theta": 1e6,
+    "tie_word_embeddings": False,
+    "quantization": {"group_size": 64, "bits": 4},
+}
+
+# The seven int4 projections of one decoder layer: (name, n_out, n_in) as
+# functions of the config (hetero/cpu_model.py:263-289).
+PROJ_NAMES = ("q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj")
+
+
+def small_config(layers: int = 2, hidden: int = 256, heads: int = 4, kv_heads: int = 2,
+                 inter: int = 512, vocab: int = 1024, gs: int = 64) -> dict:
+    """A qwen2 config with the same structure at test-friendly sizes."""
+    cfg = dict(QWEN2_7B)
+    cfg.update(hidden_size=hidden, num_hidden_layers=layers, num_attention_heads=heads,
+               num_key_value_heads=kv_heads, intermediate_size=inter, vocab_size=vocab,
+               quantization={"group_size": gs, "bits": 4})
+    return cfg
+
+
+def proj_shapes(cfg: dict) -> Dict[str, tuple]:
+    h = cfg["hidden_size"]
+    hd = h // cfg["num_attention_heads"]
+    kv = cfg["num_key_value_heads"] * hd
+    i = cfg["intermediate_size"]
+    return {"q_proj": (h, h), "k_proj": (kv, h), "v_proj": (kv, h), "o_proj": (h, h),
+            "gate_proj": (i, h), "up_proj": (i, h), "down_proj": (h, i)}
+
+
+def rng_for(seed: int, name: str) -> np.random.Generator:
+    return np.random.default_rng([int(seed), zlib.crc32(name.encode())])
+
+
+def q4_tensor(rng: np.random.Generator, n_out: int, n_in: int, gs: int = 64):
+    """(w uint32 [n_out, n_in/8], scales fp16 [n_out, n_in/gs], biases fp16)."""
+    if n_in % gs or n_in % 8:
+        raise ValueError(f"n_in={n_in} must be a multiple of gs={gs} and of 8")
+    n_words = n_out * (n_in // 8)
+    if n_words % 2 == 0:
+        # raw 64-bit draws split into two words: uniform bits, ~20x faster than
+        # Generator.integers for the ~1e9 words of the 7B-shape model
+        w = rng.bit_generator.random_raw(n_words // 2).view("<u4").reshape(n_out, n_in // 8)
+        w = w.astype(np.uint32, copy=False)
+    else:
+        w = rng.integers(0, 2 ** 32, size=(n_out, n_in // 8), dtype=np.uint32)
+    s = (np.abs(rng.standard_normal((n_out, n_in // gs), dtype=np.float32)) * 0.01)
+    s = s.astype(np.float16)
+    b = (s.astype(np.float32) * -8.0).astype(np.float16)
+    return w, s, b
+
+
+def q4_linear(seed: int, name: str, n_out: int, n_in: int, gs: int = 64):
+    return q4_tensor(rng_for(seed, name), n_out, n_in, gs)
+
+
+def fp16_normal(seed: int, name: str, shape, std: float = 0.02) -> np.ndarray:
+    r = rng_for(seed, name)
+    return (r.standard_normal(shape, dtype=np.float32) * std).astype(np.float16)
+
+
+def activation(seed: int, name: str, shape, dtype=np.float32) -> np.ndarray:
+    return rng_for(seed, name).standard_normal(shape, dtype=np.float32).astype(dtype)
+
+
+def layer_weights(cfg: dict, seed: int, idx: int, qkv_bias: bool = True) -> Dict[str, np.ndarray]:
+    """Tensors of decoder layer ``idx`` under their checkpoint names."""
+    gs = cfg["quantization"]["group_size"]
+    p = f"model.layers.{idx}"
+    out: Dict[str, np.ndarray] = {}
+    for proj, (n_out, n_in) in proj_shapes(cfg).items():
+        sub = "self_attn" if proj in ("q_proj", "k_proj", "v_proj", "o_proj") else "mlp"
+        name = f"{p}.{sub}.{proj}"
+        w, s, b = q4_linear(seed, name, n_out, n_in, gs)
+        out[f"{name}.weight"], out[f"{name}.scales"], out[f"{name}.biases"] = w, s, b
+        if qkv_bias and proj in ("q_proj", "k_proj", "v_proj"):
+            out[f"{name}.bias"] = fp16_normal(seed, f"{name}.bias", (n_out,))
+    h = cfg["hidden_size"]
+    out[f"{p}.input_layernorm.weight"] = np.ones(h, np.float16)
+    out[f"{p}.post_attention_layernorm.weight"] = np.ones(h, np.float16)
+    return out
+
+
+def model_weights(cfg: dict, seed: int, layers: Optional[Iterable[int]] = None,
+                  embed: bool = True, head: bool = True,
+                  qkv_bias: bool = True) -> Dict[str, np.ndarray]:
+    """All tensors a stage owning ``layers`` (and optionally embed/head) needs.
+
+    The embedding is an fp16 table ``model.embed_tokens.table`` (the benchmark
+    configuration asks for fp16 N(0, 0.02) embeddings rather than a quantised
+    table)."""
+    if layers is None:
+        layers = range(cfg["num_hidden_layers"])
+    out: Dict[str, np.ndarray] = {}
+    if embed:
+        out["model.embed_tokens.table"] = fp16_normal(
+            seed, "model.embed_tokens.table", (cfg["vocab_size"], cfg["hidden_size"]))
+    for i in layers:
+        out.update(layer_weights(cfg, seed, i, qkv_bias))
+    if head:
+        gs = cfg["quantization"]["group_size"]
+        w, s, b = q4_linear(seed, "lm_head", cfg["vocab_size"], cfg["hidden_size"], gs)
+        out["lm_head.weight"], out["lm_head.scales"], out["lm_head.biases"] = w, s, b
+        out["model.norm.weight"] = np.ones(cfg["hidden_size"], np.float16)
+    return out
+
+
+def prompt_ids(seed: int, n: int, vocab: int) -> np.ndarray:
+    """Uniform-random prompt token ids, shape [1, n]."""
+    return rng_for(seed, "prompt").integers(0, vocab, size=(1, n)).astype(np.int64)
