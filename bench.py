@@ -1,0 +1,463 @@
+#!/usr/bin/env python
+"""Benchmark of the fused int4 GEMV hot path on B200.
+
+Metric: q4 GEMV achieved HBM GB/s on the int4 projections of one
+Qwen2-7B-shape decoder layer at batch 1 (the benchmark's second config: q
+3584->3584, k/v 3584->512, o 3584->3584, gate/up 3584->18944, down
+18944->3584, group size 64).  A step is one pass of the layer's projections
+as the device stage launches them: q|k|v (one launch, rows concatenated), o,
+gate|up (one launch), down -- four launches of the GEMV kernel, each from its
+own fp32 activation row.  Weights are random (synthetic, seeded) in the
+reference's packed layout; four copies of the layer (526 MB, larger than the
+126 MB L2) rotate between steps so every step streams from HBM.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+N > 1 is launched by torchrun, one rank per GPU; every rank runs its own
+copy of the workload (weak scaling) and the time is the max over ranks.
+`--impl reference` times the reference's own CPU kernel (kernel/q4gemv.c,
+built from source into oracle/_ref/) on the host cores for the same metric.
+Prints one JSON line (rank 0).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+GS = 64
+HIDDEN, INTER, KV = 3584, 18944, 512
+# (name, n_out, n_in) as the stage launches them
+LAUNCHES = [("qkv", HIDDEN + 2 * KV, HIDDEN), ("o", HIDDEN, HIDDEN),
+            ("gate_up", 2 * INTER, HIDDEN), ("down", HIDDEN, INTER)]
+# the seven projections of the layer, each as its own GEMV
+PROJECTIONS = [("q", HIDDEN, HIDDEN), ("k", KV, HIDDEN), ("v", KV, HIDDEN), ("o", HIDDEN, HIDDEN),
+               ("gate", INTER, HIDDEN), ("up", INTER, HIDDEN), ("down", HIDDEN, INTER)]
+COPIES = 4
+METRIC = "q4 GEMV achieved HBM GB/s (Qwen2-7B-shape layer int4 projections, batch 1)"
+WORKLOAD = "qwen2-7b-layer-int4-projections-m1"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def alg_bytes(n_out: int, n_in: int, gs: int = GS, m: int = 1) -> int:
+    """Algorithmic bytes of one GEMV: packed weights + fp16 scales and biases +
+    fp32 x + fp32 out."""
+    return n_out * n_in // 2 + n_out * (n_in // gs) * 4 + m * n_in * 4 + m * n_out * 4
+
+
+STEP_BYTES = sum(alg_bytes(n, k) for _, n, k in LAUNCHES)
+LAYER_BYTES = sum(alg_bytes(n, k) for _, n, k in PROJECTIONS)
+
+
+def config_dict():
+    return {"workload": WORKLOAD, "hidden": HIDDEN, "intermediate": INTER, "kv_rows": KV,
+            "group_size": GS, "batch_tokens": 1,
+            "launches": [f"{n}:{r}x{k}" for n, r, k in LAUNCHES],
+            "l2": f"{COPIES} rotating weight copies ({COPIES * LAYER_BYTES / 1e6:.0f} MB) > 126 MB L2"}
+
+
+def measured_peak():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except (OSError, ValueError, KeyError):
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def profiled_traffic():
+    """DRAM bytes per GEMV launch of the layer step, from the committed ncu
+    summary (profiles/gemv_m1_layer_step.md), or None."""
+    path = os.path.join(ROOT, "profiles", "gemv_m1_layer_step.md")
+    try:
+        for line in open(path):
+            if line.startswith("traffic_bytes_per_launch:"):
+                return float(line.split(":", 1)[1].split()[0])
+    except OSError:
+        pass
+    return None
+
+
+# ---------------------------------------------------------------- clocks
+class ClockSampler:
+    """Samples SM clock and throttle reasons through NVML while running."""
+
+    REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+               0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+               0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting"}
+
+    def __init__(self, index: int, period_s: float = 0.02):
+        self.samples = []
+        self.period = period_s
+        self.stop_ev = threading.Event()
+        self.ok = False
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception:
+            self.max_mhz = None
+        self.thread = threading.Thread(target=self._run, daemon=True)
+
+    def _run(self):
+        while not self.stop_ev.is_set():
+            try:
+                mhz = self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM)
+                rs = self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                self.samples.append((time.perf_counter(), mhz, rs))
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self.ok:
+            self.thread.start()
+        return self
+
+    def __exit__(self, *a):
+        self.stop_ev.set()
+        if self.ok:
+            self.thread.join(timeout=1.0)
+
+    def summary(self, t0: float, t1: float):
+        if not self.ok:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvml unavailable"]}
+        inside = [s for s in self.samples if t0 <= s[0] <= t1]
+        used = inside or [min(self.samples, key=lambda s: abs(s[0] - (t0 + t1) / 2))] if self.samples else []
+        reasons = set()
+        for _, _, rs in used:
+            for bit, name in self.REASONS.items():
+                if rs & bit and name != "gpu_idle":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median([s[1] for s in used]) if used else None,
+                "sm_max_mhz": self.max_mhz, "reasons": sorted(reasons),
+                "samples_in_timed_region": len(inside)}
+
+
+# ---------------------------------------------------------------- ours
+def run_ours(args, rank: int, world: int, local_rank: int):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from hetero_infer_b200 import _lib, cuda_model, synth
+
+    lib = _lib.load()
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(1234 + rank)
+
+    def q4_on_device(n_out, n_in):
+        w = torch.randint(-2 ** 31, 2 ** 31 - 1, (n_out, n_in // 8), dtype=torch.int32, device=dev,
+                          generator=gen)
+        s = (torch.randn(n_out, n_in // GS, device=dev, generator=gen).abs() * 0.01).half()
+        b = (s.float() * -8.0).half()
+        return w, s, b
+
+    copies = [{name: q4_on_device(n, k) for name, n, k in LAUNCHES} for _ in range(COPIES)]
+    xs = {name: torch.randn(1, k, device=dev, generator=gen) for name, n, k in LAUNCHES}
+    outs = {name: torch.empty(1, n, device=dev) for name, n, k in LAUNCHES}
+    stream = torch.cuda.Stream(dev)
+
+    def launch(name, n, k, wsb, x, out):
+        w, s, b = wsb
+        rc = lib.hq4_gemv(w.data_ptr(), s.data_ptr(), b.data_ptr(), x.data_ptr(), out.data_ptr(),
+                          n, k, GS, 1, stream.cuda_stream)
+        _lib.check(rc, "hq4_gemv")
+
+    def step(c):
+        for name, n, k in LAUNCHES:
+            launch(name, n, k, copies[c][name], xs[name], outs[name])
+
+    # one graph per weight copy (one step each) and one covering all copies
+    graphs = []
+    with torch.cuda.stream(stream):
+        for c in range(COPIES):
+            step(c)
+        torch.cuda.synchronize(dev)
+        for c in range(COPIES):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                step(c)
+            graphs.append(g)
+        g_all = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g_all, stream=stream):
+            for c in range(COPIES):
+                step(c)
+
+    def run_steps(k):
+        full, rem = divmod(k, COPIES)
+        for _ in range(full):
+            g_all.replay()
+        for c in range(rem):
+            graphs[c].replay()
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+
+    with torch.cuda.stream(stream):
+        run_steps(args.warmup)
+    torch.cuda.synchronize(dev)
+
+    sampler = ClockSampler(local_rank)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    with sampler:
+        time.sleep(0.05)
+        barrier()
+        torch.cuda.synchronize(dev)
+        t_wall0 = time.perf_counter()
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            run_steps(args.steps)
+            e1.record(stream)
+        torch.cuda.synchronize(dev)
+        t_wall1 = time.perf_counter()
+        barrier()
+        time.sleep(0.05)
+    ms = e0.elapsed_time(e1)
+    t = torch.tensor([ms], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    value = world * args.steps * STEP_BYTES / (ms_max * 1e-3) / 1e9
+
+    result = None
+    if rank == 0:
+        peak, peak_kind = measured_peak()
+        traffic = profiled_traffic()
+        result = {
+            "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "int4 weights x fp32 activations (u8*s8->s32 tensor-core dot, fp32 scale/accumulate)",
+            "data": "synthetic (seeded random int4 weights, fp32 N(0,1) activations)",
+            "config": config_dict(),
+            "roofline": {"bound": "hbm", "achieved": round(value / world, 1), "peak": peak,
+                         "peak_kind": peak_kind, "unit": "GB/s",
+                         "frac": round(value / world / peak, 4),
+                         "frac_of_8000": round(value / world / 8000.0, 4),
+                         "traffic": traffic, "algorithmic_bytes_per_launch": STEP_BYTES / len(LAUNCHES),
+                         "kernel": "gemv_m1_kernel (avg over the step's 4 launches)"},
+            "clocks": sampler.summary(t_wall0, t_wall1),
+            "gpu_launches": len(LAUNCHES) * args.steps,
+        }
+        if not args.no_extras:
+            result["per_projection"] = per_projection(lib, dev, gen, stream, q4_on_device)
+            result["gemv_3584x18944"] = result["per_projection"]["gate"]
+            result["e2e"] = e2e_qlinear(args, dev, cuda_model, synth, np)
+            if world == 1:
+                result["cpu_baseline"] = cpu_baseline(args, budget_s=args.cpu_seconds)
+    if world > 1:
+        barrier()
+    return result
+
+
+def per_projection(lib, dev, gen, stream, q4_on_device, launches_per=200):
+    """Each of the seven projections alone, back to back, rotating weight
+    copies that together exceed L2 (CUDA events around a graph)."""
+    import torch
+    from hetero_infer_b200 import _lib
+    out = {}
+    peak, _ = measured_peak()
+    for name, n, k in PROJECTIONS:
+        nbytes = alg_bytes(n, k)
+        reps = max(2, -(-400_000_000 // nbytes))
+        ws = [q4_on_device(n, k) for _ in range(reps)]
+        x = torch.randn(1, k, device=dev, generator=gen)
+        y = torch.empty(1, n, device=dev)
+
+        def one(i):
+            w, s, b = ws[i % reps]
+            _lib.check(lib.hq4_gemv(w.data_ptr(), s.data_ptr(), b.data_ptr(), x.data_ptr(),
+                                    y.data_ptr(), n, k, GS, 1, stream.cuda_stream), "hq4_gemv")
+
+        with torch.cuda.stream(stream):
+            for i in range(reps):
+                one(i)
+            torch.cuda.synchronize(dev)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                for i in range(reps * 2):
+                    one(i)
+            g.replay()
+            torch.cuda.synchronize(dev)
+            n_rep = max(1, launches_per // (reps * 2))
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(n_rep):
+                g.replay()
+            e1.record(stream)
+        torch.cuda.synchronize(dev)
+        us = e0.elapsed_time(e1) * 1e3 / (n_rep * reps * 2)
+        gbs = nbytes / (us * 1e-6) / 1e9
+        out[name] = {"shape": f"{n}x{k}", "us": round(us, 3), "GB/s": round(gbs, 1),
+                     "frac": round(gbs / peak, 4), "frac_of_8000": round(gbs / 8000.0, 4),
+                     "bytes": nbytes}
+        del ws
+    return out
+
+
+def e2e_qlinear(args, dev, cuda_model, synth, np):
+    """The same metric through the reference-facing API: the reference's
+    QLinear calling convention (hetero/cpu_model.py:145-158) with NumPy
+    activations on the host -- every call copies x host->device, runs the
+    GEMV, and copies the result back."""
+    import torch
+    layers = []
+    for c in range(2):
+        layers.append([cuda_model.QLinear(*synth.q4_linear(c, f"e2e.{name}", n, k, GS), None, GS, 4,
+                                          device=dev) for name, n, k in PROJECTIONS])
+    xs = [synth.activation(7, f"e2e.x.{name}", (1, k)) for name, n, k in PROJECTIONS]
+    h2d = sum(x.nbytes for x in xs)
+    d2h = sum(4 * n for _, n, _ in PROJECTIONS)
+    steps = max(20, min(args.steps, 300))
+    for i in range(5):
+        for q, x in zip(layers[i % 2], xs):
+            q(x)
+    torch.cuda.synchronize(dev)
+    t0 = time.perf_counter()
+    for i in range(steps):
+        for q, x in zip(layers[i % 2], xs):
+            q(x)
+    torch.cuda.synchronize(dev)
+    dt = time.perf_counter() - t0
+    return {"value": round(steps * LAYER_BYTES / dt / 1e9, 2), "unit": "GB/s",
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+            "api": "hetero_infer_b200.cuda_model.QLinear.__call__(numpy) x 7 projections",
+            "steps": steps, "ms_per_step": dt * 1e3 / steps}
+
+
+# ---------------------------------------------------------------- CPU arms
+def _cpu_layer(seed_base: int, copies: int):
+    from hetero_infer_b200 import synth
+    return [[synth.q4_linear(seed_base + c, f"cpu.{name}", n, k, GS) for name, n, k in PROJECTIONS]
+            for c in range(copies)]
+
+
+def cpu_kernel():
+    """The reference's kernel built from source (oracle/_ref), else our port."""
+    from oracle import q4
+    if "avx2" in q4.available_ref_variants():
+        return q4.RefKernel("avx2"), "reference", "kernel/q4gemv.c -O3 -mavx2 -mfma -mf16c (oracle/_ref)"
+    return None, "port", "oracle/q4_oracle.c float path (reference build unavailable)"
+
+
+def time_cpu_layer(steps: int, threads: int, copies: int = 4, budget_s: float = None):
+    """Time `steps` layer steps (7 projections each, as the reference QLinear
+    calls q4_gemv) on `threads` host threads; returns (seconds, steps done)."""
+    import numpy as np
+    os.environ["HETERO_KERNEL_THREADS"] = str(min(threads, 16))
+    kern, kind, what = cpu_kernel()
+    layers = _cpu_layer(99, copies)
+    xs = [np.random.default_rng(5).standard_normal(k).astype(np.float32) for _, n, k in PROJECTIONS]
+    if kern is None:
+        from oracle.q4 import Oracle
+        orc = Oracle()
+        call = lambda wsb, x: orc.gemv_f32(*wsb, x, GS)
+    else:
+        call = lambda wsb, x: kern.gemv(*wsb, x, GS, nthreads=threads)
+    for wsb, x in zip(layers[0], xs):
+        call(wsb, x)
+    done = 0
+    t0 = time.perf_counter()
+    while done < steps:
+        for wsb, x in zip(layers[done % copies], xs):
+            call(wsb, x)
+        done += 1
+        if budget_s is not None and time.perf_counter() - t0 > budget_s:
+            break
+    return time.perf_counter() - t0, done, kind, what
+
+
+def cpu_cores():
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def cpu_baseline(args, budget_s: float = 10.0):
+    cores = cpu_cores()
+    dt, done, kind, what = time_cpu_layer(10 ** 9, cores, budget_s=budget_s)
+    value = done * LAYER_BYTES / dt / 1e9
+    return {"value": round(value, 2), "unit": "GB/s", "cores": cores, "kind": kind,
+            "sample": f"{done} layer steps (7 q4_gemv calls each, 4 rotating weight copies, "
+                      f"{dt:.1f} s) with HETERO_KERNEL_THREADS={min(cores, 16)}; {what}"}
+
+
+def run_reference(args, rank: int, world: int):
+    if rank != 0:
+        return None
+    cores = cpu_cores()
+    # warm-up steps, then at most ~60 s of timed steps
+    time_cpu_layer(args.warmup, cores, budget_s=15.0)
+    dt, done, kind, what = time_cpu_layer(args.steps, cores, budget_s=60.0)
+    value = done * LAYER_BYTES / dt / 1e9
+    return {
+        "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "impl": "reference",
+        "n_gpus": world, "steps": done, "warmup": args.warmup, "ms_per_step": dt * 1e3 / max(done, 1),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "int4 weights x fp32 activations (reference AVX2 path: int16 x, int32 dot)",
+        "data": "synthetic (seeded random int4 weights, fp32 N(0,1) activations)",
+        "config": config_dict(),
+        "cpu_baseline": {"value": round(value, 2), "unit": "GB/s", "cores": cores, "kind": kind,
+                         "sample": f"{done} of {args.steps} requested layer steps in {dt:.1f} s "
+                                   f"(7 q4_gemv calls each, capped at 60 s); {what}"},
+        "e2e": {"value": round(value, 2), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="skip per-projection, e2e and CPU-baseline legs")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus and rank == 0:
+        print(f"warning: --gpus {args.gpus} but WORLD_SIZE={world}", file=sys.stderr)
+
+    if args.impl == "reference":
+        res = run_reference(args, rank, world)
+    else:
+        if world > 1:
+            import datetime
+            import torch
+            import torch.distributed as dist
+            torch.cuda.set_device(local_rank)
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                    device_id=torch.device("cuda", local_rank))
+        res = run_ours(args, rank, world, local_rank)
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+    if res is not None and rank == 0:
+        print(json.dumps(res), flush=True)
+
+
+if __name__ == "__main__":
+    main()

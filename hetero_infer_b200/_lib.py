@@ -22,7 +22,9 @@ HEADER = os.path.join(_build.INCLUDE, "hq4.h")
 # name -> (restype, argtypes); kept in the order of include/hq4.h
 SIGNATURES = {
     "hq4_version": (_I, []),
+    "hq4_device_status": (_I, [_I]),
     "hq4_gemv": (_I, [_P] * 5 + [_I] * 4 + [_P]),
+    "hq4_gemv_fused": (_I, [_P] * 5 + [_I] * 4 + [_P] * 3),
     "hq4_dequant": (_I, [_P] * 4 + [_I] * 4 + [_P]),
 }
 

@@ -111,27 +111,115 @@ __device__ __forceinline__ float h2f(uint32_t bits16) {
     return __half2float(__ushort_as_half((unsigned short)bits16));
 }
 
+// ---- x as a per-group fixed-point integer ------------------------------
 // Exponent E with amax < 2^E (E = floor(log2 amax) + 1 for normal amax), so
-// that x * 2^(22-E) is an integer grid of 22 bits plus sign.  Clamped so both
+// that v = rint(x * 2^(22-E)) satisfies |v| <= 2^22.  Clamped so both
 // 2^(22-E) and 2^(E-22) are normal fp32; groups below 2^-100 round to zero.
+constexpr int kXBits = 22;
 __device__ __forceinline__ int group_exponent(float amax) {
     if (!(amax > 0.0f)) return 0;
     int e = (int)((__float_as_uint(amax) >> 23) & 0xFF) - 126;
     if (e < -100) e = -100;
-    if (e > 128) e = 128;
+    if (e > 127) e = 127;
     return e;
 }
 
-// Balanced base-256 digits of |v| <= 2^22:  v = d2*65536 + d1*256 + d0 with
-// d0, d1 in [-128, 127] and d2 in [-64, 64]; returned as raw bytes.
-__device__ __forceinline__ void digits3(int v, uint32_t& d2, uint32_t& d1, uint32_t& d0) {
-    const int a = ((v + 128) & 255) - 128;
-    const int v1 = (v - a) >> 8;
-    const int b = ((v1 + 128) & 255) - 128;
-    const int c = (v1 - b) >> 8;
-    d0 = (uint32_t)a & 255u;
-    d1 = (uint32_t)b & 255u;
-    d2 = (uint32_t)c & 255u;
+// The three balanced base-256 digits of v = rint(x * up), |v| <= 2^22, as the
+// low three bytes of one word: v = d2*2^16 + d1*2^8 + d0 with d0, d1 in
+// [-128, 127] and d2 in [-64, 64], each byte the digit's two's complement.
+// fma(x, up, 1.5*2^23) rounds x*up to the nearest integer (ties to even) and
+// leaves it in the low mantissa bits: bits = 0x4B400000 + v (at v = 2^22 the
+// mantissa carry lands in the exponent and the identity still holds).  Adding
+// 0x808080 makes every byte the biased digit d+128; xor 0x808080 unbiases.
+__device__ __forceinline__ uint32_t digits3(float x, float up) {
+    const float f = fmaf(x, up, 12582912.0f);
+    return (__float_as_uint(f) + (0x808080u - 0x4B400000u)) ^ 0x808080u;
+}
+
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+    uint32_t d;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+    return d;
+}
+
+// ---- thread-block cluster / mbarrier / bulk copy (sm_90+) ----------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ uint32_t cluster_nctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ uint32_t map_to_rank(uint32_t smem_addr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n"
+                 "barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+                 : "memory");
+}
+// Bounded wait for phase `parity` of an mbarrier; false if the bound ran out.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int max_iters) {
+    for (int i = 0; i < max_iters; i++) {
+        uint32_t done;
+        asm volatile(
+            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+            " selp.u32 %0, 1, 0, p;\n}\n"
+            : "=r"(done) : "r"(bar), "r"(parity) : "memory");
+        if (done) return true;
+    }
+    return false;
+}
+// Make this thread's generic-proxy shared-memory writes visible to the async
+// proxy (bulk copies) issued afterwards.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+// Copy `bytes` from this CTA's shared memory to a peer CTA's shared memory
+// (both 16-byte aligned, bytes % 16 == 0), signalling the peer's mbarrier.
+__device__ __forceinline__ void bulk_copy_to_peer(uint32_t dst_cluster, uint32_t src_cta, uint32_t bytes,
+                                                  uint32_t peer_bar_cluster) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+        ::"r"(dst_cluster), "r"(src_cta), "r"(bytes), "r"(peer_bar_cluster) : "memory");
+}
+// L2 policy for data many CTAs re-read (the activation row).
+__device__ __forceinline__ uint64_t l2_policy_evict_last() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+// L2 policy for data read exactly once (the packed weights).
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+// Bulk copy global -> this CTA's shared memory (16-byte aligned, bytes % 16
+// == 0), completing on the mbarrier `bar` (a shared::cta address).
+__device__ __forceinline__ void bulk_load_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar,
+                                              uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;"
+        ::"r"(dst), "l"(src), "r"(bytes), "r"(bar), "l"(policy) : "memory");
+}
+__device__ __forceinline__ void bulk_commit_and_wait_read() {
+    asm volatile("cp.async.bulk.commit_group;\n cp.async.bulk.wait_group.read 0;" ::: "memory");
 }
 __device__ __forceinline__ float exp2i(int e) {  // 2^e for |e| <= 126
     return __uint_as_float((uint32_t)(e + 127) << 23);

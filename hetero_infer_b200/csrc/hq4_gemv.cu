@@ -55,7 +55,8 @@ struct M1 {
     static constexpr int kKSteps = KG / 8;       // one word per row per k32 step
     static constexpr int kDigitBytes = KG;       // one s8 digit per value
     static constexpr int kBRegs = KG / 4;        // B registers per (group, digit)
-    static constexpr int kImgStride = 3 * KG + 16;  // bytes per group: d2|d1|d0|pad
+    static constexpr int kImgStride = 3 * KG + 16;  // bytes per group: d2|d1|d0|(2^(E-22), xsum)|pad
+    static constexpr int kMetaOff = 3 * KG;
 };
 
 struct GemvM1Params {
@@ -71,16 +72,26 @@ struct GemvM1Params {
     int n_strips, nq;
     const float* row_add;   // optional: out[r] += row_add[r]
     const float* residual;  // optional: out[r] += residual[r]
+    int* status;            // device status word; bit 0 set when a bounded wait ran out
 };
 
-// Shared memory: [ng x kImgStride image][ng x float2 meta][zero block]
+// Shared memory: [ng x kImgStride x image][zero block 64 B]
 //                [kGemvWarps x 2 x 16 floats: split-strip partials]
+//                [mbarrier: x row][raw x row, fp32, when n_in <= 8192]
 __host__ __device__ __forceinline__ size_t zero_block_offset(int ng, int stride) {
-    return (size_t)ng * stride + (((size_t)ng * sizeof(float2) + 15) & ~(size_t)15);
+    return (size_t)ng * stride;
 }
 __host__ __device__ __forceinline__ size_t partial_offset(int ng, int stride) {
     return zero_block_offset(ng, stride) + 64;
 }
+__host__ __device__ __forceinline__ size_t mbar_offset(int ng, int stride) {
+    return partial_offset(ng, stride) + (size_t)kGemvWarps * 2 * 16 * sizeof(float);
+}
+__host__ __device__ __forceinline__ size_t rawx_offset(int ng, int stride) {
+    return mbar_offset(ng, stride) + 16;
+}
+constexpr int kMbarWaitIters = 1 << 22;  // bounded wait on the x-row bulk copy
+constexpr int kRawXMax = 32 * 1024;      // x rows up to 8192 fp32 go through smem
 
 __device__ __forceinline__ void store_row(const GemvM1Params& p, int r, float y) {
     if (r >= p.n_out) return;
@@ -108,23 +119,25 @@ __device__ __forceinline__ void flush_strip(const GemvM1Params& p, int s, bool f
     }
 }
 
-// Per-CTA x image: for every lane-group, three s8 digit blocks (d2, d1, d0)
-// of KG bytes, each in k-step order with the values of a packed word
-// permuted as the u8 unpack produces them ({0,2,4,6} then {1,3,5,7}), plus
-// (2^(E-22), xsum) per group.
+// x image: for every lane-group, three s8 digit blocks (d2, d1, d0) of KG
+// bytes, each in k-step order with the values of a packed word permuted as
+// the u8 unpack produces them ({0,2,4,6} then {1,3,5,7}), followed by
+// (2^(E-22), xsum).  This builds lane-groups [g_lo, g_hi) only, from the fp32
+// values of those groups already in shared memory (xs); the CTAs of a cluster
+// each build one slice and exchange them.
 template <int KG>
-__device__ __forceinline__ void build_x_image(const float* __restrict__ x, int ng,
-                                              unsigned char* img, float2* meta) {
+__device__ __forceinline__ void build_x_slice(const float* xs, int g_lo, int g_hi,
+                                              unsigned char* img) {
     using C = M1<KG>;
     constexpr int kPer = KG / 4;  // values per thread: 4 threads per lane-group
-    const int ntask = ng * 4;
+    const int ntask = (g_hi - g_lo) * 4;
     for (int base = 0; base < ntask; base += kGemvThreads) {
         const int task = base + threadIdx.x;
         const bool ok = task < ntask;
-        const int G = task >> 2, qq = task & 3;
+        const int G = g_lo + (task >> 2), qq = task & 3;
         float v[kPer];
         if (ok) {
-            const float4* xp = reinterpret_cast<const float4*>(x + (size_t)G * KG + qq * kPer);
+            const float4* xp = reinterpret_cast<const float4*>(xs + (size_t)(G - g_lo) * KG + qq * kPer);
 #pragma unroll
             for (int i = 0; i < kPer / 4; i++) {
                 float4 f = xp[i];
@@ -145,28 +158,28 @@ __device__ __forceinline__ void build_x_image(const float* __restrict__ x, int n
         s += __shfl_xor_sync(0xffffffffu, s, 1);
         s += __shfl_xor_sync(0xffffffffu, s, 2);
         const int E = group_exponent(amax);
-        const float up = exp2i(22 - E);
+        const float up = exp2i(kXBits - E);
         if (ok) {
             unsigned char* gbase = img + (size_t)G * C::kImgStride;
 #pragma unroll
             for (int j = 0; j < kPer / 8; j++) {
                 const int word = qq * (kPer / 8) + j;
-                uint32_t d2[2] = {0u, 0u}, d1[2] = {0u, 0u}, d0[2] = {0u, 0u};
+                uint32_t r[8];
 #pragma unroll
-                for (int k = 0; k < 8; k++) {
-                    // byte slot of value k in the unpacked order {0,2,4,6,1,3,5,7}
-                    const int slot = (k & 1) * 4 + (k >> 1);
-                    uint32_t a2, a1, a0;
-                    digits3(__float2int_rn(v[8 * j + k] * up), a2, a1, a0);
-                    d2[slot >> 2] |= a2 << (8 * (slot & 3));
-                    d1[slot >> 2] |= a1 << (8 * (slot & 3));
-                    d0[slot >> 2] |= a0 << (8 * (slot & 3));
-                }
-                *reinterpret_cast<uint2*>(gbase + 0 * KG + word * 8) = make_uint2(d2[0], d2[1]);
-                *reinterpret_cast<uint2*>(gbase + 1 * KG + word * 8) = make_uint2(d1[0], d1[1]);
-                *reinterpret_cast<uint2*>(gbase + 2 * KG + word * 8) = make_uint2(d0[0], d0[1]);
+                for (int k = 0; k < 8; k++) r[k] = digits3(v[8 * j + k], up);
+                // even values {0,2,4,6} then odd {1,3,5,7}; byte k of r = digit k
+                const uint32_t e01 = prmt(prmt(r[0], r[2], 0x5140), prmt(r[4], r[6], 0x5140), 0x5410);
+                const uint32_t e11 = prmt(prmt(r[0], r[2], 0x5140), prmt(r[4], r[6], 0x5140), 0x7632);
+                const uint32_t e21 = prmt(prmt(r[0], r[2], 0x0062), prmt(r[4], r[6], 0x0062), 0x5410);
+                const uint32_t o01 = prmt(prmt(r[1], r[3], 0x5140), prmt(r[5], r[7], 0x5140), 0x5410);
+                const uint32_t o11 = prmt(prmt(r[1], r[3], 0x5140), prmt(r[5], r[7], 0x5140), 0x7632);
+                const uint32_t o21 = prmt(prmt(r[1], r[3], 0x0062), prmt(r[5], r[7], 0x0062), 0x5410);
+                *reinterpret_cast<uint2*>(gbase + 0 * KG + word * 8) = make_uint2(e21, o21);
+                *reinterpret_cast<uint2*>(gbase + 1 * KG + word * 8) = make_uint2(e11, o11);
+                *reinterpret_cast<uint2*>(gbase + 2 * KG + word * 8) = make_uint2(e01, o01);
             }
-            if (qq == 0) meta[G] = make_float2(exp2i(E - 22), s);
+            if (qq == 0)
+                *reinterpret_cast<float2*>(gbase + C::kMetaOff) = make_float2(exp2i(E - kXBits), s);
         }
     }
 }
@@ -175,9 +188,13 @@ template <int KG>
 __global__ void __launch_bounds__(kGemvThreads, 2) gemv_m1_kernel(const GemvM1Params p) {
     using C = M1<KG>;
     constexpr int D = kPrefetch;
-    extern __shared__ __align__(16) unsigned char smem[];
+    extern __shared__ __align__(128) unsigned char smem[];
     unsigned char* img = smem;
-    float2* meta = reinterpret_cast<float2*>(smem + (size_t)p.ng * C::kImgStride);
+    const uint32_t bar_x = smem_u32(smem + mbar_offset(p.ng, C::kImgStride));  // x row arrival
+    // rows short enough get the x row through one bulk copy into shared memory
+    const bool x_via_smem = p.n_in * (int)sizeof(float) <= kRawXMax;
+    float* rawx = reinterpret_cast<float*>(smem + rawx_offset(p.ng, C::kImgStride));
+    if (threadIdx.x == 0) mbar_init(bar_x, 1);
 
     pdl_launch_dependents();
 
@@ -185,12 +202,12 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_m1_kernel(const GemvM1Pa
     const int g = lane >> 2, t = lane & 3;
     const int wj = threadIdx.x >> 5;
     // this CTA's strips, and this warp's contiguous share of their units
-    const int s0 = (int)((long long)blockIdx.x * p.n_strips / gridDim.x);
-    const int s1 = (int)((long long)(blockIdx.x + 1) * p.n_strips / gridDim.x);
+    const int s0 = (int)(blockIdx.x * (uint32_t)p.n_strips / gridDim.x);
+    const int s1 = (int)((blockIdx.x + 1) * (uint32_t)p.n_strips / gridDim.x);
     const int cu0 = s0 * p.nq, nunits = (s1 - s0) * p.nq;
     const int wa = nunits < kGemvWarps ? nunits : kGemvWarps;  // warps with work
-    const int u0 = wj < wa ? cu0 + (int)((long long)wj * nunits / wa) : cu0 + nunits;
-    const int u1 = wj < wa ? cu0 + (int)((long long)(wj + 1) * nunits / wa) : cu0 + nunits;
+    const int u0 = wj < wa ? cu0 + wj * nunits / wa : cu0 + nunits;
+    const int u1 = wj < wa ? cu0 + (wj + 1) * nunits / wa : cu0 + nunits;
     const size_t wpr = (size_t)(p.n_in >> 3);
     float* partials = reinterpret_cast<float*>(smem + partial_offset(p.ng, C::kImgStride));
 
@@ -239,17 +256,32 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_m1_kernel(const GemvM1Pa
         }
     };
 
+    __syncthreads();  // mbarrier initialisation visible to every thread
 #pragma unroll
     for (int d = 0; d < D; d++) issue(wv[d], sv[d], u0 + d < u1);
 
-    // x image in shared memory (needs the producer of x)
+    // x (needs the producer of x).  Short rows: one bulk copy into shared
+    // memory (the copy engine, not the load pipeline already holding the
+    // weight prefetch); long rows are read from global memory directly.
     pdl_wait();
-    build_x_image<KG>(p.x, p.ng, img, meta);
+    bool ok = true;
+    if (x_via_smem) {
+        const uint32_t x_bytes = (uint32_t)(p.n_in * sizeof(float));
+        if (threadIdx.x == 0) {
+            mbar_arrive_expect_tx(bar_x, x_bytes);
+            bulk_load_g2s(smem_u32(rawx), p.x, x_bytes, bar_x, l2_policy_evict_last());
+        }
+        ok = mbar_wait(bar_x, 0, kMbarWaitIters);
+    }
+    if (ok) build_x_slice<KG>(x_via_smem ? rawx : p.x, 0, p.ng, img);
     {
         uint4* z = reinterpret_cast<uint4*>(smem + zero_block_offset(p.ng, C::kImgStride));
-        if (threadIdx.x < KG / 16) z[threadIdx.x] = make_uint4(0, 0, 0, 0);
+        if (threadIdx.x < 4) z[threadIdx.x] = make_uint4(0, 0, 0, 0);
     }
-    __syncthreads();
+    if (!__syncthreads_and(ok)) {  // uniform: every thread leaves together
+        if (threadIdx.x == 0 && p.status) atomicOr(p.status, 1);
+        return;
+    }
 
     // B operand: lanes g == 2t read digits d2 (n-tile 0) and d0 (n-tile 1) of
     // their lane-group, lanes g == 2t+1 read d1 (n-tile 0); every other slot
@@ -288,7 +320,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_m1_kernel(const GemvM1Pa
                 mma_u8s8_16832(c1, a0, a1, a2, a3, b10, b11);
             }
             if (gok) {
-                const float2 m = meta[G];
+                const float2 m = *reinterpret_cast<const float2*>(gb + C::kMetaOff);
                 const float dot0 = fmaf((float)c0[0], 65536.0f, fmaf((float)c0[1], 256.0f, (float)c1[0]));
                 const float dot1 = fmaf((float)c0[2], 65536.0f, fmaf((float)c0[3], 256.0f, (float)c1[2]));
                 acc0 = fmaf(h2f(sv[d][0]) * m.x, dot0, acc0);
@@ -363,9 +395,12 @@ __global__ void dequant_kernel(const uint32_t* __restrict__ w, const uint16_t* _
 
 // ---- host side -------------------------------------------------------------
 struct GemvPlan {
-    int kg, sg_shift, ng, n_sg, n_strips, nq, grid;
+    int kg, sg_shift, ng, n_sg, n_strips, nq, grid, cluster;  // cluster: always 1 here
     size_t smem;
 };
+
+// Device status word: bit 0 = a bounded wait in a kernel ran out.
+__device__ int g_hq4_status = 0;
 
 static int sm_count() {
     static int cached = -1;
@@ -376,6 +411,18 @@ static int sm_count() {
         n = 148;
     cached = n;
     return cached;
+}
+
+// Device address of g_hq4_status, looked up once per device.
+static int* status_word() {
+    static int* addr[64] = {nullptr};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+    if (!addr[dev]) {
+        int* a = nullptr;
+        if (cudaGetSymbolAddress(reinterpret_cast<void**>(&a), g_hq4_status) == cudaSuccess) addr[dev] = a;
+    }
+    return addr[dev];
 }
 
 static int log2_exact(int v) {
@@ -402,12 +449,14 @@ static int plan_gemv(int n_out, int n_in, int gs, GemvPlan& pl) {
     pl.nq = (pl.ng + 3) / 4;
     if ((long long)pl.n_strips * pl.nq > (1LL << 30)) return HQ4_ERR_SHAPE;
     const int stride = pl.kg == 64 ? M1<64>::kImgStride : M1<32>::kImgStride;
-    pl.smem = partial_offset(pl.ng, stride) + (size_t)kGemvWarps * 2 * 16 * sizeof(float);
-    if (pl.smem > 220 * 1024) return HQ4_ERR_SHAPE;  // x image must fit one CTA
-    const int ctas_per_sm = pl.smem <= 100 * 1024 ? 2 : 1;
-    const int max_grid = sm_count() * ctas_per_sm;
     // whole strips per CTA; enough of them that each warp gets a unit
     const int min_strips = (kGemvWarps + pl.nq - 1) / pl.nq;
+    pl.cluster = 1;
+    const size_t rawx = (size_t)n_in * sizeof(float) <= (size_t)kRawXMax ? (size_t)n_in * sizeof(float) : 0;
+    pl.smem = rawx_offset(pl.ng, stride) + rawx;
+    if (pl.smem > 220 * 1024) return HQ4_ERR_SHAPE;  // x image must fit one CTA
+    const int ctas_per_sm = pl.smem <= 110 * 1024 ? 2 : 1;
+    const int max_grid = sm_count() * ctas_per_sm;
     pl.grid = std::max(1, std::min(max_grid, pl.n_strips / min_strips));
     return HQ4_OK;
 }
@@ -467,6 +516,7 @@ int gemv_m1(const uint32_t* w, const uint16_t* scales, const uint16_t* biases, c
     prm.nq = pl.nq;
     prm.row_add = row_add;
     prm.residual = residual;
+    prm.status = status_word();
     return pl.kg == 64 ? launch_m1<64>(pl, prm, st) : launch_m1<32>(pl, prm, st);
 }
 
@@ -474,7 +524,17 @@ int gemv_m1(const uint32_t* w, const uint16_t* scales, const uint16_t* biases, c
 
 using namespace hq4;
 
-extern "C" int hq4_version(void) { return (0 << 16) | 1; }
+extern "C" int hq4_version(void) { return (0 << 16) | 2; }
+
+extern "C" int hq4_device_status(int clear) {
+    int v = 0;
+    if (cudaMemcpyFromSymbol(&v, g_hq4_status, sizeof(int)) != cudaSuccess) return HQ4_ERR_LAUNCH;
+    if (clear) {
+        const int z = 0;
+        cudaMemcpyToSymbol(g_hq4_status, &z, sizeof(int));
+    }
+    return v;
+}
 
 
 extern "C" int hq4_gemv(const uint32_t* w, const uint16_t* scales, const uint16_t* biases,
@@ -486,6 +546,20 @@ extern "C" int hq4_gemv(const uint32_t* w, const uint16_t* scales, const uint16_
     for (int i = 0; i < m; i++) {
         int rc = gemv_m1(w, scales, biases, x + (size_t)i * n_in, out + (size_t)i * n_out, n_out,
                          n_in, gs, nullptr, nullptr, st);
+        if (rc) return rc;
+    }
+    return HQ4_OK;
+}
+
+extern "C" int hq4_gemv_fused(const uint32_t* w, const uint16_t* scales, const uint16_t* biases,
+                              const float* x, float* out, int n_out, int n_in, int gs, int m,
+                              const float* row_add, const float* residual, void* stream) {
+    if (int rc = check_device()) return rc;
+    if (m <= 0) return HQ4_ERR_SHAPE;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    for (int i = 0; i < m; i++) {
+        int rc = gemv_m1(w, scales, biases, x + (size_t)i * n_in, out + (size_t)i * n_out, n_out,
+                         n_in, gs, row_add, residual ? residual + (size_t)i * n_out : nullptr, st);
         if (rc) return rc;
     }
     return HQ4_OK;

@@ -52,6 +52,39 @@ def q4_gemv(w: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor, x: torc
     return out.reshape(*x.shape[:-1], n_out)
 
 
+def q4_gemv_fused(w: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor, x: torch.Tensor,
+                  group_size: int = 64, row_add: Optional[torch.Tensor] = None,
+                  residual: Optional[torch.Tensor] = None,
+                  out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """GEMV with the bias / residual add fused into its store (hq4_gemv_fused).
+
+    ``out`` may alias ``residual`` (in-place residual update) but not ``x``."""
+    lib = _lib.load()
+    _need_cuda(w, "w")
+    _need_cuda(scales, "scales", torch.float16)
+    _need_cuda(biases, "biases", torch.float16)
+    n_out, n_in = w.shape[0], w.shape[1] * 8
+    xf = x.reshape(-1, n_in)
+    _need_cuda(xf, "x", torch.float32)
+    m = xf.shape[0]
+    if out is None:
+        out = torch.empty((m, n_out), dtype=torch.float32, device=x.device)
+    _need_cuda(out, "out", torch.float32)
+    ra = 0
+    if row_add is not None:
+        _need_cuda(row_add, "row_add", torch.float32)
+        ra = row_add.data_ptr()
+    rs = 0
+    if residual is not None:
+        _need_cuda(residual, "residual", torch.float32)
+        rs = residual.data_ptr()
+    rc = lib.hq4_gemv_fused(w.data_ptr(), scales.data_ptr(), biases.data_ptr(), xf.data_ptr(),
+                            out.data_ptr(), n_out, n_in, group_size, m, ra or None, rs or None,
+                            _stream_ptr(x.device))
+    _lib.check(rc, "hq4_gemv_fused")
+    return out.reshape(*x.shape[:-1], n_out)
+
+
 def q4_dequant(w: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor, row0: int, row1: int,
                group_size: int = 64, out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """fp32 expansion of rows [row0, row1) (hq4_dequant)."""

@@ -34,6 +34,12 @@ extern "C" {
 /* Library version, (major << 16) | minor. */
 int hq4_version(void);
 
+/* Device status word of the current device (synchronising): bit 0 is set
+ * when a kernel's bounded wait on its cluster x-image exchange ran out (the
+ * kernel then wrote no output).  Non-zero `clear` resets it.  Has no
+ * counterpart in the reference, whose CPU kernel cannot stall this way. */
+int hq4_device_status(int clear);
+
 /* out[m][n_out] = x[m][n_in] . W^T with W dequantised on the fly.
  * Replaces  int q4_gemv(w, scales, biases, x, out, n_out, n_in, gs, nthreads)
  * (kernel/q4gemv.c:232-233): same pointer order and shape arguments; the
@@ -46,6 +52,15 @@ int hq4_version(void);
  * 177-181): results match it to fp32 summation-order rounding. */
 int hq4_gemv(const uint32_t* w, const uint16_t* scales, const uint16_t* biases,
              const float* x, float* out, int n_out, int n_in, int gs, int m, void* stream);
+
+/* hq4_gemv with the projection's epilogue fused into the store:
+ *   out[i][r] = (x[i] . W[r]) + row_add[r] + residual[i][r]
+ * row_add (length n_out, e.g. the q/k/v bias of hetero/cpu_model.py:156-157)
+ * and residual ([m][n_out], the decoder's residual stream,
+ * hetero/cpu_model.py:305-306) may each be NULL.  out may alias residual. */
+int hq4_gemv_fused(const uint32_t* w, const uint16_t* scales, const uint16_t* biases,
+                   const float* x, float* out, int n_out, int n_in, int gs, int m,
+                   const float* row_add, const float* residual, void* stream);
 
 /* Rows [row0,row1) of W expanded to fp32 into out [row1-row0][n_in].
  * Replaces  int q4_dequant(w, scales, biases, out, row0, row1, n_in, gs,
