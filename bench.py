@@ -259,6 +259,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
             result["per_projection"] = per_projection(lib, dev, gen, stream, q4_on_device)
             result["gemv_3584x18944"] = result["per_projection"]["gate"]
             result["e2e"] = e2e_qlinear(args, dev, cuda_model, synth, np)
+            result["decode"] = decode_bench(dev)
             if world == 1:
                 result["cpu_baseline"] = cpu_baseline(args, budget_s=args.cpu_seconds)
     if world > 1:
@@ -310,6 +311,54 @@ def per_projection(lib, dev, gen, stream, q4_on_device, launches_per=200):
                      "bytes": nbytes}
         del ws
     return out
+
+
+def decode_bench(dev, n_tokens: int = 128, prompt_len: int = 32):
+    """Benchmark config 4: greedy decode of the random-init Qwen2-7B-shape model
+    on one device -- 32-token prompt, then one CUDA-graph replay per generated
+    token (embedding, 28 layers, head, argmax, position advance).  Decode tok/s
+    over the graph-replayed steps (CUDA events); TTFT is the prefill plus first
+    token."""
+    import numpy as np
+    import torch
+    from hetero_infer_b200 import cuda_model, synth
+
+    class Spec:
+        start, end, embed, head = 0, 28, True, True
+
+    cfg = dict(synth.QWEN2_7B)
+    t0 = time.perf_counter()
+    w = synth.model_weights(cfg, 0)
+    stage = cuda_model.Stage(cfg, Spec, w, device=dev, max_ctx=512)
+    del w
+    t_load = time.perf_counter() - t0
+    prompt = synth.prompt_ids(0, prompt_len, cfg["vocab_size"])
+    dec = cuda_model.GreedyDecoder(stage)
+    torch.cuda.synchronize(dev)
+    e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+    e0.record(dec.stream)
+    dec.prefill(prompt)
+    e1.record(dec.stream)
+    dec.capture()
+    torch.cuda.synchronize(dev)
+    n_steps = n_tokens - 2
+    e1b = torch.cuda.Event(enable_timing=True)
+    e1b.record(dec.stream)
+    dec.steps(n_steps)
+    e2.record(dec.stream)
+    torch.cuda.synchronize(dev)
+    toks = dec.tokens()
+    ms = e1b.elapsed_time(e2)
+    per_token_bytes = 28 * sum(alg_bytes(n, k) for _, n, k in PROJECTIONS) + alg_bytes(cfg["vocab_size"], HIDDEN)
+    tok_s = n_steps / (ms * 1e-3)
+    return {"tok_s": round(tok_s, 1), "ms_per_token": round(ms / n_steps, 4),
+            "ttft_ms": round(e0.elapsed_time(e1), 2), "generated": len(toks),
+            "prompt_tokens": prompt_len, "timed_steps": n_steps,
+            "weight_GB_per_s": round(per_token_bytes * tok_s / 1e9, 1),
+            "hbm_ceiling_tok_s": round(measured_peak()[0] * 1e9 / per_token_bytes, 1),
+            "launches_per_token": 28 * 5 + 4, "first_tokens": toks[:8],
+            "model": "qwen2-7b-shape random int4 (28 layers, h3584, 28q/4kv, i18944, v152064)",
+            "setup_s": round(t_load, 1)}
 
 
 def e2e_qlinear(args, dev, cuda_model, synth, np):

@@ -16,6 +16,7 @@ from . import build as _build
 _P = ctypes.c_void_p
 _I = ctypes.c_int
 _Z = ctypes.c_size_t
+_F = ctypes.c_float
 
 HEADER = os.path.join(_build.INCLUDE, "hq4.h")
 
@@ -26,6 +27,13 @@ SIGNATURES = {
     "hq4_gemv": (_I, [_P] * 5 + [_I] * 4 + [_P]),
     "hq4_gemv_fused": (_I, [_P] * 5 + [_I] * 4 + [_P] * 3),
     "hq4_dequant": (_I, [_P] * 4 + [_I] * 4 + [_P]),
+    "hq4_embed_f16": (_I, [_P, _P, _I, _I, _P, _P]),
+    "hq4_gemv_norm": (_I, [_P] * 5 + [_I] * 4 + [_P, _F, _I, _P, _P, _P]),
+    "hq4_qkv_rope": (_I, [_P] * 4 + [_I] * 6 + [_P, _F, _P, _P, _P, _P, _I, _P, _P, _P, _P]),
+    "hq4_attention": (_I, [_P] * 4 + [_I] * 4 + [_P, _I, _F, _P]),
+    "hq4_argmax": (_I, [_P, _I, _P, _P, _I, _P, _P]),
+    "hq4_synth_embed_f16": (_I, [ctypes.c_longlong, _I, _I, _F, _P, _P]),
+    "hq4_advance_position": (_I, [_P, _I, _P]),
 }
 
 ERRORS = {

@@ -73,7 +73,24 @@ struct GemvM1Params {
     const float* row_add;   // optional: out[r] += row_add[r]
     const float* residual;  // optional: out[r] += residual[r]
     int* status;            // device status word; bit 0 set when a bounded wait ran out
+    // optional RMSNorm of x before the product: x <- x * rsqrt(mean(x^2)+eps) * norm_w
+    const float* norm_w;
+    float eps;
+    // epilogue mode
+    int mode;               // kEpiPlain, kEpiSiluMul or kEpiQkvRope
+    // kEpiQkvRope: q|k|v rows of one decoder layer, q and k rows permuted so
+    // strip rows g and g+8 are the rotation pair (d, d + head_dim/2)
+    int q_strips, k_strips, head_dim, max_ctx;
+    int tok;                // token index inside this call (position = *pos + tok)
+    const int* pos;         // device position of token 0
+    const float* rope_cos;  // [max_ctx][head_dim/2]
+    const float* rope_sin;
+    float* q_out;           // [n_heads][head_dim], rotated
+    float* k_cache;         // [n_kv][max_ctx][head_dim]
+    float* v_cache;
 };
+
+enum : int { kEpiPlain = 0, kEpiSiluMul = 1, kEpiQkvRope = 2 };
 
 // Shared memory: [ng x kImgStride x image][zero block 64 B]
 //                [kGemvWarps x 2 x 16 floats: split-strip partials]
@@ -100,6 +117,55 @@ __device__ __forceinline__ void store_row(const GemvM1Params& p, int r, float y)
     p.out[r] = y;
 }
 
+// silu as the reference's NumPy stage writes it: x / (1 + exp(-x))
+// (hetero/cpu_model.py:169-170), every operation rounded separately.
+__device__ __forceinline__ float silu_ref(float x) {
+    return __fdiv_rn(x, __fadd_rn(1.0f, expf(-x)));
+}
+
+// Store the finished pair of rows (g, g+8) of strip s according to the mode.
+__device__ __forceinline__ void store_pair(const GemvM1Params& p, int s, int g, float y0, float y1) {
+    if (p.mode == kEpiPlain) {
+        store_row(p, s * 16 + g, y0);
+        store_row(p, s * 16 + g + 8, y1);
+        return;
+    }
+    if (p.mode == kEpiSiluMul) {
+        // strip s holds gate rows 8s..8s+7 (g) and the matching up rows (g+8)
+        const int r = s * 8 + g;
+        if (r < p.n_out / 2) p.out[r] = __fmul_rn(silu_ref(y0), y1);
+        return;
+    }
+    // kEpiQkvRope
+    if (p.row_add) {
+        y0 = __fadd_rn(y0, p.row_add[s * 16 + g]);
+        y1 = __fadd_rn(y1, p.row_add[s * 16 + g + 8]);
+    }
+    const int half = p.head_dim >> 1;
+    const int spp = half >> 3;  // strips per head (8 rotation pairs per strip)
+    const int pos = *p.pos + p.tok;
+    if (pos < 0 || pos >= p.max_ctx) return;  // outside the cache: write nothing
+    if (s < p.q_strips + p.k_strips) {
+        const bool is_q = s < p.q_strips;
+        const int sl = is_q ? s : s - p.q_strips;
+        const int head = sl / spp, j = (sl % spp) * 8 + g;
+        const float c = p.rope_cos[(size_t)pos * half + j], sn = p.rope_sin[(size_t)pos * half + j];
+        // hetero/cpu_model.py:200-203: (x1*cos - x2*sin, x1*sin + x2*cos)
+        const float o1 = __fsub_rn(__fmul_rn(y0, c), __fmul_rn(y1, sn));
+        const float o2 = __fadd_rn(__fmul_rn(y0, sn), __fmul_rn(y1, c));
+        float* dst = is_q ? p.q_out + (size_t)head * p.head_dim
+                          : p.k_cache + ((size_t)head * p.max_ctx + pos) * p.head_dim;
+        dst[j] = o1;
+        dst[j + half] = o2;
+    } else {
+        const int r0 = (s - p.q_strips - p.k_strips) * 16 + g;  // natural v row order
+        const int r1 = r0 + 8;
+        const int head0 = r0 / p.head_dim, head1 = r1 / p.head_dim;
+        p.v_cache[((size_t)head0 * p.max_ctx + pos) * p.head_dim + (r0 % p.head_dim)] = y0;
+        p.v_cache[((size_t)head1 * p.max_ctx + pos) * p.head_dim + (r1 % p.head_dim)] = y1;
+    }
+}
+
 // Sum a strip's lane partials across the 4 lanes t; store it when this warp
 // owns the whole strip, else park it in the warp's head/tail smem slot.
 __device__ __forceinline__ void flush_strip(const GemvM1Params& p, int s, bool full, float* slot,
@@ -111,8 +177,7 @@ __device__ __forceinline__ void flush_strip(const GemvM1Params& p, int s, bool f
     const int g = lane >> 2, t = lane & 3;
     if (t != 0) return;
     if (full) {
-        store_row(p, s * 16 + g, acc0);
-        store_row(p, s * 16 + g + 8, acc1);
+        store_pair(p, s, g, acc0, acc1);
     } else {
         slot[g] = acc0;
         slot[g + 8] = acc1;
@@ -127,7 +192,8 @@ __device__ __forceinline__ void flush_strip(const GemvM1Params& p, int s, bool f
 // each build one slice and exchange them.
 template <int KG>
 __device__ __forceinline__ void build_x_slice(const float* xs, int g_lo, int g_hi,
-                                              unsigned char* img) {
+                                              unsigned char* img, float norm_r,
+                                              const float* __restrict__ norm_w) {
     using C = M1<KG>;
     constexpr int kPer = KG / 4;  // values per thread: 4 threads per lane-group
     const int ntask = (g_hi - g_lo) * 4;
@@ -146,6 +212,18 @@ __device__ __forceinline__ void build_x_slice(const float* xs, int g_lo, int g_h
         } else {
 #pragma unroll
             for (int i = 0; i < kPer; i++) v[i] = 0.0f;
+        }
+        if (norm_w && ok) {
+            // hetero/cpu_model.py:164-166: (x * (1/sqrt(mean(x^2)+eps))) * w
+            const float4* wp = reinterpret_cast<const float4*>(norm_w + (size_t)G * KG + qq * kPer);
+#pragma unroll
+            for (int i = 0; i < kPer / 4; i++) {
+                const float4 nw = wp[i];
+                v[4 * i] = __fmul_rn(__fmul_rn(v[4 * i], norm_r), nw.x);
+                v[4 * i + 1] = __fmul_rn(__fmul_rn(v[4 * i + 1], norm_r), nw.y);
+                v[4 * i + 2] = __fmul_rn(__fmul_rn(v[4 * i + 2], norm_r), nw.z);
+                v[4 * i + 3] = __fmul_rn(__fmul_rn(v[4 * i + 3], norm_r), nw.w);
+            }
         }
         float amax = 0.0f, s = 0.0f;
 #pragma unroll
@@ -273,7 +351,25 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_m1_kernel(const GemvM1Pa
         }
         ok = mbar_wait(bar_x, 0, kMbarWaitIters);
     }
-    if (ok) build_x_slice<KG>(x_via_smem ? rawx : p.x, 0, p.ng, img);
+    const float* xsrc = x_via_smem ? rawx : p.x;
+    float norm_r = 1.0f;
+    if (p.norm_w) {
+        // sum of squares of the whole row: CTA reduction
+        __shared__ float red[kGemvWarps];
+        float ss = 0.0f;
+        if (ok)
+            for (int i = threadIdx.x; i < p.n_in; i += kGemvThreads) ss = fmaf(xsrc[i], xsrc[i], ss);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+        __syncthreads();
+        float tot = 0.0f;
+#pragma unroll
+        for (int i = 0; i < kGemvWarps; i++) tot += red[i];
+        const float mean = __fdiv_rn(tot, (float)p.n_in);
+        norm_r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, p.eps)));
+    }
+    if (ok) build_x_slice<KG>(xsrc, 0, p.ng, img, norm_r, p.norm_w);
     {
         uint4* z = reinterpret_cast<uint4*>(smem + zero_block_offset(p.ng, C::kImgStride));
         if (threadIdx.x < 4) z[threadIdx.x] = make_uint4(0, 0, 0, 0);
@@ -361,8 +457,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_m1_kernel(const GemvM1Pa
                 y0 += sl[g];
                 y1 += sl[g + 8];
             }
-            store_row(p, sf * 16 + g, y0);
-            store_row(p, sf * 16 + g + 8, y1);
+            store_pair(p, sf, g, y0, y1);
         }
     }
 }
@@ -494,14 +589,27 @@ static int launch_m1(const GemvPlan& pl, const GemvM1Params& prm, cudaStream_t s
     return e == cudaSuccess ? HQ4_OK : HQ4_ERR_LAUNCH;
 }
 
-int gemv_m1(const uint32_t* w, const uint16_t* scales, const uint16_t* biases, const float* x,
-            float* out, int n_out, int n_in, int gs, const float* row_add, const float* residual,
-            cudaStream_t st) {
+// Fill the shape/plan part of the parameters and launch.  `prm` carries the
+// pointers and the epilogue/prologue options.
+int gemv_launch(GemvM1Params prm, int gs, cudaStream_t st) {
     GemvPlan pl;
-    int rc = plan_gemv(n_out, n_in, gs, pl);
+    int rc = plan_gemv(prm.n_out, prm.n_in, gs, pl);
     if (rc) return rc;
-    if (((uintptr_t)w & 31) || ((uintptr_t)x & 15) || ((uintptr_t)out & 3)) return HQ4_ERR_ALIGN;
-    GemvM1Params prm;
+    if (((uintptr_t)prm.w & 31) || ((uintptr_t)prm.x & 15) || ((uintptr_t)prm.out & 3))
+        return HQ4_ERR_ALIGN;
+    if (prm.norm_w && ((uintptr_t)prm.norm_w & 15)) return HQ4_ERR_ALIGN;
+    prm.ng = pl.ng;
+    prm.sg_shift = pl.sg_shift;
+    prm.n_sg = pl.n_sg;
+    prm.n_strips = pl.n_strips;
+    prm.nq = pl.nq;
+    prm.status = status_word();
+    return pl.kg == 64 ? launch_m1<64>(pl, prm, st) : launch_m1<32>(pl, prm, st);
+}
+
+GemvM1Params gemv_params(const uint32_t* w, const uint16_t* scales, const uint16_t* biases,
+                         const float* x, float* out, int n_out, int n_in) {
+    GemvM1Params prm = {};
     prm.w = w;
     prm.sc = scales;
     prm.bi = biases;
@@ -509,16 +617,46 @@ int gemv_m1(const uint32_t* w, const uint16_t* scales, const uint16_t* biases, c
     prm.out = out;
     prm.n_out = n_out;
     prm.n_in = n_in;
-    prm.ng = pl.ng;
-    prm.sg_shift = pl.sg_shift;
-    prm.n_sg = pl.n_sg;
-    prm.n_strips = pl.n_strips;
-    prm.nq = pl.nq;
+    prm.mode = kEpiPlain;
+    return prm;
+}
+
+int gemv_m1(const uint32_t* w, const uint16_t* scales, const uint16_t* biases, const float* x,
+            float* out, int n_out, int n_in, int gs, const float* row_add, const float* residual,
+            cudaStream_t st) {
+    GemvM1Params prm = gemv_params(w, scales, biases, x, out, n_out, n_in);
     prm.row_add = row_add;
     prm.residual = residual;
-    prm.status = status_word();
-    return pl.kg == 64 ? launch_m1<64>(pl, prm, st) : launch_m1<32>(pl, prm, st);
+    return gemv_launch(prm, gs, st);
 }
+
+int gemv_launch_stage(const uint32_t* w, const uint16_t* scales, const uint16_t* biases,
+                      const float* x, float* out, int n_out, int n_in, int gs, const float* row_add,
+                      const float* residual, const float* norm_w, float eps, int mode, int q_strips,
+                      int k_strips, int head_dim, int max_ctx, int tok, const int* pos,
+                      const float* rope_cos, const float* rope_sin, float* q_out, float* k_cache,
+                      float* v_cache, cudaStream_t st) {
+    GemvM1Params prm = gemv_params(w, scales, biases, x, out, n_out, n_in);
+    prm.row_add = row_add;
+    prm.residual = residual;
+    prm.norm_w = norm_w;
+    prm.eps = eps;
+    prm.mode = mode;
+    prm.q_strips = q_strips;
+    prm.k_strips = k_strips;
+    prm.head_dim = head_dim;
+    prm.max_ctx = max_ctx;
+    prm.tok = tok;
+    prm.pos = pos;
+    prm.rope_cos = rope_cos;
+    prm.rope_sin = rope_sin;
+    prm.q_out = q_out;
+    prm.k_cache = k_cache;
+    prm.v_cache = v_cache;
+    return gemv_launch(prm, gs, st);
+}
+
+int check_device_cap() { return check_device(); }
 
 }  // namespace hq4
 

@@ -1,0 +1,273 @@
+// The non-GEMV kernels of the qwen2 stage forward (hetero/cpu_model.py:164-368)
+// and the C entry points that expose the stage's fused GEMV modes.
+//
+//  * embedding:  fp16 table row gather -> fp32 hidden state
+//  * attention:  grouped-query SDPA over the KV cache, one CTA per
+//                (query head, query token); causal when several tokens
+//                (hetero/cpu_model.py:233-252)
+//  * argmax:     greedy sampling, first index wins ties (numpy argmax,
+//                hetero/backends.py:106-109)
+//  * position:   the device-side token position the decode step reads, so a
+//                whole step can be replayed as one CUDA graph
+#include <algorithm>
+#include <cfloat>
+
+#include "hq4_common.cuh"
+#include "hq4.h"
+
+namespace hq4 {
+
+// from hq4_gemv.cu
+struct GemvM1Params;
+int gemv_launch_stage(const uint32_t* w, const uint16_t* scales, const uint16_t* biases,
+                      const float* x, float* out, int n_out, int n_in, int gs, const float* row_add,
+                      const float* residual, const float* norm_w, float eps, int mode, int q_strips,
+                      int k_strips, int head_dim, int max_ctx, int tok, const int* pos,
+                      const float* rope_cos, const float* rope_sin, float* q_out, float* k_cache,
+                      float* v_cache, cudaStream_t st);
+int check_device_cap();
+
+static cudaLaunchAttribute pdl_attr() {
+    cudaLaunchAttribute a;
+    a.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    a.val.programmaticStreamSerializationAllowed = 1;
+    return a;
+}
+
+template <typename Kern, typename... Args>
+static int launch_pdl(Kern kern, dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args... args) {
+    cudaLaunchAttribute attr[1] = {pdl_attr()};
+    cudaLaunchConfig_t lc = {};
+    lc.gridDim = grid;
+    lc.blockDim = block;
+    lc.dynamicSmemBytes = smem;
+    lc.stream = st;
+    lc.attrs = attr;
+    lc.numAttrs = 1;
+    return cudaLaunchKernelEx(&lc, kern, args...) == cudaSuccess ? HQ4_OK : HQ4_ERR_LAUNCH;
+}
+
+// ---- embedding ---------------------------------------------------------------
+__global__ void embed_kernel(const __half* __restrict__ table, const int* __restrict__ ids, int n,
+                             int hidden, float* __restrict__ out) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const int t = blockIdx.y;
+    if (t >= n) return;
+    const int id = ids[t];
+    const __half* row = table + (size_t)id * hidden;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < hidden; i += gridDim.x * blockDim.x)
+        out[(size_t)t * hidden + i] = __half2float(row[i]);
+}
+
+// ---- attention ---------------------------------------------------------------
+// CTA (head h, query token i): position p = *pos + i attends to keys [0, p].
+// scores: one key per warp iteration, lanes split head_dim; softmax in fp32
+// as the reference writes it (s - max, exp, / sum); out[d] = sum_s p_s v_s[d].
+constexpr int kAttnThreads = 128;
+
+__global__ void __launch_bounds__(kAttnThreads) attention_kernel(
+    const float* __restrict__ q, const float* __restrict__ k_cache, const float* __restrict__ v_cache,
+    float* __restrict__ out, int n_heads, int n_kv, int head_dim, int max_ctx, const int* __restrict__ pos,
+    float scale) {
+    extern __shared__ float sc[];  // [max positions]
+    __shared__ float red[kAttnThreads / 32];
+    pdl_launch_dependents();
+    pdl_wait();
+    const int h = blockIdx.x, i = blockIdx.y;
+    const int kh = h / (n_heads / n_kv);
+    const int p = *pos + i;
+    if (p < 0 || p >= max_ctx) return;  // outside the cache: write nothing
+    const int n = p + 1;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = kAttnThreads / 32;
+    const float* qh = q + ((size_t)i * n_heads + h) * head_dim;
+    const float* kbase = k_cache + (size_t)kh * max_ctx * head_dim;
+    const float* vbase = v_cache + (size_t)kh * max_ctx * head_dim;
+    // query slice in registers: lane owns elements lane, lane+32, ...
+    float qr[8];
+    const int per = head_dim / 32;  // head_dim <= 256
+#pragma unroll
+    for (int j = 0; j < 8; j++) qr[j] = j < per ? qh[lane + 32 * j] : 0.0f;
+    float mx = -FLT_MAX;
+    for (int s = warp; s < n; s += nw) {
+        const float* kr = kbase + (size_t)s * head_dim;
+        float d = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 8; j++)
+            if (j < per) d = fmaf(qr[j], kr[lane + 32 * j], d);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+        d = __fmul_rn(d, scale);
+        if (lane == 0) sc[s] = d;
+        mx = fmaxf(mx, d);
+    }
+    if (lane == 0) red[warp] = mx;
+    __syncthreads();
+    mx = red[0];
+    for (int j = 1; j < nw; j++) mx = fmaxf(mx, red[j]);
+    __syncthreads();
+    float sum = 0.0f;
+    for (int s = threadIdx.x; s < n; s += kAttnThreads) {
+        const float e = expf(__fsub_rn(sc[s], mx));
+        sc[s] = e;
+        sum += e;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    if (lane == 0) red[warp] = sum;
+    __syncthreads();
+    float tot = 0.0f;
+    for (int j = 0; j < nw; j++) tot += red[j];
+    for (int s = threadIdx.x; s < n; s += kAttnThreads) sc[s] = __fdiv_rn(sc[s], tot);
+    __syncthreads();
+    for (int d = threadIdx.x; d < head_dim; d += kAttnThreads) {
+        float acc = 0.0f;
+        for (int s = 0; s < n; s++) acc = fmaf(sc[s], vbase[(size_t)s * head_dim + d], acc);
+        out[((size_t)i * n_heads + h) * head_dim + d] = acc;
+    }
+}
+
+// ---- argmax --------------------------------------------------------------------
+// Largest value, lowest index among equals.  Writes the index to idx_out and,
+// when given, to history[*pos] (the generated-token record).
+constexpr int kArgmaxThreads = 1024;
+
+__global__ void __launch_bounds__(kArgmaxThreads) argmax_kernel(const float* __restrict__ x, int n,
+                                                                int* __restrict__ idx_out,
+                                                                int* __restrict__ history, int hist_len,
+                                                                const int* __restrict__ pos) {
+    __shared__ float bv[kArgmaxThreads / 32];
+    __shared__ int bi[kArgmaxThreads / 32];
+    pdl_launch_dependents();
+    pdl_wait();
+    float best = -FLT_MAX;
+    int bidx = 0x7fffffff;
+    for (int i = threadIdx.x; i < n; i += kArgmaxThreads) {
+        const float v = x[i];
+        if (v > best) {  // strided scan: later i has a larger index, keep first
+            best = v;
+            bidx = i;
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bidx, o);
+        if (ov > best || (ov == best && oi < bidx)) {
+            best = ov;
+            bidx = oi;
+        }
+    }
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (lane == 0) {
+        bv[warp] = best;
+        bi[warp] = bidx;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        best = bv[0];
+        bidx = bi[0];
+        for (int j = 1; j < kArgmaxThreads / 32; j++)
+            if (bv[j] > best || (bv[j] == best && bi[j] < bidx)) {
+                best = bv[j];
+                bidx = bi[j];
+            }
+        *idx_out = bidx;
+        if (history) {
+            const int at = *pos;
+            if (at >= 0 && at < hist_len) history[at] = bidx;
+        }
+    }
+}
+
+__global__ void advance_kernel(int* pos, int delta) {
+    pdl_launch_dependents();
+    pdl_wait();
+    if (threadIdx.x == 0) *pos += delta;
+}
+
+}  // namespace hq4
+
+using namespace hq4;
+
+extern "C" int hq4_embed_f16(const uint16_t* table, const int* ids, int n_tokens, int hidden,
+                             float* out, void* stream) {
+    if (int rc = check_device_cap()) return rc;
+    if (n_tokens <= 0 || hidden <= 0) return HQ4_ERR_SHAPE;
+    return launch_pdl(embed_kernel, dim3(std::min(8, (hidden + 255) / 256), n_tokens), dim3(256), 0,
+                      static_cast<cudaStream_t>(stream), reinterpret_cast<const __half*>(table), ids,
+                      n_tokens, hidden, out);
+}
+
+extern "C" int hq4_attention(const float* q, const float* k_cache, const float* v_cache, float* out,
+                             int n_heads, int n_kv, int head_dim, int max_ctx, const int* pos,
+                             int n_tokens, float scale, void* stream) {
+    if (int rc = check_device_cap()) return rc;
+    if (n_heads <= 0 || n_kv <= 0 || n_heads % n_kv || head_dim % 32 || head_dim > 256 ||
+        n_tokens <= 0 || max_ctx <= 0)
+        return HQ4_ERR_SHAPE;
+    const size_t smem = (size_t)max_ctx * sizeof(float);
+    if (smem > 200 * 1024) return HQ4_ERR_SHAPE;
+    static bool attr = false;
+    if (!attr) {
+        cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        attr = true;
+    }
+    return launch_pdl(attention_kernel, dim3(n_heads, n_tokens), dim3(kAttnThreads), smem,
+                      static_cast<cudaStream_t>(stream), q, k_cache, v_cache, out, n_heads, n_kv,
+                      head_dim, max_ctx, pos, scale);
+}
+
+extern "C" int hq4_argmax(const float* x, int n, int* idx_out, int* history, int hist_len,
+                          const int* pos, void* stream) {
+    if (int rc = check_device_cap()) return rc;
+    if (n <= 0) return HQ4_ERR_SHAPE;
+    if (history && (!pos || hist_len <= 0)) return HQ4_ERR_SHAPE;
+    return launch_pdl(argmax_kernel, dim3(1), dim3(kArgmaxThreads), 0, static_cast<cudaStream_t>(stream),
+                      x, n, idx_out, history, hist_len, pos);
+}
+
+extern "C" int hq4_advance_position(int* pos, int delta, void* stream) {
+    if (int rc = check_device_cap()) return rc;
+    return launch_pdl(advance_kernel, dim3(1), dim3(32), 0, static_cast<cudaStream_t>(stream), pos, delta);
+}
+
+extern "C" int hq4_gemv_norm(const uint32_t* w, const uint16_t* scales, const uint16_t* biases,
+                             const float* x, float* out, int n_out, int n_in, int gs, int m,
+                             const float* norm_w, float eps, int silu_mul, const float* row_add,
+                             const float* residual, void* stream) {
+    if (int rc = check_device_cap()) return rc;
+    if (m <= 0 || (silu_mul && n_out % 16)) return HQ4_ERR_SHAPE;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const int n_store = silu_mul ? n_out / 2 : n_out;
+    for (int i = 0; i < m; i++) {
+        int rc = gemv_launch_stage(w, scales, biases, x + (size_t)i * n_in, out + (size_t)i * n_store,
+                                   n_out, n_in, gs, silu_mul ? nullptr : row_add,
+                                   (residual && !silu_mul) ? residual + (size_t)i * n_out : nullptr, norm_w,
+                                   eps, silu_mul ? 1 : 0, 0, 0, 0, 0, 0, nullptr, nullptr, nullptr,
+                                   nullptr, nullptr, nullptr, st);
+        if (rc) return rc;
+    }
+    return HQ4_OK;
+}
+
+extern "C" int hq4_qkv_rope(const uint32_t* w, const uint16_t* scales, const uint16_t* biases,
+                            const float* x, int n_heads, int n_kv, int head_dim, int n_in, int gs, int m,
+                            const float* norm_w, float eps, const float* bias, const int* pos,
+                            const float* rope_cos, const float* rope_sin, int max_ctx, float* q_out,
+                            float* k_cache, float* v_cache, void* stream) {
+    if (int rc = check_device_cap()) return rc;
+    if (m <= 0 || head_dim % 16 || n_heads % n_kv) return HQ4_ERR_SHAPE;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const int half = head_dim / 2;
+    const int q_strips = n_heads * half / 8, k_strips = n_kv * half / 8;
+    const int n_out = (n_heads + 2 * n_kv) * head_dim;
+    for (int i = 0; i < m; i++) {
+        int rc = gemv_launch_stage(w, scales, biases, x + (size_t)i * n_in, q_out, n_out, n_in, gs, bias,
+                                   nullptr, norm_w, eps, 2, q_strips, k_strips, head_dim, max_ctx, i, pos,
+                                   rope_cos, rope_sin, q_out + (size_t)i * n_heads * head_dim, k_cache,
+                                   v_cache, st);
+        if (rc) return rc;
+    }
+    return HQ4_OK;
+}

@@ -89,3 +89,464 @@ class QLinear:
         h_out.copy_(d_out, non_blocking=True)
         torch.cuda.current_stream(self.device).synchronize()
         return h_out.numpy().copy().reshape(*lead, self.n_out)
+
+
+# ---------------------------------------------------------------------------
+# The qwen2 stage (hetero/cpu_model.py:164-368) on the device
+# ---------------------------------------------------------------------------
+
+def rope_tables(head_dim: int, base: float, n: int):
+    """cos/sin tables [n][head_dim/2], computed on the host with the same NumPy
+    float32 expression as the reference's RoPE (hetero/cpu_model.py:181-193),
+    so the rotation is bit-identical to it."""
+    half = head_dim // 2
+    inv = base ** (-np.arange(0, half, dtype=np.float32) * 2.0 / head_dim)
+    ang = np.arange(n, dtype=np.float32)[:, None] * inv[None, :]
+    return np.cos(ang), np.sin(ang)
+
+
+def rope_pair_rows(n_heads: int, head_dim: int) -> np.ndarray:
+    """Row order for q or k that puts the rotation pair (d, d + hd/2) of every
+    head on rows g and g+8 of one 16-row strip (the layout hq4_qkv_rope reads)."""
+    half = head_dim // 2
+    rows = []
+    for h in range(n_heads):
+        for jb in range(0, half, 8):
+            base = h * head_dim + jb
+            rows.extend(range(base, base + 8))
+            rows.extend(range(base + half, base + half + 8))
+    return np.asarray(rows, dtype=np.int64)
+
+
+def interleave_gate_up(gate: np.ndarray, up: np.ndarray) -> np.ndarray:
+    """Rows of the fused gate|up matrix: per 16-row strip, gate rows 8s..8s+7
+    then up rows 8s..8s+7 (the layout the silu*up epilogue reads)."""
+    n = gate.shape[0]
+    if n % 8:
+        raise ValueError("intermediate size must be a multiple of 8")
+    g = gate.reshape(n // 8, 8, *gate.shape[1:])
+    u = up.reshape(n // 8, 8, *up.shape[1:])
+    return np.concatenate([g, u], axis=1).reshape(2 * n, *gate.shape[1:])
+
+
+class _Packed:
+    """A packed int4 matrix on the device (w int32 view, fp16 scales/biases)."""
+
+    def __init__(self, w, s, b, device):
+        self.w = _dev_array(w, device=device)
+        self.s = _dev_array(s, torch.float16, device)
+        self.b = _dev_array(b, torch.float16, device)
+        self.n_out, self.n_in = int(w.shape[0]), int(w.shape[1]) * 8
+
+
+class DeviceKVCache:
+    """Per-request KV cache of a whole stage: fp32 k, v [layers][n_kv][max_ctx][hd]
+    and the device position the kernels read (the reference keeps one growing
+    cache per layer, hetero/cpu_model.py:207-230; here the capacity is
+    preallocated and `offset` mirrors the position on the host)."""
+
+    def __init__(self, n_layers: int):
+        self.n_layers = n_layers
+        self.k = self.v = self.pos = None
+        self.offset = 0
+
+    def __len__(self):
+        return self.n_layers
+
+    def __getitem__(self, i):
+        return self  # per-layer views are taken by the stage
+
+    def allocate(self, n_kv, head_dim, max_ctx, device):
+        if self.k is None:
+            shape = (self.n_layers, n_kv, max_ctx, head_dim)
+            self.k = torch.zeros(shape, dtype=torch.float32, device=device)
+            self.v = torch.zeros(shape, dtype=torch.float32, device=device)
+            self.pos = torch.zeros(1, dtype=torch.int32, device=device)
+            self.max_ctx = max_ctx
+
+
+class _Layer:
+    def __init__(self, cfg, w, idx, device):
+        from . import _lib
+        p = f"model.layers.{idx}"
+        H = cfg["hidden_size"]
+        nh, nkv = cfg["num_attention_heads"], cfg["num_key_value_heads"]
+        hd = H // nh
+        gs = cfg["quantization"]["group_size"]
+        get = lambda proj, part: w[f"{p}.{proj}.{part}"]
+        pq, pk = rope_pair_rows(nh, hd), rope_pair_rows(nkv, hd)
+        parts = []
+        for part in ("weight", "scales", "biases"):
+            q = get("self_attn.q_proj", part)[pq]
+            k = get("self_attn.k_proj", part)[pk]
+            v = get("self_attn.v_proj", part)
+            parts.append(np.concatenate([q, k, v], axis=0))
+        self.qkv = _Packed(*parts, device)
+        bias = []
+        for proj, perm, n in (("q_proj", pq, nh * hd), ("k_proj", pk, nkv * hd), ("v_proj", None, nkv * hd)):
+            b = w.get(f"{p}.self_attn.{proj}.bias")
+            b = np.zeros(n, np.float32) if b is None else np.asarray(b, np.float32)
+            bias.append(b[perm] if perm is not None else b)
+        self.qkv_bias = _dev_array(np.concatenate(bias), torch.float32, device)
+        self.o = _Packed(get("self_attn.o_proj", "weight"), get("self_attn.o_proj", "scales"),
+                         get("self_attn.o_proj", "biases"), device)
+        if w.get(f"{p}.self_attn.o_proj.bias") is not None:
+            raise NotImplementedError("o_proj bias")
+        gu = [interleave_gate_up(get("mlp.gate_proj", part), get("mlp.up_proj", part))
+              for part in ("weight", "scales", "biases")]
+        self.gate_up = _Packed(*gu, device)
+        self.down = _Packed(get("mlp.down_proj", "weight"), get("mlp.down_proj", "scales"),
+                            get("mlp.down_proj", "biases"), device)
+        self.in_w = _dev_array(np.asarray(w[f"{p}.input_layernorm.weight"], np.float32), torch.float32, device)
+        self.post_w = _dev_array(np.asarray(w[f"{p}.post_attention_layernorm.weight"], np.float32),
+                                 torch.float32, device)
+        self.gs, self.H, self.nh, self.nkv, self.hd = gs, H, nh, nkv, hd
+        self.I = cfg["intermediate_size"]
+        self._lib = _lib.load()
+
+
+class Stage:
+    """The device counterpart of ``hetero/cpu_model.py:Stage`` (same constructor
+    and call signature).  Hidden states, KV cache and softmax are fp32 as in
+    the reference; every product is a libhq4 kernel.
+
+    Per layer, five launches: q|k|v GEMV (RMSNorm prologue, bias + RoPE +
+    cache append epilogue), attention, o GEMV (+ residual), gate|up GEMV
+    (RMSNorm prologue, silu*up epilogue), down GEMV (+ residual)."""
+
+    def __init__(self, cfg: dict, spec, w: dict, device="cuda", max_ctx: int = 2048):
+        from . import _lib, synth
+        if cfg.get("model_type") != "qwen2" or "quantization" not in cfg:
+            raise NotImplementedError("device backend handles quantised qwen2 only")
+        if cfg["quantization"]["bits"] != 4:
+            raise NotImplementedError("device backend reads 4-bit weights only")
+        self.cfg, self.spec = cfg, spec
+        self.device = torch.device(device)
+        self.lib = _lib.load()
+        self.max_ctx = int(max_ctx)
+        self.eps = float(cfg["rms_norm_eps"])
+        H = cfg["hidden_size"]
+        self.H, self.nh, self.nkv = H, cfg["num_attention_heads"], cfg["num_key_value_heads"]
+        self.hd = H // self.nh
+        self.gs = cfg["quantization"]["group_size"]
+        self.I = cfg["intermediate_size"]
+        self.V = cfg["vocab_size"]
+        # the reference scales scores by head_dim ** -0.5 as a float32 multiply
+        self.scale = float(np.float32(self.hd ** -0.5))
+        self.layers = [_Layer(cfg, w, i, self.device) for i in range(spec.start, spec.end)]
+        self.embed_table = None
+        self.embed_q = None
+        if spec.embed:
+            if synth.EMBED_SYNTH_KEY in w:
+                t = torch.empty((self.V, H), dtype=torch.float16, device=self.device)
+                rc = self.lib.hq4_synth_embed_f16(int(w[synth.EMBED_SYNTH_KEY]), self.V, H, 0.02,
+                                                  t.data_ptr(), self._stream())
+                _lib.check(rc, "hq4_synth_embed_f16")
+                self.embed_table = t
+            elif "model.embed_tokens.table" in w:
+                self.embed_table = _dev_array(w["model.embed_tokens.table"], torch.float16, self.device)
+            else:  # quantised table, dequantised row by row (cpu_model.py:334-338)
+                self.embed_q = _Packed(w["model.embed_tokens.weight"], w["model.embed_tokens.scales"],
+                                       w["model.embed_tokens.biases"], self.device)
+        if spec.head:
+            self.norm_w = _dev_array(np.asarray(w["model.norm.weight"], np.float32), torch.float32, self.device)
+            if cfg.get("tie_word_embeddings", False):
+                self.lm_head = _Packed(w["model.embed_tokens.weight"], w["model.embed_tokens.scales"],
+                                       w["model.embed_tokens.biases"], self.device)
+                self.lm_bias = None
+            else:
+                self.lm_head = _Packed(w["lm_head.weight"], w["lm_head.scales"], w["lm_head.biases"],
+                                       self.device)
+                lb = w.get("lm_head.bias")
+                self.lm_bias = None if lb is None else _dev_array(np.asarray(lb, np.float32), torch.float32,
+                                                                  self.device)
+        cos, sin = rope_tables(self.hd, float(cfg["rope_theta"]), self.max_ctx)
+        self.rope_cos = _dev_array(cos, torch.float32, self.device)
+        self.rope_sin = _dev_array(sin, torch.float32, self.device)
+
+    # -- plumbing ----------------------------------------------------------
+    def _stream(self):
+        return torch.cuda.current_stream(self.device).cuda_stream
+
+    def _check(self, rc, what):
+        from . import _lib
+        _lib.check(rc, what)
+
+    def new_caches(self) -> DeviceKVCache:
+        c = DeviceKVCache(len(self.layers))
+        c.allocate(self.nkv, self.hd, self.max_ctx, self.device)
+        return c
+
+    # -- pieces ------------------------------------------------------------
+    def embed(self, ids) -> torch.Tensor:
+        ids_np = np.asarray(ids).reshape(-1).astype(np.int32)
+        n = ids_np.size
+        out = torch.empty((n, self.H), dtype=torch.float32, device=self.device)
+        if self.embed_table is not None:
+            d_ids = torch.from_numpy(ids_np).to(self.device)
+            self._check(self.lib.hq4_embed_f16(self.embed_table.data_ptr(), d_ids.data_ptr(), n, self.H,
+                                               out.data_ptr(), self._stream()), "hq4_embed_f16")
+        else:
+            e = self.embed_q
+            for i, t in enumerate(ids_np):
+                self._check(self.lib.hq4_dequant(e.w.data_ptr(), e.s.data_ptr(), e.b.data_ptr(),
+                                                 out[i].data_ptr(), int(t), int(t) + 1, self.H, self.gs,
+                                                 self._stream()), "hq4_dequant")
+        return out.view(*np.asarray(ids).shape, self.H)
+
+    def layer_forward(self, i: int, h: torch.Tensor, cache: DeviceKVCache, L: int, bufs=None):
+        """One decoder layer on L tokens, in place on h [L, H]."""
+        lay, lib, st = self.layers[i], self.lib, self._stream()
+        q = bufs["q"] if bufs else torch.empty((L, self.nh * self.hd), dtype=torch.float32, device=self.device)
+        a = bufs["a"] if bufs else torch.empty((L, self.nh * self.hd), dtype=torch.float32, device=self.device)
+        m = bufs["m"] if bufs else torch.empty((L, self.I), dtype=torch.float32, device=self.device)
+        kc, vc = cache.k[i], cache.v[i]
+        self._check(lib.hq4_qkv_rope(lay.qkv.w.data_ptr(), lay.qkv.s.data_ptr(), lay.qkv.b.data_ptr(),
+                                     h.data_ptr(), self.nh, self.nkv, self.hd, self.H, self.gs, L,
+                                     lay.in_w.data_ptr(), self.eps, lay.qkv_bias.data_ptr(),
+                                     cache.pos.data_ptr(), self.rope_cos.data_ptr(),
+                                     self.rope_sin.data_ptr(), cache.max_ctx, q.data_ptr(), kc.data_ptr(),
+                                     vc.data_ptr(), st), "hq4_qkv_rope")
+        self._check(lib.hq4_attention(q.data_ptr(), kc.data_ptr(), vc.data_ptr(), a.data_ptr(), self.nh,
+                                      self.nkv, self.hd, cache.max_ctx, cache.pos.data_ptr(), L, self.scale,
+                                      st), "hq4_attention")
+        self._check(lib.hq4_gemv_fused(lay.o.w.data_ptr(), lay.o.s.data_ptr(), lay.o.b.data_ptr(),
+                                       a.data_ptr(), h.data_ptr(), self.H, self.H, self.gs, L, None,
+                                       h.data_ptr(), st), "hq4_gemv_fused(o)")
+        self._check(lib.hq4_gemv_norm(lay.gate_up.w.data_ptr(), lay.gate_up.s.data_ptr(),
+                                      lay.gate_up.b.data_ptr(), h.data_ptr(), m.data_ptr(), 2 * self.I,
+                                      self.H, self.gs, L, lay.post_w.data_ptr(), self.eps, 1, None, None,
+                                      st), "hq4_gemv_norm(gate_up)")
+        self._check(lib.hq4_gemv_fused(lay.down.w.data_ptr(), lay.down.s.data_ptr(), lay.down.b.data_ptr(),
+                                       m.data_ptr(), h.data_ptr(), self.H, self.I, self.gs, L, None,
+                                       h.data_ptr(), st), "hq4_gemv_fused(down)")
+
+    def head_logits(self, h: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """RMSNorm + vocabulary projection of rows h [R, H] -> [R, V]."""
+        R = h.shape[0]
+        if out is None:
+            out = torch.empty((R, self.V), dtype=torch.float32, device=self.device)
+        lm = self.lm_head
+        self._check(self.lib.hq4_gemv_norm(lm.w.data_ptr(), lm.s.data_ptr(), lm.b.data_ptr(), h.data_ptr(),
+                                           out.data_ptr(), self.V, self.H, self.gs, R, self.norm_w.data_ptr(),
+                                           self.eps, 0,
+                                           self.lm_bias.data_ptr() if self.lm_bias is not None else None,
+                                           None, self._stream()), "hq4_gemv_norm(lm_head)")
+        return out
+
+    def _advance(self, cache: DeviceKVCache, L: int):
+        self._check(self.lib.hq4_advance_position(cache.pos.data_ptr(), L, self._stream()),
+                    "hq4_advance_position")
+        cache.offset += L
+
+    # -- the reference's surface ---------------------------------------------
+    def body(self, x, caches=None, mask=None):
+        """Embedding (if owned) plus this stage's layers; no head."""
+        return self._run(x, caches, apply_head=False, last_only=False)
+
+    def head_forward(self, x, last_only: bool = True):
+        h = self._as_hidden(x)
+        if last_only:
+            h = h[:, -1:, :]
+        B, L, H = h.shape
+        return self.head_logits(h.reshape(B * L, H).contiguous()).view(B, L, self.V)
+
+    def __call__(self, x, caches=None, mask=None, apply_head=True, last_only=False):
+        return self._run(x, caches, apply_head, last_only)
+
+    def _as_hidden(self, x) -> torch.Tensor:
+        if isinstance(x, torch.Tensor):
+            return x.to(self.device, torch.float32)
+        return torch.from_numpy(np.ascontiguousarray(x, dtype=np.float32)).to(self.device)
+
+    def _run(self, x, caches, apply_head, last_only):
+        if self.spec.embed:
+            h = self.embed(x)
+        else:
+            h = self._as_hidden(x)
+        if h.dim() != 3 or h.shape[0] != 1:
+            raise NotImplementedError("device stage runs batch 1 (as the reference's decode)")
+        L = h.shape[1]
+        h = h.reshape(L, self.H).contiguous()
+        cache = caches
+        if cache is None or isinstance(cache, list):
+            cache = DeviceKVCache(len(self.layers))  # no cache: a scratch one (positions 0..L-1)
+        cache.allocate(self.nkv, self.hd, self.max_ctx, self.device)
+        if cache.offset + L > cache.max_ctx:
+            raise ValueError(f"context {cache.offset + L} exceeds max_ctx {cache.max_ctx}")
+        for i in range(len(self.layers)):
+            self.layer_forward(i, h, cache, L)
+        if len(self.layers):
+            self._advance(cache, L)
+        if self.spec.head and apply_head:
+            rows = h[-1:] if last_only else h
+            return self.head_logits(rows.contiguous()).view(1, rows.shape[0], self.V)
+        return h.view(1, L, self.H)
+
+
+class CudaBackend:
+    """The reference's backend surface (hetero/backends.py:70-130) on B200."""
+
+    name = "cuda+q4"
+    weight_expansion = 1.0
+
+    def __init__(self, device="cuda", max_ctx: int = 2048):
+        self.device = torch.device(device)
+        self.max_ctx = max_ctx
+
+    def load_stage(self, model_dir, spec, index=None):
+        raise NotImplementedError("checkpoint loading is not built yet; use build_stage(cfg, spec, weights)")
+
+    def build_stage(self, cfg, spec, weights):
+        return Stage(cfg, spec, weights, self.device, self.max_ctx)
+
+    def new_caches(self, n: int):
+        return DeviceKVCache(n)
+
+    def array(self, data):
+        return np.asarray(data)
+
+    def eval(self, *xs):
+        torch.cuda.current_stream(self.device).synchronize()
+
+    def hidden(self, shape):
+        return torch.zeros(shape, dtype=torch.float32, device=self.device)
+
+    def to_wire(self, x) -> np.ndarray:
+        if isinstance(x, torch.Tensor):
+            return x.to(torch.float16).cpu().numpy()
+        return np.asarray(x, dtype=np.float16)
+
+    def from_wire(self, a: np.ndarray):
+        return torch.from_numpy(np.asarray(a, dtype=np.float32)).to(self.device)
+
+    def sample(self, logits, temperature: float, top_p: float, rng) -> int:
+        from . import _lib
+        if temperature <= 0 and isinstance(logits, torch.Tensor) and logits.is_cuda:
+            z = logits.reshape(-1).contiguous()
+            idx = torch.empty(1, dtype=torch.int32, device=z.device)
+            lib = _lib.load()
+            _lib.check(lib.hq4_argmax(z.data_ptr(), z.numel(), idx.data_ptr(), None, 0, None,
+                                      torch.cuda.current_stream(z.device).cuda_stream), "hq4_argmax")
+            return int(idx.item())
+        # temperature / top-p sampling: the reference's own NumPy procedure
+        z = logits.reshape(-1).float().cpu().numpy() if isinstance(logits, torch.Tensor) else \
+            np.asarray(logits, dtype=np.float32).reshape(-1)
+        if temperature <= 0:
+            return int(z.argmax())
+        z = z / temperature
+        z -= z.max()
+        p = np.exp(z)
+        p /= p.sum()
+        if top_p < 1.0:
+            order = np.argsort(-p)
+            keep = np.cumsum(p[order]) - p[order] < top_p
+            masked = np.zeros_like(p)
+            masked[order[keep]] = p[order[keep]]
+            p = masked / masked.sum()
+        return int(rng.choice(len(p), p=p))
+
+    def peak_bytes(self) -> int:
+        return int(torch.cuda.max_memory_allocated(self.device))
+
+    def reset_peak(self):
+        torch.cuda.reset_peak_memory_stats(self.device)
+
+    def clear_cache(self):
+        torch.cuda.empty_cache()
+
+
+def get(name: str = "auto"):
+    """`cuda` selects this backend (the reference's get() chooses mlx/numpy)."""
+    if name in ("auto", "cuda", "gpu"):
+        return CudaBackend()
+    raise ValueError(f"unknown backend {name}")
+
+
+class GreedyDecoder:
+    """Batch-1 greedy generation on one device stage that owns the embedding
+    and the head (the single-node decode loop of hetero/coordinator.py:266-292).
+
+    The prompt is prefilled eagerly; after that one CUDA graph holds a whole
+    decode step -- embedding of the previous token, every layer, the head,
+    argmax, position advance -- and is replayed once per token.  The token, the
+    position and the history of generated tokens stay on the device, so there
+    is no host round trip between steps; `generate` reads the history once."""
+
+    def __init__(self, stage: Stage, cache: Optional[DeviceKVCache] = None):
+        if not (stage.spec.embed and stage.spec.head):
+            raise ValueError("GreedyDecoder needs a stage with both embedding and head")
+        self.stage = stage
+        self.cache = cache or stage.new_caches()
+        dev = stage.device
+        self.tok = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.history = torch.zeros(stage.max_ctx, dtype=torch.int32, device=dev)
+        self.h = torch.empty((1, stage.H), dtype=torch.float32, device=dev)
+        self.logits = torch.empty((1, stage.V), dtype=torch.float32, device=dev)
+        self.bufs = {"q": torch.empty((1, stage.nh * stage.hd), dtype=torch.float32, device=dev),
+                     "a": torch.empty((1, stage.nh * stage.hd), dtype=torch.float32, device=dev),
+                     "m": torch.empty((1, stage.I), dtype=torch.float32, device=dev)}
+        self.graph = None
+        self.stream = torch.cuda.Stream(dev)
+
+    def _argmax(self):
+        s = self.stage
+        s._check(s.lib.hq4_argmax(self.logits.data_ptr(), s.V, self.tok.data_ptr(), self.history.data_ptr(),
+                                  s.max_ctx, self.cache.pos.data_ptr(), s._stream()), "hq4_argmax")
+
+    def _step(self):
+        s = self.stage
+        s._check(s.lib.hq4_embed_f16(s.embed_table.data_ptr(), self.tok.data_ptr(), 1, s.H,
+                                     self.h.data_ptr(), s._stream()), "hq4_embed_f16")
+        for i in range(len(s.layers)):
+            s.layer_forward(i, self.h, self.cache, 1, self.bufs)
+        s._check(s.lib.hq4_advance_position(self.cache.pos.data_ptr(), 1, s._stream()), "advance")
+        s.head_logits(self.h, self.logits)
+        self._argmax()
+
+    def prefill(self, prompt) -> None:
+        """Prompt [1, P] through the stage (causal), first token sampled on device."""
+        s = self.stage
+        if s.embed_table is None:
+            raise NotImplementedError("graph decode needs an fp16 embedding table")
+        with torch.cuda.stream(self.stream):
+            logits = s(prompt, self.cache, apply_head=True, last_only=True)
+            self.logits.copy_(logits.view(1, s.V))
+            self._argmax()
+        self.start = self.cache.offset
+
+    def capture(self) -> None:
+        """Record one decode step as a CUDA graph (after one eager step, which
+        is a real step: its token goes to the history like any other)."""
+        with torch.cuda.stream(self.stream):
+            self._step()
+            self.cache.offset += 1
+            torch.cuda.current_stream().synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=self.stream):
+                self._step()
+        self.graph = g
+
+    def steps(self, n: int) -> None:
+        """Replay n decode steps (asynchronously on the decoder's stream)."""
+        if self.cache.offset + n > self.stage.max_ctx:
+            raise ValueError("context would exceed max_ctx")
+        with torch.cuda.stream(self.stream):
+            for _ in range(n):
+                self.graph.replay()
+        self.cache.offset += n
+
+    def tokens(self):
+        """Generated tokens so far (first from the prefill)."""
+        torch.cuda.current_stream().wait_stream(self.stream)
+        return self.history[self.start:self.cache.offset + 1].cpu().tolist()
+
+    def generate(self, prompt, n_tokens: int):
+        """Prefill + n_tokens-1 decode steps -> list of n_tokens token ids."""
+        self.prefill(prompt)
+        if n_tokens > 1:
+            self.capture()
+            if n_tokens > 2:
+                self.steps(n_tokens - 2)
+        toks = self.tokens()
+        return toks[:n_tokens]

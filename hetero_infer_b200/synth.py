@@ -12,6 +12,16 @@ benchmark configurations name:
   ``N(0, 0.02)`` (qwen2 has them; ``hetero/cpu_model.py:266`` reads them with
   ``w.get``).
 
+The embedding table (152064 x 3584 for the 7B shape) is the one tensor too
+large to generate on the host for every run, and only the rows looked up
+matter.  It uses a counter-based generator instead: element (r, c) is
+0.02 * (sum of 12 uniform 24-bit integers - 6 * 2^24) / 2^24 -- an
+Irwin-Hall(12) approximation of N(0, 1) -- with the integers drawn from
+splitmix64 of (seed, r, c, i), summed exactly in integers, converted to fp32
+once, scaled, and rounded to fp16.  ``embed_rows`` evaluates any rows on the
+host; the device kernel ``hq4_synth_embed_f16`` fills the full table with the
+same bits.
+
 Every tensor draws from its own ``numpy.random.default_rng([seed, crc32(name)])``
 stream, so one tensor (or one layer) can be regenerated alone and the values do
 not depend on which other tensors were generated before it.
@@ -92,6 +102,33 @@ def fp16_normal(seed: int, name: str, shape, std: float = 0.02) -> np.ndarray:
     return (r.standard_normal(shape, dtype=np.float32) * std).astype(np.float16)
 
 
+def _splitmix64(z: np.ndarray) -> np.ndarray:
+    with np.errstate(over="ignore"):
+        z = z + np.uint64(0x9E3779B97F4A7C15)
+        z = (z ^ (z >> np.uint64(30))) * np.uint64(0xBF58476D1CE4E5B9)
+        z = (z ^ (z >> np.uint64(27))) * np.uint64(0x94D049BB133111EB)
+        return z ^ (z >> np.uint64(31))
+
+
+def embed_rows(seed: int, ids, hidden: int, std: float = 0.02) -> np.ndarray:
+    """Rows `ids` of the counter-based synthetic embedding table, fp16."""
+    ids = np.asarray(ids, dtype=np.uint64).reshape(-1)
+    col = np.arange(hidden, dtype=np.uint64)
+    with np.errstate(over="ignore"):
+        key = (np.uint64(seed) * np.uint64(0x9E3779B97F4A7C15)
+               + ids[:, None] * np.uint64(hidden) + col[None, :])
+        acc = np.zeros(key.shape, dtype=np.int64)
+        for i in range(12):
+            z = _splitmix64(key * np.uint64(12) + np.uint64(i))
+            acc += (z >> np.uint64(40)).astype(np.int64)
+    acc -= 6 * (1 << 24)
+    v = acc.astype(np.float32) * np.float32(1.0 / (1 << 24))
+    return (v * np.float32(std)).astype(np.float16)
+
+
+EMBED_SYNTH_KEY = "model.embed_tokens.synth_seed"
+
+
 def activation(seed: int, name: str, shape, dtype=np.float32) -> np.ndarray:
     return rng_for(seed, name).standard_normal(shape, dtype=np.float32).astype(dtype)
 
@@ -119,15 +156,16 @@ def model_weights(cfg: dict, seed: int, layers: Optional[Iterable[int]] = None,
                   qkv_bias: bool = True) -> Dict[str, np.ndarray]:
     """All tensors a stage owning ``layers`` (and optionally embed/head) needs.
 
-    The embedding is an fp16 table ``model.embed_tokens.table`` (the benchmark
-    configuration asks for fp16 N(0, 0.02) embeddings rather than a quantised
-    table)."""
+    The embedding is the counter-based fp16 table described above (the
+    benchmark configuration asks for fp16 N(0, 0.02) embeddings rather than a
+    quantised table); it is represented by its seed under EMBED_SYNTH_KEY and
+    materialised by whoever needs it (``embed_rows`` on the host, the device
+    kernel on the GPU)."""
     if layers is None:
         layers = range(cfg["num_hidden_layers"])
     out: Dict[str, np.ndarray] = {}
     if embed:
-        out["model.embed_tokens.table"] = fp16_normal(
-            seed, "model.embed_tokens.table", (cfg["vocab_size"], cfg["hidden_size"]))
+        out[EMBED_SYNTH_KEY] = np.array(int(seed) & 0x7FFFFFFF, dtype=np.int64)
     for i in layers:
         out.update(layer_weights(cfg, seed, i, qkv_bias))
     if head:

@@ -68,6 +68,69 @@ int hq4_gemv_fused(const uint32_t* w, const uint16_t* scales, const uint16_t* bi
 int hq4_dequant(const uint32_t* w, const uint16_t* scales, const uint16_t* biases,
                 float* out, int row0, int row1, int n_in, int gs, void* stream);
 
+/* ---- qwen2 stage forward (hetero/cpu_model.py:164-368) ---------------------
+ * Hidden states, KV cache and attention are fp32 as in the reference's NumPy
+ * stage.  `pos` is a device int: the position of the call's first token
+ * (the reference's KVCache.offset, cpu_model.py:207-230); it lets a whole
+ * decode step be replayed as one CUDA graph. */
+
+/* out[t] = fp32(table[ids[t]]) for an fp16 embedding table [vocab][hidden];
+ * ids is a device int array of n_tokens. */
+int hq4_embed_f16(const uint16_t* table, const int* ids, int n_tokens, int hidden,
+                  float* out, void* stream);
+
+/* GEMV with RMSNorm of x fused into its prologue (cpu_model.py:164-166):
+ *   x' = (x * (1/sqrt(mean(x^2) + eps))) * norm_w          (norm_w may be NULL)
+ * silu_mul = 0: out[m][n_out] = x'.W^T (+ row_add) (+ residual)
+ * silu_mul = 1: W holds gate and up rows interleaved per 16-row strip (rows
+ *   0-7 = gate rows 8s..8s+7, rows 8-15 = up rows 8s..8s+7) and
+ *   out[m][n_out/2] = silu(gate) * up  (cpu_model.py:169-170, 291-292). */
+int hq4_gemv_norm(const uint32_t* w, const uint16_t* scales, const uint16_t* biases,
+                  const float* x, float* out, int n_out, int n_in, int gs, int m,
+                  const float* norm_w, float eps, int silu_mul, const float* row_add,
+                  const float* residual, void* stream);
+
+/* The attention block's input projections for m tokens at positions
+ * *pos .. *pos+m-1 (cpu_model.py:269-278): RMSNorm(x) . [Wq;Wk;Wv]^T + bias,
+ * rotary embedding of q and k (half-split, cos/sin tables [max_ctx][head_dim/2]
+ * built on the host as cpu_model.py:173-204 builds them), k and v appended to
+ * the caches [n_kv][max_ctx][head_dim], rotated q written to q_out
+ * [m][n_heads][head_dim].  W/scales/biases/bias rows are q, k, v concatenated
+ * with the q and k rows of each head permuted so that every 16-row strip
+ * holds 8 rotation pairs: rows 0-7 = dims j..j+7, rows 8-15 = dims
+ * j+hd/2..j+hd/2+7 (j = 0, 8, ..., hd/2-8). */
+int hq4_qkv_rope(const uint32_t* w, const uint16_t* scales, const uint16_t* biases,
+                 const float* x, int n_heads, int n_kv, int head_dim, int n_in, int gs, int m,
+                 const float* norm_w, float eps, const float* bias, const int* pos,
+                 const float* rope_cos, const float* rope_sin, int max_ctx, float* q_out,
+                 float* k_cache, float* v_cache, void* stream);
+
+/* Grouped-query attention for n_tokens queries q [n_tokens][n_heads][head_dim]
+ * at positions *pos + i over cache entries [0, *pos + i] (causal), scores
+ * scaled by `scale`, fp32 softmax (cpu_model.py:233-252); out has the layout
+ * of q. head_dim a multiple of 32 up to 256; max_ctx * 4 bytes <= 200 KB.
+ * Queries whose position is outside [0, max_ctx) write nothing (likewise the
+ * cache writes of hq4_qkv_rope). */
+int hq4_attention(const float* q, const float* k_cache, const float* v_cache, float* out,
+                  int n_heads, int n_kv, int head_dim, int max_ctx, const int* pos,
+                  int n_tokens, float scale, void* stream);
+
+/* Greedy sampling (hetero/backends.py:106-109): index of the largest of x[0..n),
+ * lowest index among equals, written to *idx_out; also to history[*pos] when
+ * history is not NULL and 0 <= *pos < hist_len. */
+int hq4_argmax(const float* x, int n, int* idx_out, int* history, int hist_len, const int* pos,
+               void* stream);
+
+/* Fill an fp16 [vocab][hidden] table with the benchmark's counter-based
+ * synthetic N(0, std) embedding (seeded; see hetero_infer_b200/synth.py,
+ * which evaluates the same rows on the host).  No reference counterpart: the
+ * reference loads its embedding from a checkpoint. */
+int hq4_synth_embed_f16(long long seed, int vocab, int hidden, float std, uint16_t* out,
+                        void* stream);
+
+/* *pos += delta on the device (advances the decode position inside a graph). */
+int hq4_advance_position(int* pos, int delta, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

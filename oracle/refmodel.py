@@ -68,10 +68,21 @@ def build_stage(cm, cfg: dict, weights: Dict[str, np.ndarray], start: int, end: 
 
     The benchmark model has an fp16 embedding table rather than a quantised one;
     the stage's ``embed`` is replaced by a plain fp16->fp32 row lookup, which is
-    what the device stage does too."""
+    what the device stage does too.  A synthetic table (hetero_infer_b200.synth)
+    is evaluated row by row on demand."""
     from hetero.shard import ShardSpec
+    from hetero_infer_b200 import synth
     w = dict(weights)
     table = w.pop("model.embed_tokens.table", None)
+    seed = w.pop(synth.EMBED_SYNTH_KEY, None)
+    hidden = cfg["hidden_size"]
+    if table is None and seed is not None:
+        s_ = int(seed)
+        table_rows = lambda ids: synth.embed_rows(s_, ids, hidden)
+    elif table is not None:
+        table_rows = lambda ids: table[np.asarray(ids).reshape(-1)]
+    else:
+        table_rows = None
     if embed:
         # Stage.__init__ insists on quantised embedding tensors when it owns the
         # embedding; give it placeholders and swap in the fp16 lookup below.
@@ -80,9 +91,9 @@ def build_stage(cm, cfg: dict, weights: Dict[str, np.ndarray], start: int, end: 
         w["model.embed_tokens.biases"] = np.zeros((1, 1), np.float16)
     stage = cm.Stage(cfg, ShardSpec(start, end, embed, head), w)
     if embed:
-        if table is None:
-            raise KeyError("model.embed_tokens.table")
-        stage.embed = lambda ids: table[np.asarray(ids).reshape(-1)].astype(np.float32).reshape(
+        if table_rows is None:
+            raise KeyError("embedding table")
+        stage.embed = lambda ids: table_rows(np.asarray(ids).reshape(-1)).astype(np.float32).reshape(
             *np.asarray(ids).shape, -1)
     return stage
 

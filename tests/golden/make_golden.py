@@ -1,0 +1,122 @@
+"""Generate the golden fixtures in this directory from the reference itself.
+
+Runs the reference's own NumPy stage (hetero/cpu_model.py, imported unmodified
+from the reference tree, with its kernel/q4gemv.c compiled from source into
+oracle/_ref/ by oracle/Makefile) on the seeded synthetic models of
+hetero_infer_b200/synth.py, and records what it produces.  Needs the reference
+tree (build container only); the GPU tests read the fixtures it writes.
+
+  python tests/golden/make_golden.py [--small] [--big]
+
+golden_small.npz  2-layer qwen2 (hidden 256): prompt, 8 greedy tokens and the
+                  per-step last-position logits, for the reference's float and
+                  AVX2 kernel builds.
+golden_7b.json    the benchmark's Qwen2-7B-shape random model (seed 0): 32-token
+                  prompt, 128 greedy tokens, per-step top-1/top-2 margin, logits
+                  L2 norm and top-5 (index, value), for both kernel builds.
+"""
+import argparse
+import json
+import os
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(os.path.dirname(HERE))
+sys.path.insert(0, ROOT)
+
+SMALL = dict(layers=2, hidden=256, heads=4, kv_heads=2, inter=512, vocab=1024)
+SMALL_SEED, SMALL_PROMPT, SMALL_TOKENS = 7, 6, 8
+BIG_SEED, BIG_PROMPT, BIG_TOKENS = 0, 32, 128
+
+
+def run_small(variant):
+    from hetero_infer_b200 import synth
+    from oracle import refmodel
+    cfg = synth.small_config(**SMALL)
+    w = synth.model_weights(cfg, SMALL_SEED)
+    cm = refmodel.load_cpu_model(variant)
+    st = refmodel.build_stage(cm, cfg, w, 0, cfg["num_hidden_layers"], True, True)
+    prompt = synth.prompt_ids(SMALL_SEED, SMALL_PROMPT, cfg["vocab_size"])
+    caches = [cm.KVCache() for _ in st.layers]
+    x, toks, logits = prompt, [], []
+    for _ in range(SMALL_TOKENS):
+        y = st(x, caches, apply_head=True, last_only=True)
+        z = np.asarray(y[0, -1], np.float32)
+        logits.append(z)
+        toks.append(int(z.argmax()))
+        x = np.array([[toks[-1]]])
+    return prompt, np.array(toks, np.int64), np.stack(logits)
+
+
+def run_big(variant):
+    from hetero_infer_b200 import synth
+    from oracle import refmodel
+    cfg = dict(synth.QWEN2_7B)
+    t0 = time.time()
+    w = synth.model_weights(cfg, BIG_SEED)
+    cm = refmodel.load_cpu_model(variant)
+    st = refmodel.build_stage(cm, cfg, w, 0, cfg["num_hidden_layers"], True, True)
+    prompt = synth.prompt_ids(BIG_SEED, BIG_PROMPT, cfg["vocab_size"])
+    caches = [cm.KVCache() for _ in st.layers]
+    x, steps = prompt, []
+    for _ in range(BIG_TOKENS):
+        y = st(x, caches, apply_head=True, last_only=True)
+        z = np.asarray(y[0, -1], np.float32)
+        top = np.argsort(-z, kind="stable")[:5]
+        srt = np.sort(z)
+        steps.append({"token": int(z.argmax()), "margin": float(srt[-1] - srt[-2]),
+                      "norm": float(np.linalg.norm(z)), "top5_idx": [int(i) for i in top],
+                      "top5_val": [float(z[i]) for i in top]})
+        x = np.array([[steps[-1]["token"]]])
+    return prompt, steps, time.time() - t0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--small", action="store_true")
+    ap.add_argument("--big", action="store_true")
+    a = ap.parse_args()
+    if not (a.small or a.big):
+        a.small = a.big = True
+    subprocess.run(["make", "-C", os.path.join(ROOT, "oracle"), "all"], check=True, capture_output=True)
+    if a.small:
+        out = {}
+        for v in ("float", "avx2"):
+            # each variant in its own process: the reference module binds one kernel
+            code = ("import sys, numpy as np; sys.path.insert(0, %r); sys.path.insert(0, %r); "
+                    "import make_golden as m; p, t, l = m.run_small(%r); "
+                    "np.savez(%r, prompt=p, tokens=t, logits=l)") % (
+                ROOT, HERE, v, os.path.join(HERE, f"_tmp_{v}.npz"))
+            subprocess.run([sys.executable, "-c", code], check=True)
+            d = np.load(os.path.join(HERE, f"_tmp_{v}.npz"))
+            out["prompt"] = d["prompt"]
+            out[f"tokens_{v}"], out[f"logits_{v}"] = d["tokens"], d["logits"]
+            os.remove(os.path.join(HERE, f"_tmp_{v}.npz"))
+        np.savez_compressed(os.path.join(HERE, "golden_small.npz"), **out)
+        print("golden_small.npz", {k: v.shape for k, v in out.items()})
+    if a.big:
+        res = {"config": "QWEN2_7B", "seed": BIG_SEED, "prompt_tokens": BIG_PROMPT,
+               "generated": BIG_TOKENS, "variants": {}}
+        for v in ("avx2", "float"):
+            code = ("import sys, json; sys.path.insert(0, %r); sys.path.insert(0, %r); "
+                    "import make_golden as m; p, s, dt = m.run_big(%r); "
+                    "json.dump({'prompt': [int(i) for i in p.reshape(-1)], 'steps': s, 'seconds': dt}, "
+                    "open(%r, 'w'))") % (ROOT, HERE, v, os.path.join(HERE, f"_tmp_{v}.json"))
+            subprocess.run([sys.executable, "-c", code], check=True)
+            d = json.load(open(os.path.join(HERE, f"_tmp_{v}.json")))
+            os.remove(os.path.join(HERE, f"_tmp_{v}.json"))
+            res["prompt"] = d["prompt"]
+            res["variants"][v] = {"steps": d["steps"], "seconds": round(d["seconds"], 1),
+                                  "kernel": "kernel/q4gemv.c built " +
+                                            ("-O3 -mavx2 -mfma -mf16c" if v == "avx2" else "-O3 (portable fp32 path)")}
+            print(v, "tokens", [s["token"] for s in d["steps"]][:16], "...", round(d["seconds"], 1), "s")
+        with open(os.path.join(HERE, "golden_7b.json"), "w") as f:
+            json.dump(res, f)
+
+
+if __name__ == "__main__":
+    main()
