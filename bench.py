@@ -235,6 +235,9 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     ms_max = float(t.item())
     value = world * args.steps * STEP_BYTES / (ms_max * 1e-3) / 1e9
 
+    pipe = None
+    if world > 1 and not args.no_extras:
+        pipe = {f"micro{m}": pipeline_bench(rank, world, dev, m) for m in (4, 8)}
     result = None
     if rank == 0:
         peak, peak_kind = measured_peak()
@@ -255,11 +258,14 @@ def run_ours(args, rank: int, world: int, local_rank: int):
             "clocks": sampler.summary(t_wall0, t_wall1),
             "gpu_launches": len(LAUNCHES) * args.steps,
         }
+        if pipe is not None:
+            result["pipeline"] = pipe
         if not args.no_extras:
             result["per_projection"] = per_projection(lib, dev, gen, stream, q4_on_device)
             result["gemv_3584x18944"] = result["per_projection"]["gate"]
             result["e2e"] = e2e_qlinear(args, dev, cuda_model, synth, np)
-            result["decode"] = decode_bench(dev)
+            if world == 1:
+                result["decode"] = decode_bench(dev)
             if world == 1:
                 result["cpu_baseline"] = cpu_baseline(args, budget_s=args.cpu_seconds)
     if world > 1:
@@ -359,6 +365,49 @@ def decode_bench(dev, n_tokens: int = 128, prompt_len: int = 32):
             "launches_per_token": 28 * 5 + 4, "first_tokens": toks[:8],
             "model": "qwen2-7b-shape random int4 (28 layers, h3584, 28q/4kv, i18944, v152064)",
             "setup_s": round(t_load, 1)}
+
+
+def pipeline_bench(rank: int, world: int, dev, n_micro: int, n_tokens: int = 256, prompt_len: int = 32):
+    """Benchmark config 5: the 7B-shape random model split by the planner over
+    the `world` GPUs (NCCL send/recv of the fp16 hidden state between stages,
+    lm_head row-sharded over all ranks), `n_micro` independent streams in
+    flight, `n_tokens` per stream.  Aggregate decode tok/s over the pipelined
+    decode (device time, max over ranks)."""
+    import torch
+    import torch.distributed as dist
+    from hetero_infer_b200 import pipeline, planner, synth
+    cfg = dict(synth.QWEN2_7B)
+    plan = planner.plan_gpu_pipeline(cfg, world, layer_s=60e-6, head_s=52e-6)
+    spec = plan.specs[rank]
+    w = synth.model_weights(cfg, 0, layers=range(spec.start, spec.end), embed=spec.embed, head=True)
+    comp = pipeline.DeviceCompute(cfg, spec, w, pipeline.head_rows(cfg["vocab_size"], world, rank), dev,
+                                  max_ctx=512)
+    del w
+    pr = pipeline.PipelineRank(pipeline.Comm(rank, world, dev), comp, n_micro)
+    prompts = [synth.prompt_ids(1000 + m, prompt_len, cfg["vocab_size"]) for m in range(n_micro)]
+    pr.prefill(prompts)
+    dist.barrier(device_ids=[dev.index])
+    torch.cuda.synchronize(dev)
+    t0 = time.perf_counter()
+    pr.decode(n_tokens - 1)
+    torch.cuda.synchronize(dev)
+    dt = time.perf_counter() - t0
+    t = torch.tensor([dt], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    dt = float(t.item())
+    gen = n_micro * (n_tokens - 1)
+    zeros = all(t == 0 for toks in pr.tokens for t in toks)
+    return {"streams": n_micro, "tokens_per_stream": n_tokens, "decode_tokens": gen,
+            "tok_s": round(gen / dt, 1), "seconds": round(dt, 3), "ticks": pr.ticks,
+            "ms_per_tick": round(dt * 1e3 / pr.ticks, 4), "cuts": plan.cuts,
+            "head": "row-sharded over all ranks", "wire": "fp16 NCCL send/recv (reference format)",
+            "first_tokens": pr.tokens[0][:6],
+            "tokens_note": ("every token 0, as the reference's own stages produce on this model: its residual "
+                            "stream exceeds fp16 range at the cut, the fp16 wire carries inf, the next RMSNorm "
+                            "NaN, and numpy argmax of NaN logits is 0 (tests/golden/golden_7b_pipe.json)")
+            if zeros else "finite logits",
+            "timing": "host wall clock around the decode loop "
+            "(each tick synchronises on the sampled token), max over ranks"}
 
 
 def e2e_qlinear(args, dev, cuda_model, synth, np):
@@ -481,6 +530,10 @@ def main():
     ap.add_argument("--no-extras", action="store_true",
                     help="skip per-projection, e2e and CPU-baseline legs")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--pipeline-only", type=int, default=0, metavar="TOKENS",
+                    help="N>1: only run the config-5 pipeline (TOKENS per stream, 4 and 8 streams)")
+    ap.add_argument("--decode-only", type=int, default=0, metavar="TOKENS",
+                    help="only run the config-4 decode (TOKENS generated) and print its JSON")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -490,6 +543,25 @@ def main():
     if world != args.gpus and rank == 0:
         print(f"warning: --gpus {args.gpus} but WORLD_SIZE={world}", file=sys.stderr)
 
+    if args.decode_only:
+        import torch
+        torch.cuda.set_device(local_rank)
+        print(json.dumps(decode_bench(torch.device("cuda", local_rank), n_tokens=max(3, args.decode_only))),
+              flush=True)
+        return
+    if args.pipeline_only and world > 1 and args.impl == "ours":
+        import datetime
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local_rank)
+        dev = torch.device("cuda", local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+        out = {f"micro{m}": pipeline_bench(rank, world, dev, m, n_tokens=max(3, args.pipeline_only))
+               for m in (4, 8)}
+        if rank == 0:
+            print(json.dumps({"pipeline": out, "n_gpus": world}), flush=True)
+        dist.destroy_process_group()
+        return
     if args.impl == "reference":
         res = run_reference(args, rank, world)
     else:

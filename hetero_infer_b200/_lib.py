@@ -27,11 +27,11 @@ SIGNATURES = {
     "hq4_gemv": (_I, [_P] * 5 + [_I] * 4 + [_P]),
     "hq4_gemv_fused": (_I, [_P] * 5 + [_I] * 4 + [_P] * 3),
     "hq4_dequant": (_I, [_P] * 4 + [_I] * 4 + [_P]),
-    "hq4_embed_f16": (_I, [_P, _P, _I, _I, _P, _P]),
+    "hq4_embed_f16": (_I, [_P, _P, _I, _I, _I, _P, _P]),
     "hq4_gemv_norm": (_I, [_P] * 5 + [_I] * 4 + [_P, _F, _I, _P, _P, _P]),
     "hq4_qkv_rope": (_I, [_P] * 4 + [_I] * 6 + [_P, _F, _P, _P, _P, _P, _I, _P, _P, _P, _P]),
     "hq4_attention": (_I, [_P] * 4 + [_I] * 4 + [_P, _I, _F, _P]),
-    "hq4_argmax": (_I, [_P, _I, _P, _P, _I, _P, _P]),
+    "hq4_argmax": (_I, [_P, _I, _P, _P, _I, _P, _P, _P]),
     "hq4_synth_embed_f16": (_I, [ctypes.c_longlong, _I, _I, _F, _P, _P]),
     "hq4_advance_position": (_I, [_P, _I, _P]),
 }
@@ -44,6 +44,25 @@ ERRORS = {
 }
 
 _lib = None
+
+# HQ4_CHECKS=1: every call made through `checked()` validates its tensors
+# (device, minimum size, alignment) before the launch.
+CHECKS = os.environ.get("HQ4_CHECKS", "0") == "1"
+
+
+def expect(t, nbytes: int, what: str, align: int = 4):
+    """Raise unless tensor t is on the current CUDA device, holds at least
+    nbytes from its data pointer on, and is `align`-byte aligned."""
+    if not CHECKS or t is None:
+        return
+    import torch
+    if not t.is_cuda or t.device.index != torch.cuda.current_device():
+        raise RuntimeError(f"{what}: tensor on {t.device}, current device {torch.cuda.current_device()}")
+    have = (t.untyped_storage().nbytes() - t.storage_offset() * t.element_size())
+    if have < nbytes:
+        raise RuntimeError(f"{what}: needs {nbytes} bytes, tensor holds {have}")
+    if t.data_ptr() % align:
+        raise RuntimeError(f"{what}: pointer not {align}-byte aligned")
 
 
 def declared_symbols(header: str = HEADER):

@@ -494,7 +494,8 @@ struct GemvPlan {
     size_t smem;
 };
 
-// Device status word: bit 0 = a bounded wait in a kernel ran out.
+// Device status word: bit 0 = a bounded wait in a kernel ran out, bit 1 = a
+// token id outside the embedding table (the row was written as zeros).
 __device__ int g_hq4_status = 0;
 
 static int sm_count() {
@@ -509,7 +510,7 @@ static int sm_count() {
 }
 
 // Device address of g_hq4_status, looked up once per device.
-static int* status_word() {
+int* status_word() {
     static int* addr[64] = {nullptr};
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;

@@ -26,6 +26,7 @@ int gemv_launch_stage(const uint32_t* w, const uint16_t* scales, const uint16_t*
                       const float* rope_cos, const float* rope_sin, float* q_out, float* k_cache,
                       float* v_cache, cudaStream_t st);
 int check_device_cap();
+int* status_word();
 
 static cudaLaunchAttribute pdl_attr() {
     cudaLaunchAttribute a;
@@ -48,16 +49,20 @@ static int launch_pdl(Kern kern, dim3 grid, dim3 block, size_t smem, cudaStream_
 }
 
 // ---- embedding ---------------------------------------------------------------
+// An id outside [0, vocab) reads nothing: its row is written as zeros and
+// status bit 1 is set (the reference's table indexing raises there).
 __global__ void embed_kernel(const __half* __restrict__ table, const int* __restrict__ ids, int n,
-                             int hidden, float* __restrict__ out) {
+                             int hidden, int vocab, float* __restrict__ out, int* status) {
     pdl_launch_dependents();
     pdl_wait();
     const int t = blockIdx.y;
     if (t >= n) return;
     const int id = ids[t];
-    const __half* row = table + (size_t)id * hidden;
+    const bool ok = id >= 0 && id < vocab;
+    if (!ok && blockIdx.x == 0 && threadIdx.x == 0 && status) atomicOr(status, 2);
+    const __half* row = table + (size_t)(ok ? id : 0) * hidden;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < hidden; i += gridDim.x * blockDim.x)
-        out[(size_t)t * hidden + i] = __half2float(row[i]);
+        out[(size_t)t * hidden + i] = ok ? __half2float(row[i]) : 0.0f;
 }
 
 // ---- attention ---------------------------------------------------------------
@@ -128,23 +133,35 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(
 }
 
 // ---- argmax --------------------------------------------------------------------
-// Largest value, lowest index among equals.  Writes the index to idx_out and,
-// when given, to history[*pos] (the generated-token record).
+// numpy argmax order (hetero/backends.py:106-109 calls z.argmax()): a NaN is
+// above every number and the first NaN wins; otherwise the largest value,
+// lowest index among equals (-inf included, so the result is always in
+// [0, n)).  Writes the index to idx_out and, when given, to history[*pos]
+// (the generated-token record).
 constexpr int kArgmaxThreads = 1024;
+
+__device__ __forceinline__ bool argmax_before(float v, int i, float bv, int bi) {
+    const bool vn = v != v, bn = bv != bv;
+    if (vn || bn) return vn && (!bn || i < bi);
+    return v > bv || (v == bv && i < bi);
+}
 
 __global__ void __launch_bounds__(kArgmaxThreads) argmax_kernel(const float* __restrict__ x, int n,
                                                                 int* __restrict__ idx_out,
                                                                 int* __restrict__ history, int hist_len,
-                                                                const int* __restrict__ pos) {
+                                                                const int* __restrict__ pos,
+                                                                float* __restrict__ val_out) {
     __shared__ float bv[kArgmaxThreads / 32];
     __shared__ int bi[kArgmaxThreads / 32];
     pdl_launch_dependents();
     pdl_wait();
-    float best = -FLT_MAX;
+    // (-inf, INT_MAX) loses to every element, so any thread that saw one
+    // element holds an index in [0, n)
+    float best = -INFINITY;
     int bidx = 0x7fffffff;
     for (int i = threadIdx.x; i < n; i += kArgmaxThreads) {
         const float v = x[i];
-        if (v > best) {  // strided scan: later i has a larger index, keep first
+        if (argmax_before(v, i, best, bidx)) {
             best = v;
             bidx = i;
         }
@@ -153,7 +170,7 @@ __global__ void __launch_bounds__(kArgmaxThreads) argmax_kernel(const float* __r
     for (int o = 16; o > 0; o >>= 1) {
         const float ov = __shfl_xor_sync(0xffffffffu, best, o);
         const int oi = __shfl_xor_sync(0xffffffffu, bidx, o);
-        if (ov > best || (ov == best && oi < bidx)) {
+        if (argmax_before(ov, oi, best, bidx)) {
             best = ov;
             bidx = oi;
         }
@@ -168,11 +185,12 @@ __global__ void __launch_bounds__(kArgmaxThreads) argmax_kernel(const float* __r
         best = bv[0];
         bidx = bi[0];
         for (int j = 1; j < kArgmaxThreads / 32; j++)
-            if (bv[j] > best || (bv[j] == best && bi[j] < bidx)) {
+            if (argmax_before(bv[j], bi[j], best, bidx)) {
                 best = bv[j];
                 bidx = bi[j];
             }
         *idx_out = bidx;
+        if (val_out) *val_out = best;
         if (history) {
             const int at = *pos;
             if (at >= 0 && at < hist_len) history[at] = bidx;
@@ -191,12 +209,14 @@ __global__ void advance_kernel(int* pos, int delta) {
 using namespace hq4;
 
 extern "C" int hq4_embed_f16(const uint16_t* table, const int* ids, int n_tokens, int hidden,
-                             float* out, void* stream) {
+                             int vocab, float* out, void* stream) {
     if (int rc = check_device_cap()) return rc;
-    if (n_tokens <= 0 || hidden <= 0) return HQ4_ERR_SHAPE;
+    if (n_tokens <= 0 || hidden <= 0 || vocab <= 0) return HQ4_ERR_SHAPE;
+    int* status = status_word();
+    if (!status) return HQ4_ERR_LAUNCH;
     return launch_pdl(embed_kernel, dim3(std::min(8, (hidden + 255) / 256), n_tokens), dim3(256), 0,
                       static_cast<cudaStream_t>(stream), reinterpret_cast<const __half*>(table), ids,
-                      n_tokens, hidden, out);
+                      n_tokens, hidden, vocab, out, status);
 }
 
 extern "C" int hq4_attention(const float* q, const float* k_cache, const float* v_cache, float* out,
@@ -219,12 +239,12 @@ extern "C" int hq4_attention(const float* q, const float* k_cache, const float* 
 }
 
 extern "C" int hq4_argmax(const float* x, int n, int* idx_out, int* history, int hist_len,
-                          const int* pos, void* stream) {
+                          const int* pos, float* val_out, void* stream) {
     if (int rc = check_device_cap()) return rc;
     if (n <= 0) return HQ4_ERR_SHAPE;
     if (history && (!pos || hist_len <= 0)) return HQ4_ERR_SHAPE;
     return launch_pdl(argmax_kernel, dim3(1), dim3(kArgmaxThreads), 0, static_cast<cudaStream_t>(stream),
-                      x, n, idx_out, history, hist_len, pos);
+                      x, n, idx_out, history, hist_len, pos, val_out);
 }
 
 extern "C" int hq4_advance_position(int* pos, int delta, void* stream) {

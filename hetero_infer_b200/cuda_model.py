@@ -282,10 +282,12 @@ class Stage:
         ids_np = np.asarray(ids).reshape(-1).astype(np.int32)
         n = ids_np.size
         out = torch.empty((n, self.H), dtype=torch.float32, device=self.device)
+        if ids_np.size and (ids_np.min() < 0 or ids_np.max() >= self.V):
+            raise ValueError(f"token id out of range [0, {self.V})")
         if self.embed_table is not None:
             d_ids = torch.from_numpy(ids_np).to(self.device)
             self._check(self.lib.hq4_embed_f16(self.embed_table.data_ptr(), d_ids.data_ptr(), n, self.H,
-                                               out.data_ptr(), self._stream()), "hq4_embed_f16")
+                                               self.embed_table.shape[0], out.data_ptr(), self._stream()), "hq4_embed_f16")
         else:
             e = self.embed_q
             for i, t in enumerate(ids_np):
@@ -296,11 +298,26 @@ class Stage:
 
     def layer_forward(self, i: int, h: torch.Tensor, cache: DeviceKVCache, L: int, bufs=None):
         """One decoder layer on L tokens, in place on h [L, H]."""
+        from ._lib import expect
         lay, lib, st = self.layers[i], self.lib, self._stream()
         q = bufs["q"] if bufs else torch.empty((L, self.nh * self.hd), dtype=torch.float32, device=self.device)
         a = bufs["a"] if bufs else torch.empty((L, self.nh * self.hd), dtype=torch.float32, device=self.device)
         m = bufs["m"] if bufs else torch.empty((L, self.I), dtype=torch.float32, device=self.device)
         kc, vc = cache.k[i], cache.v[i]
+        f4 = 4
+        expect(h, L * self.H * f4, "h", 16)
+        expect(q, L * self.nh * self.hd * f4, "q", 16)
+        expect(a, L * self.nh * self.hd * f4, "a", 16)
+        expect(m, L * self.I * f4, "m", 16)
+        expect(kc, self.nkv * cache.max_ctx * self.hd * f4, "k_cache")
+        expect(vc, self.nkv * cache.max_ctx * self.hd * f4, "v_cache")
+        expect(cache.pos, 4, "pos")
+        for t, nb, nm in ((lay.qkv.w, lay.qkv.n_out * self.H // 2, "qkv.w"), (lay.o.w, self.H * self.H // 2, "o.w"),
+                          (lay.gate_up.w, 2 * self.I * self.H // 2, "gu.w"), (lay.down.w, self.H * self.I // 2, "down.w"),
+                          (self.rope_cos, cache.max_ctx * self.hd // 2 * f4, "cos")):
+            expect(t, nb, nm, 32 if nm.endswith(".w") else 4)
+        if cache.max_ctx > self.max_ctx:
+            raise RuntimeError("cache larger than the stage's rope table")
         self._check(lib.hq4_qkv_rope(lay.qkv.w.data_ptr(), lay.qkv.s.data_ptr(), lay.qkv.b.data_ptr(),
                                      h.data_ptr(), self.nh, self.nkv, self.hd, self.H, self.gs, L,
                                      lay.in_w.data_ptr(), self.eps, lay.qkv_bias.data_ptr(),
@@ -323,9 +340,12 @@ class Stage:
 
     def head_logits(self, h: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
         """RMSNorm + vocabulary projection of rows h [R, H] -> [R, V]."""
+        from ._lib import expect
         R = h.shape[0]
         if out is None:
             out = torch.empty((R, self.V), dtype=torch.float32, device=self.device)
+        expect(h, R * self.H * 4, "head h", 16)
+        expect(out, R * self.V * 4, "logits")
         lm = self.lm_head
         self._check(self.lib.hq4_gemv_norm(lm.w.data_ptr(), lm.s.data_ptr(), lm.b.data_ptr(), h.data_ptr(),
                                            out.data_ptr(), self.V, self.H, self.gs, R, self.norm_w.data_ptr(),
@@ -426,7 +446,7 @@ class CudaBackend:
             z = logits.reshape(-1).contiguous()
             idx = torch.empty(1, dtype=torch.int32, device=z.device)
             lib = _lib.load()
-            _lib.check(lib.hq4_argmax(z.data_ptr(), z.numel(), idx.data_ptr(), None, 0, None,
+            _lib.check(lib.hq4_argmax(z.data_ptr(), z.numel(), idx.data_ptr(), None, 0, None, None,
                                       torch.cuda.current_stream(z.device).cuda_stream), "hq4_argmax")
             return int(idx.item())
         # temperature / top-p sampling: the reference's own NumPy procedure
@@ -492,11 +512,11 @@ class GreedyDecoder:
     def _argmax(self):
         s = self.stage
         s._check(s.lib.hq4_argmax(self.logits.data_ptr(), s.V, self.tok.data_ptr(), self.history.data_ptr(),
-                                  s.max_ctx, self.cache.pos.data_ptr(), s._stream()), "hq4_argmax")
+                                  s.max_ctx, self.cache.pos.data_ptr(), None, s._stream()), "hq4_argmax")
 
     def _step(self):
         s = self.stage
-        s._check(s.lib.hq4_embed_f16(s.embed_table.data_ptr(), self.tok.data_ptr(), 1, s.H,
+        s._check(s.lib.hq4_embed_f16(s.embed_table.data_ptr(), self.tok.data_ptr(), 1, s.H, s.embed_table.shape[0],
                                      self.h.data_ptr(), s._stream()), "hq4_embed_f16")
         for i in range(len(s.layers)):
             s.layer_forward(i, self.h, self.cache, 1, self.bufs)

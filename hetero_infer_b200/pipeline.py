@@ -1,0 +1,313 @@
+"""Pipelined decode across the GPUs of one box (one process per GPU).
+
+The reference pipelines a model over machines: each node runs a contiguous
+slice of layers, hidden states travel to the next node as fp16 frames over
+TCP, and several requests in flight keep every stage busy
+(hetero/engine.py:68-147, hetero/transport.py:86-225,
+hetero/coordinator.py:294-325).  Here the nodes are GPUs of one NVSwitch box
+and the transport is NCCL over NVLink:
+
+* stage i holds layers [cuts[i], cuts[i+1]) of the plan (planner.py); stage 0
+  also embeds;
+* per tick, one grouped NCCL send/recv moves the fp16 hidden state
+  (hetero/backends.py:100-104 wire format, 7168 B per token for the 7B shape)
+  from every stage to the next -- grouped, so no rank waits on a send whose
+  receiver is still busy with a collective;
+* the vocabulary projection is row-sharded over all stages: the last stage's
+  fp32 hidden state is broadcast, every rank computes V/N logits and their
+  (max, first index), and an 8-byte-per-rank all-gather picks the token with
+  numpy's argmax rule (largest value, lowest index);
+* microbatches are independent requests with their own KV caches.  Rank 0
+  admits, each tick, the next microbatch (round robin) whose previous token is
+  known; stage i works on what rank 0 admitted i ticks earlier.  The schedule
+  is a pure function of (microbatches, steps, stages), so every rank computes
+  it and the send/recv pairs match without any control messages.
+
+The runner is written against a small compute interface so the same schedule
+and communication run on GPUs (NCCL, device stage) and in CPU tests (gloo,
+the NumPy stage oracle).
+"""
+from __future__ import annotations
+
+from typing import Dict, List, Optional, Sequence
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+
+def admission_schedule(n_micro: int, n_steps: int, n_stages: int) -> List[int]:
+    """Microbatch rank 0 admits at each tick (-1: none) for `n_steps` decode
+    steps per microbatch.  A microbatch admitted at tick t has its next token
+    at the end of tick t + n_stages - 1, so it is admissible again at
+    t + n_stages."""
+    ready = [0] * n_micro
+    left = [n_steps] * n_micro
+    out: List[int] = []
+    nxt, t = 0, 0
+    while any(left):
+        pick = -1
+        for j in range(n_micro):
+            m = (nxt + j) % n_micro
+            if left[m] > 0 and ready[m] <= t:
+                pick = m
+                break
+        out.append(pick)
+        if pick >= 0:
+            left[pick] -= 1
+            ready[pick] = t + n_stages
+            nxt = (pick + 1) % n_micro
+        t += 1
+    return out
+
+
+class Comm:
+    """The few torch.distributed operations the pipeline uses."""
+
+    def __init__(self, rank: int, world: int, device: torch.device, group=None):
+        self.rank, self.world, self.device, self.group = rank, world, device, group
+
+    def exchange(self, send: Optional[torch.Tensor], recv: Optional[torch.Tensor]) -> None:
+        """Send to rank+1 and/or receive from rank-1 as one group."""
+        ops = []
+        if send is not None:
+            ops.append(dist.P2POp(dist.isend, send, self.rank + 1, group=self.group))
+        if recv is not None:
+            ops.append(dist.P2POp(dist.irecv, recv, self.rank - 1, group=self.group))
+        if ops:
+            for r in dist.batch_isend_irecv(ops):
+                r.wait()
+
+    def broadcast(self, t: torch.Tensor, src: int) -> None:
+        dist.broadcast(t, src, group=self.group)
+
+    def all_gather(self, t: torch.Tensor) -> torch.Tensor:
+        if dist.get_backend(self.group) == "nccl":
+            out = torch.empty((self.world,) + tuple(t.shape), dtype=t.dtype, device=t.device)
+            dist.all_gather_into_tensor(out, t, group=self.group)
+            return out
+        parts = [torch.empty_like(t) for _ in range(self.world)]
+        dist.all_gather(parts, t, group=self.group)
+        return torch.stack(parts)
+
+
+def pick_token(pairs: torch.Tensor) -> int:
+    """Global argmax from per-shard (value, global index) rows, each the numpy
+    argmax of its contiguous shard: numpy argmax over the whole vocabulary,
+    i.e. the first NaN if any shard holds one, else the largest value, lowest
+    index among equals."""
+    p = pairs.double().cpu().numpy()
+    vals, idx = p[:, 0], p[:, 1]
+    nan = np.isnan(vals)
+    if nan.any():
+        return int(idx[nan].min())
+    return int(idx[vals == vals.max()].min())
+
+
+class PipelineRank:
+    """One rank's side of the pipelined decode.
+
+    compute: object with
+      hidden_dim, wire_dtype (torch.float16: the reference's format),
+      new_cache(), embed_forward(ids, cache) -> h, forward(h, cache) -> h,
+      to_wire(h) -> wire_dtype tensor on the comm device, from_wire(t) -> h,
+      to_comm32(h_last) -> fp32 [H] tensor on the comm device,
+      head(h32) -> (max value, global index) of this rank's vocabulary shard.
+    """
+
+    def __init__(self, comm: Comm, compute, n_micro: int):
+        self.comm, self.c, self.n_micro = comm, compute, n_micro
+        self.caches = [compute.new_cache() for _ in range(n_micro)]
+        self.tokens: List[List[int]] = [[] for _ in range(n_micro)]
+        self.ticks = 0
+
+    @property
+    def first(self) -> bool:
+        return self.comm.rank == 0
+
+    @property
+    def last(self) -> bool:
+        return self.comm.rank == self.comm.world - 1
+
+    def _head(self, h_last) -> int:
+        """Broadcast the last stage's final hidden state, row-sharded head,
+        all-gather of (max, index) -> the token (identical on every rank)."""
+        H = self.c.hidden_dim
+        buf = self.c.to_comm32(h_last) if self.last else torch.empty(H, dtype=torch.float32,
+                                                                        device=self.comm.device)
+        self.comm.broadcast(buf, self.comm.world - 1)
+        val, idx = self.c.head(buf)
+        pair = torch.tensor([val, float(idx)], dtype=torch.float64, device=self.comm.device)
+        return pick_token(self.comm.all_gather(pair))
+
+    def prefill(self, prompts: Sequence[np.ndarray]) -> None:
+        """Each prompt [1, P] through the stages one after another; the first
+        generated token of every microbatch comes from the sharded head."""
+        W, r = self.comm.world, self.comm.rank
+        for m, prompt in enumerate(prompts):
+            P = int(np.asarray(prompt).shape[-1])
+            h = None
+            for s in range(W):   # stage s computes at sub-tick s
+                if r == s:
+                    if self.first:
+                        h = self.c.embed_forward(np.asarray(prompt).reshape(1, P), self.caches[m])
+                    else:
+                        h = self.c.forward(self.c.from_wire(wire_in), self.caches[m])
+                    if not self.last:
+                        self.comm.exchange(self.c.to_wire(h), None)
+                elif r == s + 1:
+                    wire_in = torch.empty((1, P, self.c.hidden_dim), dtype=self.c.wire_dtype,
+                                          device=self.comm.device)
+                    self.comm.exchange(None, wire_in)
+            tok = self._head(h if self.last else None)
+            self.tokens[m].append(tok)
+
+    def decode(self, n_steps: int) -> None:
+        """n_steps more tokens for every microbatch, pipelined."""
+        W, r = self.comm.world, self.comm.rank
+        adm = admission_schedule(self.n_micro, n_steps, W)
+        n_ticks = len(adm) + W - 1
+        H = self.c.hidden_dim
+        out_prev = None       # this rank's wire output of the previous tick
+        for t in range(n_ticks):
+            # this rank works on what rank 0 admitted r ticks ago -- which is
+            # also what rank r-1 worked on (and sends now) one tick ago
+            mine = adm[t - r] if 0 <= t - r < len(adm) else -1
+            recv = None
+            if r > 0 and mine >= 0:
+                recv = torch.empty((1, 1, H), dtype=self.c.wire_dtype, device=self.comm.device)
+            self.comm.exchange(out_prev if (not self.last and out_prev is not None) else None, recv)
+            out_prev = None
+            h = None
+            if mine >= 0:
+                if self.first:
+                    h = self.c.embed_forward(np.array([[self.tokens[mine][-1]]]), self.caches[mine])
+                else:
+                    h = self.c.forward(self.c.from_wire(recv), self.caches[mine])
+                if not self.last:
+                    out_prev = self.c.to_wire(h)
+            # head of the microbatch the last stage finished this tick
+            done = adm[t - (W - 1)] if 0 <= t - (W - 1) < len(adm) else -1
+            if done >= 0:
+                tok = self._head(h if self.last else None)
+                self.tokens[done].append(tok)
+        self.ticks += n_ticks
+
+
+# ---------------------------------------------------------------------------
+# compute adapters
+# ---------------------------------------------------------------------------
+
+class DeviceCompute:
+    """Stage slice on this rank's GPU plus its row shard of the vocabulary
+    projection (libhq4 kernels: the stage forward, the norm-fused head GEMV,
+    argmax with value).
+
+    wire: "float16" is the reference's hand-off (backends.py:100-104; values
+    beyond fp16 range become inf there and here alike); "float32" sends the
+    fp32 hidden state unchanged, so the pipelined model computes exactly what
+    one unsplit stage computes (not a reference format)."""
+
+    def __init__(self, cfg: dict, spec, weights: Dict[str, np.ndarray], head_rows: tuple,
+                 device: torch.device, max_ctx: int = 1024, wire: str = "float16"):
+        from . import _lib, cuda_model
+        if wire not in ("float16", "float32"):
+            raise ValueError(f"wire must be float16 or float32, not {wire!r}")
+        self.wire_dtype = getattr(torch, wire)
+        self.cfg, self.device = cfg, device
+        self.hidden_dim = cfg["hidden_size"]
+        self.stage = cuda_model.Stage(cfg, spec, weights, device=device, max_ctx=max_ctx)
+        lo, hi = head_rows
+        self.lo, self.hi = lo, hi
+        gs = cfg["quantization"]["group_size"]
+        self.gs = gs
+        self.lm_w = cuda_model._dev_array(weights["lm_head.weight"][lo:hi], device=device)
+        self.lm_s = cuda_model._dev_array(weights["lm_head.scales"][lo:hi], torch.float16, device)
+        self.lm_b = cuda_model._dev_array(weights["lm_head.biases"][lo:hi], torch.float16, device)
+        self.norm_w = cuda_model._dev_array(np.asarray(weights["model.norm.weight"], np.float32),
+                                            torch.float32, device)
+        self.logits = torch.empty(hi - lo, dtype=torch.float32, device=device)
+        self.idx = torch.empty(1, dtype=torch.int32, device=device)
+        self.val = torch.empty(1, dtype=torch.float32, device=device)
+        self.lib = _lib.load()
+        self._check = _lib.check
+
+    def new_cache(self):
+        return self.stage.new_caches()
+
+    def embed_forward(self, ids, cache):
+        return self.stage(ids, cache, apply_head=False)
+
+    def forward(self, h, cache):
+        return self.stage(h, cache, apply_head=False)
+
+    def to_wire(self, h):
+        return h.to(self.wire_dtype).contiguous()
+
+    def from_wire(self, t):
+        return t.to(torch.float32)
+
+    def to_comm32(self, h):
+        return h.reshape(-1, self.hidden_dim)[-1].contiguous()
+
+    def head(self, h32):
+        from ._lib import expect
+        expect(h32, self.hidden_dim * 4, "head x", 16)
+        expect(self.logits, (self.hi - self.lo) * 4, "shard logits")
+        expect(self.lm_w, (self.hi - self.lo) * self.hidden_dim // 2, "lm shard w", 32)
+        st = torch.cuda.current_stream(self.device).cuda_stream
+        self._check(self.lib.hq4_gemv_norm(self.lm_w.data_ptr(), self.lm_s.data_ptr(), self.lm_b.data_ptr(),
+                                           h32.data_ptr(), self.logits.data_ptr(), self.hi - self.lo,
+                                           self.hidden_dim, self.gs, 1, self.norm_w.data_ptr(),
+                                           float(self.cfg["rms_norm_eps"]), 0, None, None, st), "head")
+        self._check(self.lib.hq4_argmax(self.logits.data_ptr(), self.hi - self.lo, self.idx.data_ptr(), None, 0,
+                                        None, self.val.data_ptr(), st), "argmax")
+        return float(self.val.item()), self.lo + int(self.idx.item())
+
+
+class OracleCompute:
+    """The same on the CPU with the NumPy stage oracle (test infrastructure:
+    lets the schedule and communication run under gloo without a GPU)."""
+
+    wire_dtype = torch.float16
+
+    def __init__(self, cfg: dict, start: int, end: int, weights: Dict[str, np.ndarray], head_rows: tuple,
+                 embed_rows=None):
+        from oracle import stage as ost
+        self.cfg, self.hidden_dim = cfg, cfg["hidden_size"]
+        self.stage = ost.OracleStage(cfg, weights, start, end, start == 0, False, embed_rows=embed_rows)
+        lo, hi = head_rows
+        self.lo = lo
+        self.norm_w = np.asarray(weights["model.norm.weight"], np.float32)
+        self.lm = ost.OLinear(self.stage.orc, weights["lm_head.weight"][lo:hi], weights["lm_head.scales"][lo:hi],
+                              weights["lm_head.biases"][lo:hi], None, cfg["quantization"]["group_size"])
+        self._ost = ost
+
+    def new_cache(self):
+        return self.stage.new_caches()
+
+    def embed_forward(self, ids, cache):
+        return self.stage(ids, cache, apply_head=False)
+
+    def forward(self, h, cache):
+        return self.stage(h, cache, apply_head=False)
+
+    def to_wire(self, h):
+        return torch.from_numpy(np.ascontiguousarray(np.asarray(h, dtype=np.float16)))
+
+    def from_wire(self, t):
+        return t.numpy().astype(np.float32)
+
+    def to_comm32(self, h):
+        return torch.from_numpy(np.ascontiguousarray(np.asarray(h, np.float32).reshape(-1, self.hidden_dim)[-1]))
+
+    def head(self, h32):
+        x = self._ost.rms_norm(h32.numpy().reshape(1, 1, -1), self.norm_w, self.cfg["rms_norm_eps"])
+        z = self.lm(x).reshape(-1)
+        i = int(z.argmax())
+        return float(z[i]), self.lo + i
+
+
+def head_rows(vocab: int, world: int, rank: int) -> tuple:
+    """Row range of the vocabulary projection on `rank` (contiguous, balanced)."""
+    return (vocab * rank // world, vocab * (rank + 1) // world)

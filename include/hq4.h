@@ -35,9 +35,11 @@ extern "C" {
 int hq4_version(void);
 
 /* Device status word of the current device (synchronising): bit 0 is set
- * when a kernel's bounded wait on its cluster x-image exchange ran out (the
- * kernel then wrote no output).  Non-zero `clear` resets it.  Has no
- * counterpart in the reference, whose CPU kernel cannot stall this way. */
+ * when a kernel's bounded wait (the bulk copy of x into shared memory) ran
+ * out -- the kernel then wrote no output; bit 1 when hq4_embed_f16 met a
+ * token id outside [0, vocab) -- that row was written as zeros.  Non-zero
+ * `clear` resets it.  No counterpart in the reference: its CPU kernel
+ * cannot stall, and its table indexing raises IndexError on a bad id. */
 int hq4_device_status(int clear);
 
 /* out[m][n_out] = x[m][n_in] . W^T with W dequantised on the fly.
@@ -75,9 +77,10 @@ int hq4_dequant(const uint32_t* w, const uint16_t* scales, const uint16_t* biase
  * decode step be replayed as one CUDA graph. */
 
 /* out[t] = fp32(table[ids[t]]) for an fp16 embedding table [vocab][hidden];
- * ids is a device int array of n_tokens. */
+ * ids is a device int array of n_tokens.  An id outside [0, vocab) reads
+ * nothing: its row is zeros and status bit 1 is set (hq4_device_status). */
 int hq4_embed_f16(const uint16_t* table, const int* ids, int n_tokens, int hidden,
-                  float* out, void* stream);
+                  int vocab, float* out, void* stream);
 
 /* GEMV with RMSNorm of x fused into its prologue (cpu_model.py:164-166):
  *   x' = (x * (1/sqrt(mean(x^2) + eps))) * norm_w          (norm_w may be NULL)
@@ -115,11 +118,13 @@ int hq4_attention(const float* q, const float* k_cache, const float* v_cache, fl
                   int n_heads, int n_kv, int head_dim, int max_ctx, const int* pos,
                   int n_tokens, float scale, void* stream);
 
-/* Greedy sampling (hetero/backends.py:106-109): index of the largest of x[0..n),
- * lowest index among equals, written to *idx_out; also to history[*pos] when
- * history is not NULL and 0 <= *pos < hist_len. */
+/* Greedy sampling (hetero/backends.py:106-109): numpy argmax of x[0..n) --
+ * the first NaN if there is one, else the largest value, lowest index among
+ * equals (the result is always in [0, n)) -- written to *idx_out; also to history[*pos] when
+ * history is not NULL and 0 <= *pos < hist_len; the largest value to *val_out
+ * when val_out is not NULL (a row-sharded head reduces (value, index) pairs). */
 int hq4_argmax(const float* x, int n, int* idx_out, int* history, int hist_len, const int* pos,
-               void* stream);
+               float* val_out, void* stream);
 
 /* Fill an fp16 [vocab][hidden] table with the benchmark's counter-based
  * synthetic N(0, std) embedding (seeded; see hetero_infer_b200/synth.py,

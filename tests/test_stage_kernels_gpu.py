@@ -1,0 +1,92 @@
+"""Edge cases of the stage kernels through the C ABI.
+
+argmax follows numpy's z.argmax() (hetero/backends.py:106-109): the first NaN
+wins, else the largest value with the lowest index among equals, and -inf
+rows give index 0 -- the result is always a valid index.  The embedding
+gather reads nothing for an id outside the table: the row is zeros and the
+device status word gets bit 1."""
+import numpy as np
+import pytest
+
+
+@pytest.fixture(scope="module")
+def lib(cuda):
+    from hetero_infer_b200 import _lib
+    return _lib.load()
+
+
+def _argmax(lib, x):
+    import torch
+    d = torch.from_numpy(np.ascontiguousarray(x, np.float32)).cuda()
+    idx = torch.full((1,), -7, dtype=torch.int32, device="cuda")
+    val = torch.empty(1, dtype=torch.float32, device="cuda")
+    rc = lib.hq4_argmax(d.data_ptr(), d.numel(), idx.data_ptr(), None, 0, None, val.data_ptr(),
+                        torch.cuda.current_stream().cuda_stream)
+    assert rc == 0
+    torch.cuda.synchronize()
+    return int(idx.item()), float(val.item())
+
+
+def _cases():
+    rng = np.random.default_rng(3)
+    out = []
+    for n in (1, 31, 1024, 1025, 76032, 152064):
+        out.append(rng.standard_normal(n).astype(np.float32))
+    z = np.full(5000, np.nan, np.float32)
+    out.append(z)                                        # all NaN -> 0
+    z = rng.standard_normal(5000).astype(np.float32)
+    z[[777, 3001]] = np.nan
+    out.append(z)                                        # first NaN
+    z = rng.standard_normal(5000).astype(np.float32)
+    z[4999] = np.nan
+    z[10] = np.inf
+    out.append(z)                                        # NaN beats +inf
+    out.append(np.full(3000, -np.inf, np.float32))       # all -inf -> 0
+    z = np.full(3000, -np.inf, np.float32)
+    z[2500] = -1e30
+    out.append(z)
+    z = np.zeros(70000, np.float32)
+    z[[69999, 40000, 1500]] = 2.0
+    out.append(z)                                        # ties -> lowest
+    out.append(np.round(rng.standard_normal(152064) * 2).astype(np.float32))  # many ties
+    z = np.full(2048, -np.finfo(np.float32).max, np.float32)
+    out.append(z)
+    return out
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("ci", range(len(_cases())))
+def test_argmax_is_numpy_argmax(lib, ci):
+    z = _cases()[ci]
+    i, v = _argmax(lib, z)
+    assert i == int(z.argmax())
+    assert 0 <= i < z.size
+    if np.isnan(z[i]):
+        assert np.isnan(v)
+    else:
+        assert v == z[i]
+
+
+@pytest.mark.gpu
+def test_embed_rejects_out_of_range_ids(lib):
+    import torch
+    vocab, hidden = 1000, 256
+    rng = np.random.default_rng(0)
+    table = torch.from_numpy((rng.standard_normal((vocab, hidden)) * 0.02).astype(np.float16)).cuda()
+    st = torch.cuda.current_stream().cuda_stream
+    lib.hq4_device_status(1)
+    ids = torch.tensor([5, 999, 0], dtype=torch.int32, device="cuda")
+    out = torch.empty((3, hidden), dtype=torch.float32, device="cuda")
+    assert lib.hq4_embed_f16(table.data_ptr(), ids.data_ptr(), 3, hidden, vocab, out.data_ptr(), st) == 0
+    torch.cuda.synchronize()
+    assert torch.equal(out, table[ids.long()].float())
+    assert lib.hq4_device_status(0) == 0
+    ids = torch.tensor([7, vocab, -1, 2 ** 31 - 1, 3], dtype=torch.int32, device="cuda")
+    out = torch.full((5, hidden), 9.0, dtype=torch.float32, device="cuda")
+    assert lib.hq4_embed_f16(table.data_ptr(), ids.data_ptr(), 5, hidden, vocab, out.data_ptr(), st) == 0
+    torch.cuda.synchronize()
+    assert torch.equal(out[0], table[7].float()) and torch.equal(out[4], table[3].float())
+    assert float(out[1:4].abs().sum()) == 0.0
+    assert lib.hq4_device_status(1) & 2
+    assert lib.hq4_device_status(0) == 0
+    assert lib.hq4_embed_f16(table.data_ptr(), ids.data_ptr(), 5, hidden, 0, out.data_ptr(), st) == -1
