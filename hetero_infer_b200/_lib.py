@@ -28,6 +28,8 @@ SIGNATURES = {
     "hq4_gemv_fused": (_I, [_P] * 5 + [_I] * 4 + [_P] * 3),
     "hq4_dequant": (_I, [_P] * 4 + [_I] * 4 + [_P]),
     "hq4_embed_f16": (_I, [_P, _P, _I, _I, _I, _P, _P]),
+    "hq4_gemm_w4a16": (_I, [_P, _P, _P, _P, _I, _P, _I, _I, _I, _I, _P, _P, _P]),
+    "hq4_gemm_plan": (_I, [_I, _I, _I, _I, _P]),
     "hq4_gemv_norm": (_I, [_P] * 5 + [_I] * 4 + [_P, _F, _I, _P, _P, _P]),
     "hq4_qkv_rope": (_I, [_P] * 4 + [_I] * 6 + [_P, _F, _P, _P, _P, _P, _I, _P, _P, _P, _P]),
     "hq4_attention": (_I, [_P] * 4 + [_I] * 4 + [_P, _I, _F, _P]),

@@ -187,6 +187,30 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int max
 }
 // Make this thread's generic-proxy shared-memory writes visible to the async
 // proxy (bulk copies) issued afterwards.
+// Wait for phase `parity` of an mbarrier for at most `limit_ns` of wall
+// time (%globaltimer); false if the limit ran out.  Bounds the wait however
+// long each try_wait suspends.
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+__device__ __forceinline__ bool mbar_wait_ns(uint32_t bar, uint32_t parity, uint64_t limit_ns) {
+    uint64_t t0 = 0;
+    for (uint32_t i = 0;; i++) {
+        uint32_t done;
+        asm volatile(
+            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+            " selp.u32 %0, 1, 0, p;\n}\n"
+            : "=r"(done) : "r"(bar), "r"(parity) : "memory");
+        if (done) return true;
+        if ((i & 63) == 0) {
+            const uint64_t now = globaltimer_ns();
+            if (i == 0) t0 = now;
+            else if (now - t0 > limit_ns) return false;
+        }
+    }
+}
 __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }

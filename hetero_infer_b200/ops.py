@@ -101,3 +101,50 @@ def q4_dequant(w: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor, row0
                          row0, row1, n_in, group_size, _stream_ptr(w.device))
     _lib.check(rc, "hq4_dequant")
     return out
+
+
+def q4_gemm(w: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor, x: torch.Tensor,
+            group_size: int = 64, row_add: Optional[torch.Tensor] = None,
+            residual: Optional[torch.Tensor] = None,
+            out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """W4A16 GEMM on the tcgen05 tensor cores (hq4_gemm_w4a16):
+    ``out[m, n_out] = x[m, n_in] @ dequant(w).T`` with x bf16 or fp32 and an
+    fp32 result, for token counts where the product is a dense contraction."""
+    lib = _lib.load()
+    _need_cuda(w, "w")
+    if w.dtype not in (torch.int32, torch.uint32):
+        raise RuntimeError("w must hold packed uint32 words")
+    _need_cuda(scales, "scales", torch.float16)
+    _need_cuda(biases, "biases", torch.float16)
+    n_out, n_in = w.shape[0], w.shape[1] * 8
+    xf = x.reshape(-1, n_in)
+    _need_cuda(xf, "x")
+    if xf.dtype not in (torch.bfloat16, torch.float32):
+        raise RuntimeError(f"x must be bfloat16 or float32, got {xf.dtype}")
+    m = xf.shape[0]
+    if out is None:
+        out = torch.empty((m, n_out), dtype=torch.float32, device=x.device)
+    _need_cuda(out, "out", torch.float32)
+    ra = 0
+    if row_add is not None:
+        _need_cuda(row_add, "row_add", torch.float32)
+        ra = row_add.data_ptr()
+    rs = 0
+    if residual is not None:
+        _need_cuda(residual, "residual", torch.float32)
+        rs = residual.data_ptr()
+    rc = lib.hq4_gemm_w4a16(w.data_ptr(), scales.data_ptr(), biases.data_ptr(), xf.data_ptr(),
+                            1 if xf.dtype == torch.float32 else 0, out.data_ptr(), n_out, n_in,
+                            group_size, m, ra or None, rs or None, _stream_ptr(x.device))
+    _lib.check(rc, "hq4_gemm_w4a16")
+    return out.reshape(*x.shape[:-1], n_out)
+
+
+def gemm_plan(n_out: int, n_in: int, m: int, x_is_f32: bool = False) -> dict:
+    """The launch plan hq4_gemm_w4a16 uses for a shape (host only)."""
+    import ctypes
+    lib = _lib.load()
+    info = (ctypes.c_int * 8)()
+    _lib.check(lib.hq4_gemm_plan(n_out, n_in, m, 1 if x_is_f32 else 0, info), "hq4_gemm_plan")
+    keys = ("row_tiles", "ksplit", "token_tiles", "tile_tokens", "stages", "smem", "tmem_cols", "threads")
+    return dict(zip(keys, list(info)))

@@ -35,11 +35,12 @@ extern "C" {
 int hq4_version(void);
 
 /* Device status word of the current device (synchronising): bit 0 is set
- * when a kernel's bounded wait (the bulk copy of x into shared memory) ran
- * out -- the kernel then wrote no output; bit 1 when hq4_embed_f16 met a
- * token id outside [0, vocab) -- that row was written as zeros.  Non-zero
- * `clear` resets it.  No counterpart in the reference: its CPU kernel
- * cannot stall, and its table indexing raises IndexError on a bad id. */
+ * when a kernel's bounded wait (a bulk copy or pipeline barrier) ran out --
+ * that kernel's output is not valid; bit 1 when hq4_embed_f16 met a token id
+ * outside [0, vocab) -- that row was written as zeros; bit 2 when
+ * hq4_gemm_w4a16 met an activation outside fp16 range.  Non-zero `clear`
+ * resets it.  No counterpart in the reference: its CPU kernel cannot stall,
+ * its table indexing raises IndexError on a bad id, and it computes in fp32. */
 int hq4_device_status(int clear);
 
 /* out[m][n_out] = x[m][n_in] . W^T with W dequantised on the fly.
@@ -69,6 +70,27 @@ int hq4_gemv_fused(const uint32_t* w, const uint16_t* scales, const uint16_t* bi
  * nthreads)  (kernel/q4gemv.c:359-360).  Bit-exact with the reference. */
 int hq4_dequant(const uint32_t* w, const uint16_t* scales, const uint16_t* biases,
                 float* out, int row0, int row1, int n_in, int gs, void* stream);
+
+/* W4A16 GEMM on the tcgen05 tensor cores for token counts where the product
+ * is a dense contraction (microbatched decode, prefill):
+ *   out[t][n] = sum_k x[t][k] * (q[n][k]*scales[n][g] + biases[n][g])
+ *               (+ row_add[n]) (+ residual[t][n])
+ * Replaces QLinear._gemm (hetero/cpu_model.py:118-136: q4_dequant of 512-row
+ * blocks, kernel/q4gemv.c:311-379, then a BLAS matmul).  Weight layout as
+ * hq4_gemv; x is [m][n_in] bf16 (x_is_f32 = 0) or fp32 (x_is_f32 = 1), 16-byte
+ * aligned; out fp32 [m][n_out].  Weights are rounded once to fp16 and x is
+ * converted to fp16 (exact for bf16 x with |x| < 65520; larger magnitudes set
+ * status bit 2); products and sums are fp32.  gs must be a power of two >= 64
+ * dividing n_in (the reference's AVX2 build has the same gs % 64 rule,
+ * q4gemv.c:234-240), else -1.  Deterministic; allocates nothing. */
+int hq4_gemm_w4a16(const uint32_t* w, const uint16_t* scales, const uint16_t* biases, const void* x,
+                   int x_is_f32, float* out, int n_out, int n_in, int gs, int m,
+                   const float* row_add, const float* residual, void* stream);
+
+/* Launch plan hq4_gemm_w4a16 would use (no launch): info[0..7] = row tiles,
+ * K-split cluster size, token tiles, tokens per tile, pipeline stages, shared
+ * memory bytes, TMEM columns, threads per CTA.  No reference counterpart. */
+int hq4_gemm_plan(int n_out, int n_in, int m, int x_is_f32, int* info);
 
 /* ---- qwen2 stage forward (hetero/cpu_model.py:164-368) ---------------------
  * Hidden states, KV cache and attention are fp32 as in the reference's NumPy

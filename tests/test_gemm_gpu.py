@@ -1,0 +1,149 @@
+"""W4A16 tcgen05 GEMM (hq4_gemm_w4a16) on the GPU.
+
+Two references per case:
+* exact: the product it is defined to compute -- weights rounded once to fp16
+  (fp16(q*s+b)), activations converted to fp16 -- in float64 (torch on the
+  device).  Only fp32 accumulation order separates the two: <= 1e-5.
+* spec: the reference's float path, out = x . (q*s+b)^T in full precision
+  (hetero/cpu_model.py QLinear, kernel/q4gemv.c:113-139 per token).  The bar
+  is the north star's 1e-3 relative L2; fp16 weight rounding costs ~3e-4.
+"""
+import numpy as np
+import pytest
+
+from hetero_infer_b200 import synth
+
+EXACT_TOL = 1e-5
+SPEC_TOL = 1e-3
+
+
+def rel_l2(a, b):
+    import torch
+    a = a.double()
+    b = b.double()
+    return float((a - b).norm() / b.norm().clamp_min(1e-300))
+
+
+def _case(n_out, n_in, m, gs, seed, x_dtype):
+    import torch
+    rng = np.random.default_rng(seed)
+    w, s, b = synth.q4_tensor(rng, n_out, n_in, gs)
+    x = torch.from_numpy(rng.standard_normal((m, n_in), dtype=np.float32)).cuda().to(x_dtype)
+    dw = torch.from_numpy(w.view(np.int32)).cuda()
+    ds = torch.from_numpy(s).cuda()
+    db = torch.from_numpy(b).cuda()
+    return dw, ds, db, x
+
+
+def _dequant64(dw, ds, db, gs):
+    """(q*s+b) in float64 on the device, [n_out, n_in] (exact)."""
+    import torch
+    n_out, wpr = dw.shape
+    wu = dw.to(torch.int64) & 0xFFFFFFFF
+    shifts = torch.arange(8, device=dw.device, dtype=torch.int64) * 4
+    q = ((wu.unsqueeze(-1) >> shifts) & 0xF).reshape(n_out, wpr * 8).double()
+    s = ds.double().repeat_interleave(gs, dim=1)
+    b = db.double().repeat_interleave(gs, dim=1)
+    return q * s + b
+
+
+def _refs(dw, ds, db, x, gs):
+    import torch
+    w64 = _dequant64(dw, ds, db, gs)
+    x64 = x.double()
+    exact = x.float().half().double() @ w64.half().double().T
+    spec = x64 @ w64.T
+    return exact, spec
+
+
+SHAPES = [
+    # n_out, n_in, m, gs, x dtype
+    (128, 64, 1, 64, "bf16"),
+    (256, 512, 7, 64, "bf16"),
+    (384, 1024, 16, 128, "bf16"),
+    (1000, 256, 33, 64, "bf16"),          # ragged row tile
+    (512, 3584, 300, 64, "bf16"),         # two token tiles, K split over a cluster
+    (18944, 3584, 64, 64, "bf16"),        # gate/up, config 3
+    (18944, 3584, 256, 64, "bf16"),       # gate/up, config 3, tensor-bound
+    (3584, 18944, 256, 64, "bf16"),       # down, config 3, K split
+    (3584, 18944, 4, 64, "bf16"),
+    (4608, 3584, 48, 256, "f32"),
+    (3584, 3584, 128, 64, "f32"),
+]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("ci", range(len(SHAPES)))
+def test_gemm_matches_exact_and_reference(cuda, ci):
+    import torch
+    from hetero_infer_b200 import ops
+    n_out, n_in, m, gs, xd = SHAPES[ci]
+    dw, ds, db, x = _case(n_out, n_in, m, gs, seed=100 + ci,
+                          x_dtype=torch.bfloat16 if xd == "bf16" else torch.float32)
+    y = ops.q4_gemm(dw, ds, db, x, gs)
+    torch.cuda.synchronize()
+    exact, spec = _refs(dw, ds, db, x, gs)
+    e1, e2 = rel_l2(y, exact), rel_l2(y, spec)
+    assert e1 <= EXACT_TOL, f"{SHAPES[ci]}: vs fp16-operand product {e1:.2e} (plan {ops.gemm_plan(n_out, n_in, m, xd == 'f32')})"
+    assert e2 <= SPEC_TOL, f"{SHAPES[ci]}: vs reference {e2:.2e}"
+    y2 = ops.q4_gemm(dw, ds, db, x, gs)
+    torch.cuda.synchronize()
+    assert torch.equal(y, y2), "not deterministic"
+
+
+@pytest.mark.gpu
+def test_gemm_row_add_residual_and_reference_oracle(cuda, oracle):
+    """Fused bias + residual in the store; and the spec reference taken from
+    the C oracle of q4gemv.c's float path itself (per token)."""
+    import torch
+    from hetero_infer_b200 import ops
+    n_out, n_in, m, gs = 640, 1536, 24, 64
+    dw, ds, db, x = _case(n_out, n_in, m, gs, seed=7, x_dtype=torch.bfloat16)
+    ra = torch.randn(n_out, device="cuda")
+    res = torch.randn(m, n_out, device="cuda")
+    y = ops.q4_gemm(dw, ds, db, x, gs, row_add=ra, residual=res)
+    exact, _ = _refs(dw, ds, db, x, gs)
+    assert rel_l2(y, exact + ra.double() + res.double()) <= EXACT_TOL
+    w = dw.cpu().numpy().view(np.uint32)
+    s = ds.cpu().numpy()
+    b = db.cpu().numpy()
+    xs = x.float().cpu().numpy()
+    ref = oracle.gemv_f32(w, s, b, xs, gs)
+    got = (y - ra - res).cpu().numpy()
+    assert float(np.linalg.norm(got - ref) / np.linalg.norm(ref)) <= SPEC_TOL
+
+
+@pytest.mark.gpu
+def test_gemm_error_codes(cuda):
+    import torch
+    from hetero_infer_b200 import _lib
+    lib = _lib.load()
+    dw, ds, db, x = _case(256, 512, 8, 64, seed=1, x_dtype=torch.bfloat16)
+    out = torch.empty(8, 256, device="cuda")
+    st = torch.cuda.current_stream().cuda_stream
+    call = lambda xp, gs, n_in=512: lib.hq4_gemm_w4a16(dw.data_ptr(), ds.data_ptr(), db.data_ptr(), xp, 0,
+                                                       out.data_ptr(), 256, n_in, gs, 8, None, None, st)
+    assert call(x.data_ptr(), 32) == -1          # gs below 64 (q4gemv.c:234-240 AVX2 rule)
+    assert call(x.data_ptr(), 96) == -1          # not a power of two
+    assert call(x.data_ptr(), 64, n_in=500) == -1
+    assert call(x.data_ptr() + 2, 64) == -2      # x not 16-byte aligned
+    assert call(x.data_ptr(), 64) == 0
+    torch.cuda.synchronize()
+    assert lib.hq4_device_status(0) & 5 == 0
+
+
+@pytest.mark.gpu
+def test_gemm_range_flag(cuda):
+    """bf16 activations beyond fp16 range set status bit 2 (no silent inf)."""
+    import torch
+    from hetero_infer_b200 import _lib, ops
+    lib = _lib.load()
+    dw, ds, db, x = _case(256, 512, 8, 64, seed=2, x_dtype=torch.bfloat16)
+    lib.hq4_device_status(1)
+    ops.q4_gemm(dw, ds, db, x, 64)
+    torch.cuda.synchronize()
+    assert lib.hq4_device_status(0) & 4 == 0
+    x[3, 100] = 1e6
+    ops.q4_gemm(dw, ds, db, x, 64)
+    torch.cuda.synchronize()
+    assert lib.hq4_device_status(1) & 4
