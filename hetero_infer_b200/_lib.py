@@ -15,6 +15,7 @@ from . import build as _build
 
 _P = ctypes.c_void_p
 _I = ctypes.c_int
+_LL = ctypes.c_longlong
 _Z = ctypes.c_size_t
 _F = ctypes.c_float
 
@@ -28,7 +29,8 @@ SIGNATURES = {
     "hq4_gemv_fused": (_I, [_P] * 5 + [_I] * 4 + [_P] * 3),
     "hq4_dequant": (_I, [_P] * 4 + [_I] * 4 + [_P]),
     "hq4_embed_f16": (_I, [_P, _P, _I, _I, _I, _P, _P]),
-    "hq4_gemm_w4a16": (_I, [_P, _P, _P, _P, _I, _P, _I, _I, _I, _I, _P, _P, _P]),
+    "hq4_gemm_w4a16": (_I, [_P, _P, _P, _P, _I, _P, _I, _I, _I, _I, _P, _P, _P, _LL, _P]),
+    "hq4_gemm_workspace_bytes": (_LL, [_I, _I, _I]),
     "hq4_gemm_plan": (_I, [_I, _I, _I, _I, _P]),
     "hq4_gemv_norm": (_I, [_P] * 5 + [_I] * 4 + [_P, _F, _I, _P, _P, _P]),
     "hq4_qkv_rope": (_I, [_P] * 4 + [_I] * 6 + [_P, _F, _P, _P, _P, _P, _I, _P, _P, _P, _P]),
@@ -70,7 +72,7 @@ def expect(t, nbytes: int, what: str, align: int = 4):
 def declared_symbols(header: str = HEADER):
     """Function names declared in include/hq4.h."""
     text = open(header).read()
-    return re.findall(r"^\s*(?:int|size_t|void)\s+(hq4_\w+)\s*\(", text, flags=re.M)
+    return re.findall(r"^\s*(?:int|size_t|void|long long)\s+(hq4_\w+)\s*\(", text, flags=re.M)
 
 
 def load(path: str = None) -> ctypes.CDLL:

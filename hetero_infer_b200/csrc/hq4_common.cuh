@@ -43,6 +43,28 @@ __device__ __forceinline__ uint32_t ldg_u16(const uint16_t* p) {
     asm volatile("ld.global.nc.L1::evict_last.u16 %0, [%1];" : "=h"(v) : "l"(p));
     return v;
 }
+// 8-byte read-only load (4 fp16 scales or biases), kept in L1 for the
+// neighbouring rows' threads.
+__device__ __forceinline__ uint2 ldg_u32x2(const uint16_t* p) {
+    uint2 v;
+    asm volatile("ld.global.nc.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
+    return v;
+}
+// 16-byte streaming load straight into four caller registers (a prefetch
+// target must be the asm output itself: any select or copy of the result
+// would wait for the load where it is issued).
+__device__ __forceinline__ void ldg128_into(const uint32_t* p, uint32_t& a, uint32_t& b, uint32_t& c, uint32_t& d) {
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(a), "=r"(b), "=r"(c), "=r"(d) : "l"(p));
+}
+// Four consecutive fp16 values (8-byte aligned) into four 16-bit registers.
+__device__ __forceinline__ void ldg_u16x4_into(const uint16_t* p, unsigned short& a, unsigned short& b,
+                                               unsigned short& c, unsigned short& d) {
+    asm volatile("ld.global.nc.v4.u16 {%0,%1,%2,%3}, [%4];" : "=h"(a), "=h"(b), "=h"(c), "=h"(d) : "l"(p));
+}
+__device__ __forceinline__ void ldg_u16_into(const uint16_t* p, unsigned short& a) {
+    asm volatile("ld.global.nc.u16 %0, [%1];" : "=h"(a) : "l"(p));
+}
 // Coherent (L1-bypassing) load for values written by other CTAs this launch.
 __device__ __forceinline__ float ldcg_f32(const float* p) {
     float v;
@@ -196,19 +218,17 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
     return t;
 }
 __device__ __forceinline__ bool mbar_wait_ns(uint32_t bar, uint32_t parity, uint64_t limit_ns) {
-    uint64_t t0 = 0;
-    for (uint32_t i = 0;; i++) {
+    // each try_wait may suspend the thread in hardware (up to ~1 ms) until the
+    // phase completes, so a waiting warp does not take issue slots
+    const uint64_t t0 = globaltimer_ns();
+    for (;;) {
         uint32_t done;
         asm volatile(
-            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
             " selp.u32 %0, 1, 0, p;\n}\n"
-            : "=r"(done) : "r"(bar), "r"(parity) : "memory");
+            : "=r"(done) : "r"(bar), "r"(parity), "r"(1000000u) : "memory");
         if (done) return true;
-        if ((i & 63) == 0) {
-            const uint64_t now = globaltimer_ns();
-            if (i == 0) t0 = now;
-            else if (now - t0 > limit_ns) return false;
-        }
+        if (globaltimer_ns() - t0 > limit_ns) return false;
     }
 }
 __device__ __forceinline__ void fence_proxy_async_smem() {

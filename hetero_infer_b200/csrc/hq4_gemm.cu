@@ -5,21 +5,28 @@
 // QLinear._gemm (hetero/cpu_model.py:118-136) as fp32 dequantisation of
 // 512-row blocks (kernel/q4gemv.c:311-379) followed by a BLAS matmul.
 //
-// One CTA owns 128 weight rows (the MMA's M) x up to 256 tokens (its N) and a
-// contiguous range of 64-wide k-blocks:
+// Two launches per call:
 //
-//   warps 0-3   dequantise: thread = weight row; the row's 32 packed bytes of
-//               a k-block become 64 fp16 values (q as fp16 through the 0x6400
-//               exponent trick, then one fma with the group's scale and bias:
-//               a single rounding of q*s+b), written K-major with the 128-byte
-//               swizzle; after the mainloop the same warps read the fp32
-//               accumulator out of TMEM (warp w owns lanes 32w..32w+31);
-//   warps 4-11  convert the activation tile (bf16 or fp32) to fp16 in the
-//               same layout;
-//   warp 12     allocates TMEM and, from one thread, issues
-//               tcgen05.mma.cta_group::1.kind::f16 (K=16 per instruction) on
-//               each stage once both operands are in, releasing the stage
-//               through tcgen05.commit.
+//  1. xprep: the activations (bf16 or fp32) become fp16 in a caller-owned
+//     workspace laid out as the exact shared-memory image of the B operand --
+//     per (token tile, 64-wide k-block) one contiguous [T][64] fp16 block,
+//     K-major with the 128-byte swizzle.  A B stage is then one bulk copy.
+//  2. the GEMM.  One CTA owns 128 weight rows (the MMA's M) x T <= 256 tokens
+//     (its N) x a contiguous range of k-blocks:
+//       warps 0-7  dequantise: two threads per weight row, each turning 16
+//                  packed bytes of a k-block into 32 fp16 values (q as fp16
+//                  through the 0x6400 exponent trick, then one fma with the
+//                  group's scale and bias: a single rounding of q*s+b),
+//                  written K-major with the 128-byte swizzle; packed words are
+//                  prefetched in registers 4 k-blocks at a time, kSbPre
+//                  such groups ahead.  After the
+//                  mainloop the same warps read the fp32 accumulator out of
+//                  TMEM (warp w owns lanes 32(w%4)..+31).
+//       warp 8     one thread streams the workspace blocks into the B stages
+//                  (cp.async.bulk, completing on the stage's mbarrier).
+//       warp 9     allocates TMEM and, from one thread, issues
+//                  tcgen05.mma.cta_group::1.kind::f16 (K=16 per instruction)
+//                  once a stage is full, releasing it through tcgen05.commit.
 //
 // Inside a 64-wide k-block the k order is permuted identically for weights
 // and activations (word j of a row holds k = 8j..8j+7; its values are stored
@@ -30,14 +37,12 @@
 // are few row tiles (the 3584-row down projection has 28): every CTA of the
 // cluster stores its fp32 partial tile in its own shared memory, and after a
 // cluster barrier CTA j sums token slice j over the cluster ranks in rank
-// order (distributed shared memory loads).  Deterministic, no workspace, no
-// atomics.
+// order (distributed shared memory loads).  Deterministic, no atomics.
 //
 // Precision: weights are rounded once to fp16 (relative error <= 2^-11),
-// activations are converted to fp16 exactly for bf16 input in fp16 range
-// (|x| < 65520; larger magnitudes set status bit 2), products and sums are
-// fp32.  Relative L2 error vs the reference's fp32 path is ~3e-4 for fp16
-// weight rounding alone (acceptance bar 1e-3).
+// activations are converted to fp16 (exact for bf16 x with |x| < 65520;
+// larger magnitudes set status bit 2), products and sums are fp32.  Relative
+// L2 error vs the reference's fp32 path is ~3e-4 (acceptance bar 1e-3).
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
@@ -52,22 +57,22 @@ int check_device_cap();
 int* status_word();
 
 constexpr int kGemmRows = 128;                          // MMA M
-constexpr int kAWarps = 4;                              // dequant + epilogue
-constexpr int kXWarps = 8;                              // activation conversion
-constexpr int kMmaWarp = kAWarps + kXWarps;             // warp 12
-constexpr int kGemmThreads = (kAWarps + kXWarps + 1) * 32;
+constexpr int kAWarps = 8;                              // dequant + epilogue
+constexpr int kLoadWarp = kAWarps;                      // warp 8: B-stage bulk copies
+constexpr int kMmaWarp = kAWarps + 1;                   // warp 9: TMEM + MMA issue
+constexpr int kGemmThreads = (kAWarps + 2) * 32;
 constexpr int kAStageBytes = kGemmRows * 128;           // 128 rows x 64 fp16
-constexpr int kWPre = 8;                                // packed k-blocks in flight per row
-constexpr int kXPre = 2;                                // activation k-blocks in flight
-constexpr uint64_t kGemmWaitNs = 1000000000ull;  // 1 s: a correct kernel never waits this long
-constexpr int kMaxTileBf16 = 256, kMaxTileF32 = 128;
+constexpr int kSbPre = 3;                               // super-blocks (4 k-blocks) in flight per thread
+constexpr uint64_t kGemmWaitNs = 1000000000ull;         // 1 s: a correct kernel never waits this long
+constexpr int kMaxTile = 256;
 constexpr int kGemmSmemMax = 220 * 1024;
+constexpr int kPrepThreads = 256;
 
 struct GemmParams {
     const uint32_t* w;
     const uint16_t* sc;
     const uint16_t* bi;
-    const void* x;
+    const unsigned char* xw;   // prepared activations (workspace)
     float* out;
     const float* row_add;
     const float* residual;
@@ -154,62 +159,77 @@ __device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cas
 __device__ __forceinline__ __half2 bits_h2(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
 
 // 8 nibbles of w -> fp16 q*s+b in the order n0,n4,n1,n5,n2,n6,n3,n7.
+// A nibble in bits 0-3 of a 16-bit half OR-ed into 0x6400 (1024.0) reads as
+// 1024 + q; in bits 4-7 OR-ed into 0x5400 (64.0, whose mantissa LSB is 1/16)
+// as 64 + q.  Subtracting the magic is exact, and one fma then rounds q*s+b
+// once.  One shift per word (for nibbles 2, 3, 6, 7).
 __device__ __forceinline__ uint4 dequant_word(uint32_t w, __half2 s2, __half2 b2) {
-    const __half2 k1024 = bits_h2(0x64006400u);
-    uint32_t o[4];
-#pragma unroll
-    for (int j = 0; j < 4; j++) {
-        const uint32_t p = lop3_and_or(w >> (4 * j), 0x000F000Fu, 0x64006400u);
-        o[j] = h2_bits(__hfma2(__hsub2(bits_h2(p), k1024), s2, b2));
-    }
-    return make_uint4(o[0], o[1], o[2], o[3]);
+    const __half2 k1024 = bits_h2(0x64006400u), k64 = bits_h2(0x54005400u);
+    const uint32_t w8 = w >> 8;
+    const uint32_t p0 = lop3_and_or(w, 0x000F000Fu, 0x64006400u);   // n0, n4
+    const uint32_t p1 = lop3_and_or(w, 0x00F000F0u, 0x54005400u);   // n1, n5
+    const uint32_t p2 = lop3_and_or(w8, 0x000F000Fu, 0x64006400u);  // n2, n6
+    const uint32_t p3 = lop3_and_or(w8, 0x00F000F0u, 0x54005400u);  // n3, n7
+    uint4 o;
+    o.x = h2_bits(__hfma2(__hsub2(bits_h2(p0), k1024), s2, b2));
+    o.y = h2_bits(__hfma2(__hsub2(bits_h2(p1), k64), s2, b2));
+    o.z = h2_bits(__hfma2(__hsub2(bits_h2(p2), k1024), s2, b2));
+    o.w = h2_bits(__hfma2(__hsub2(bits_h2(p3), k64), s2, b2));
+    return o;
 }
 
-// 8 fp32 activations x0..x7 -> fp16 in the order x0,x4,x1,x5,x2,x6,x3,x7;
-// amax tracks the largest magnitude seen (range check).
-__device__ __forceinline__ uint4 pack_x8(const float (&f)[8], float& amax) {
-    uint32_t o[4];
-#pragma unroll
-    for (int j = 0; j < 4; j++) {
-        amax = fmaxf(amax, fmaxf(fabsf(f[j]), fabsf(f[j + 4])));
-        o[j] = h2_bits(__floats2half2_rn(f[j], f[j + 4]));  // low half = f[j]
-    }
-    return make_uint4(o[0], o[1], o[2], o[3]);
-}
-
+// ---- activation preparation ---------------------------------------------------
+// One thread per (token, 8-value word): x[t][8j..8j+7] -> fp16 in the order
+// x0,x4,x1,x5,x2,x6,x3,x7, stored in block (t / T, j / 8) of the workspace at
+// row t % T, chunk j % 8 (128-byte swizzle).  Tokens past m are zeros.
 template <bool XF32>
-struct XChunk {
-    uint32_t v[XF32 ? 8 : 4];
-};
-
-template <bool XF32>
-__device__ __forceinline__ void load_x_chunk(const void* x, size_t elem, XChunk<XF32>& c) {
-    if constexpr (XF32) {
-        const uint4* p = reinterpret_cast<const uint4*>(reinterpret_cast<const float*>(x) + elem);
-        const uint4 a = __ldg(p), b = __ldg(p + 1);
-        c.v[0] = a.x; c.v[1] = a.y; c.v[2] = a.z; c.v[3] = a.w;
-        c.v[4] = b.x; c.v[5] = b.y; c.v[6] = b.z; c.v[7] = b.w;
-    } else {
-        const uint4 a = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(x) + elem));
-        c.v[0] = a.x; c.v[1] = a.y; c.v[2] = a.z; c.v[3] = a.w;
-    }
-}
-
-template <bool XF32>
-__device__ __forceinline__ void chunk_floats(const XChunk<XF32>& c, float (&f)[8]) {
-    if constexpr (XF32) {
+__global__ void __launch_bounds__(kPrepThreads) gemm_xprep_kernel(const void* __restrict__ x,
+                                                                unsigned char* __restrict__ ws, int m, int m_pad,
+                                                                int n_in, int t_tile, int* status) {
+    pdl_launch_dependents();
+    pdl_wait();  // x comes from the previous kernel; the workspace may still be read by the previous GEMM
+    const int wpr = n_in >> 3, nkb = n_in >> 6;
+    const long long total = (long long)m_pad * wpr;
+    float amax = 0.0f;
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (long long)gridDim.x * blockDim.x) {
+        const int t = (int)(i / wpr), j = (int)(i - (long long)t * wpr);
+        float f[8];
+        if (t < m) {
+            if constexpr (XF32) {
+                const float4* p = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(x) +
+                                                                  (size_t)t * n_in + (size_t)j * 8);
+                const float4 a = __ldg(p), b = __ldg(p + 1);
+                f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w;
+                f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+            } else {
+                const uint4 a = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(x) +
+                                                                     (size_t)t * n_in + (size_t)j * 8));
+                const uint32_t v[4] = {a.x, a.y, a.z, a.w};
 #pragma unroll
-        for (int j = 0; j < 8; j++) f[j] = __uint_as_float(c.v[j]);
-    } else {
+                for (int u = 0; u < 4; u++) {  // bf16 pair -> two fp32 (exact)
+                    f[2 * u] = __uint_as_float(v[u] << 16);
+                    f[2 * u + 1] = __uint_as_float(v[u] & 0xFFFF0000u);
+                }
+            }
+        } else {
 #pragma unroll
-        for (int j = 0; j < 4; j++) {  // bf16 pair -> two fp32 (exact)
-            f[2 * j] = __uint_as_float(c.v[j] << 16);
-            f[2 * j + 1] = __uint_as_float(c.v[j] & 0xFFFF0000u);
+            for (int u = 0; u < 8; u++) f[u] = 0.0f;
         }
+        uint32_t o[4];
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            amax = fmaxf(amax, fmaxf(fabsf(f[u]), fabsf(f[u + 4])));
+            o[u] = h2_bits(__floats2half2_rn(f[u], f[u + 4]));  // low half = f[u]
+        }
+        const int tt = t / t_tile, tin = t - tt * t_tile, kb = j >> 3, c = j & 7;
+        const size_t blk = ((size_t)tt * nkb + kb) * (size_t)(t_tile * 128);
+        *reinterpret_cast<uint4*>(ws + blk + sw128_off(tin, c)) = make_uint4(o[0], o[1], o[2], o[3]);
     }
+    if (amax >= 65520.0f && status) atomicOr(status, 4);
 }
 
-template <bool XF32>
+// ---- the GEMM -------------------------------------------------------------------------
 __global__ void __launch_bounds__(kGemmThreads, 1) gemm_w4a16_kernel(const GemmParams p) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
@@ -228,14 +248,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_w4a16_kernel(const GemmP
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int row0 = blockIdx.x * kGemmRows;
     const int kr = blockIdx.y;  // K-split rank (= cluster rank: the cluster spans grid y)
-    const int tok0 = blockIdx.z * T;
+    const int tt = blockIdx.z, tok0 = tt * T;
     const int mt = min(T, p.m - tok0);
     const int kb0 = (int)((long long)kr * p.nkb / p.ks), kb1 = (int)((long long)(kr + 1) * p.nkb / p.ks);
     const int nk = kb1 - kb0;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; s++) {
-            mbar_init(full_bar(s), kAWarps + kXWarps);
+            mbar_init(full_bar(s), kAWarps + 1);  // one arrive per dequant warp + the copy's expect_tx
             mbar_init(empty_bar(s), 1);
         }
         mbar_init(accum_bar, 1);
@@ -252,108 +272,102 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_w4a16_kernel(const GemmP
 
     bool fail = false;
     if (warp < kAWarps) {
-        // ---- dequantise weights: thread = row ------------------------------------
-        const int r = warp * 32 + lane;
+        // ---- dequantise weights -------------------------------------------------------------
+        // Every dequant thread takes part in every k-block, in order (each
+        // waits for consecutive completions of each stage barrier, so none can
+        // be satisfied by an older phase of the same parity).  Thread (r, h):
+        // weight row r, words 4h..4h+3 of each k-block; warps 0-3 are h = 0,
+        // warps 4-7 h = 1.  Packed words are fetched a super-block (4
+        // k-blocks) at a time, so the two threads of a row request its 128
+        // contiguous bytes together -- one burst per row, as DRAM wants.
+        const int h = warp >> 2;
+        const int r = (warp & 3) * 32 + lane;
         const int grow = row0 + r;
         const bool rok = grow < p.n_out;
         const size_t wpr = (size_t)(p.n_in >> 3);
-        const uint32_t* wrow = p.w + (size_t)(rok ? grow : 0) * wpr;
+        const uint32_t* wrow = p.w + (size_t)(rok ? grow : 0) * wpr + 4 * h;
         const uint16_t* srow = p.sc + (size_t)(rok ? grow : 0) * p.n_sg;
         const uint16_t* brow = p.bi + (size_t)(rok ? grow : 0) * p.n_sg;
-        uint32_t q[kWPre][8];
-        uint32_t sb[kWPre];
-        auto fetch = [&](int i, uint32_t (&qq)[8], uint32_t& sbv) {
-            if (i < nk && rok) {
-                const int kb = kb0 + i;
-                ldg256_stream(wrow + (size_t)kb * 8, qq);
-                const int g = kb >> p.gs_shift;
-                sbv = (uint32_t)ldg_u16(srow + g) | ((uint32_t)ldg_u16(brow + g) << 16);
+        // gs = 64 with 8-byte aligned scale rows: 4 scales (biases) in one load
+        const bool vec_sb = p.gs_shift == 0 && (p.n_sg & 3) == 0 && (kb0 & 3) == 0 &&
+                            (((uintptr_t)p.sc | (uintptr_t)p.bi) & 7) == 0;
+        const int nsb = (nk + 3) >> 2;  // super-blocks in this CTA's K range
+        uint32_t q[kSbPre][16];
+        unsigned short sv[kSbPre][4], bv[kSbPre][4];
+        // Loads go straight into the ring registers, unconditionally: past
+        // the end of the range (or for a row past n_out) the address is
+        // clamped to valid data that is then not used.
+        auto fetch = [&](int sb, uint32_t (&qq)[16], unsigned short (&ss)[4], unsigned short (&bb)[4]) {
+            const int kbs = kb0 + 4 * min(sb, nsb - 1);  // first k-block of the super-block
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const int kb = min(kbs + u, kb1 - 1);
+                ldg128_into(wrow + (size_t)kb * 8, qq[4 * u], qq[4 * u + 1], qq[4 * u + 2], qq[4 * u + 3]);
+            }
+            if (vec_sb && kbs + 3 < kb1) {
+                ldg_u16x4_into(srow + kbs, ss[0], ss[1], ss[2], ss[3]);
+                ldg_u16x4_into(brow + kbs, bb[0], bb[1], bb[2], bb[3]);
             } else {
 #pragma unroll
-                for (int j = 0; j < 8; j++) qq[j] = 0;
-                sbv = 0;
-            }
-        };
-#pragma unroll
-        for (int d = 0; d < kWPre; d++) fetch(d, q[d], sb[d]);
-        for (int ib = 0; ib < nk && !fail; ib += kWPre) {
-#pragma unroll
-            for (int d = 0; d < kWPre; d++) {
-                const int i = ib + d;
-                if (i < nk && !fail) {
-                    const int s = i % S;
-                    if (i >= S && !mbar_wait_ns(empty_bar(s), (uint32_t)((i / S) - 1) & 1u, kGemmWaitNs)) {
-                        fail = true;
-                    } else {
-                        const __half2 s2 = __half2half2(__ushort_as_half((unsigned short)(sb[d] & 0xFFFFu)));
-                        const __half2 b2 = __half2half2(__ushort_as_half((unsigned short)(sb[d] >> 16)));
-                        unsigned char* dst = sm + (a_base - base) + (size_t)s * kAStageBytes;
-#pragma unroll
-                        for (int c = 0; c < 8; c++) {
-                            const uint4 v = rok ? dequant_word(q[d][c], s2, b2) : make_uint4(0, 0, 0, 0);
-                            *reinterpret_cast<uint4*>(dst + sw128_off(r, c)) = v;
-                        }
-                        fence_proxy_async_smem();
-                        __syncwarp();
-                        if (lane == 0) mbar_arrive(full_bar(s));
-                        fetch(i + kWPre, q[d], sb[d]);
-                    }
-                }
-            }
-        }
-    } else if (warp < kMmaWarp) {
-        // ---- activations -> fp16 B tile ----------------------------------------------
-        pdl_wait();
-        const int xi = threadIdx.x - kAWarps * 32;        // 0..255
-        constexpr int kXThreads = kXWarps * 32;
-        const int nchunks = T * 8;                        // (token, word) pairs per k-block
-        constexpr int kMaxC = (XF32 ? kMaxTileF32 : kMaxTileBf16) * 8 / kXThreads;
-        XChunk<XF32> xb[kXPre][kMaxC];
-        float amax = 0.0f;
-        auto fetch = [&](int i, XChunk<XF32> (&dst)[kMaxC]) {
-#pragma unroll
-            for (int j = 0; j < kMaxC; j++) {
-                const int ch = xi + j * kXThreads;
-                const int t = ch >> 3, c = ch & 7;
-                if (i < nk && ch < nchunks && t < mt) {
-                    const size_t elem = (size_t)(tok0 + t) * p.n_in + (size_t)(kb0 + i) * 64 + c * 8;
-                    load_x_chunk<XF32>(p.x, elem, dst[j]);
-                } else {
-#pragma unroll
-                    for (int u = 0; u < (XF32 ? 8 : 4); u++) dst[j].v[u] = 0;
+                for (int u = 0; u < 4; u++) {
+                    const int g = min(kbs + u, kb1 - 1) >> p.gs_shift;
+                    ldg_u16_into(srow + g, ss[u]);
+                    ldg_u16_into(brow + g, bb[u]);
                 }
             }
         };
 #pragma unroll
-        for (int d = 0; d < kXPre; d++) fetch(d, xb[d]);
-        for (int ib = 0; ib < nk && !fail; ib += kXPre) {
+        for (int d = 0; d < kSbPre; d++) fetch(d, q[d], sv[d], bv[d]);
+        for (int sbb = 0; sbb < nsb && !fail; sbb += kSbPre) {
 #pragma unroll
-            for (int d = 0; d < kXPre; d++) {
-                const int i = ib + d;
-                if (i < nk && !fail) {
-                    const int s = i % S;
-                    if (i >= S && !mbar_wait_ns(empty_bar(s), (uint32_t)((i / S) - 1) & 1u, kGemmWaitNs)) {
-                        fail = true;
-                    } else {
-                        unsigned char* dst = sm + (b_base - base) + (size_t)s * b_stage;
+            for (int d = 0; d < kSbPre; d++) {
+                const int sb = sbb + d;
+                if (sb < nsb && !fail) {
 #pragma unroll
-                        for (int j = 0; j < kMaxC; j++) {
-                            const int ch = xi + j * kXThreads;
-                            if (ch < nchunks) {
-                                float f[8];
-                                chunk_floats<XF32>(xb[d][j], f);
-                                *reinterpret_cast<uint4*>(dst + sw128_off(ch >> 3, ch & 7)) = pack_x8(f, amax);
+                    for (int u = 0; u < 4; u++) {
+                        const int i = 4 * sb + u;  // local k-block
+                        if (i < nk && !fail) {
+                            const int s = i % S;
+                            if (i >= S &&
+                                !mbar_wait_ns(empty_bar(s), (uint32_t)((i / S) - 1) & 1u, kGemmWaitNs)) {
+                                fail = true;
+                            } else {
+                                const __half2 s2 = __half2half2(__ushort_as_half(sv[d][u]));
+                                const __half2 b2 = __half2half2(__ushort_as_half(bv[d][u]));
+                                unsigned char* dst = sm + (a_base - base) + (size_t)s * kAStageBytes;
+#pragma unroll
+                                for (int c = 0; c < 4; c++) {
+                                    const uint4 v = rok ? dequant_word(q[d][4 * u + c], s2, b2)
+                                                        : make_uint4(0, 0, 0, 0);
+                                    *reinterpret_cast<uint4*>(dst + sw128_off(r, 4 * h + c)) = v;
+                                }
+                                fence_proxy_async_smem();
+                                __syncwarp();
+                                if (lane == 0) mbar_arrive(full_bar(s));
                             }
                         }
-                        fence_proxy_async_smem();
-                        __syncwarp();
-                        if (lane == 0) mbar_arrive(full_bar(s));
-                        fetch(i + kXPre, xb[d]);
                     }
+                    fetch(sb + kSbPre, q[d], sv[d], bv[d]);
                 }
             }
         }
-        if (amax >= 65520.0f && p.status) atomicOr(p.status, 4);
+    } else if (warp == kLoadWarp) {
+        // ---- B stages: one bulk copy of a prepared block each ---------------------------
+        if (lane == 0) {
+            pdl_wait();  // the workspace is written by the preparation kernel
+            const uint64_t pol = l2_policy_evict_last();
+            const unsigned char* src = p.xw + ((size_t)tt * p.nkb + kb0) * (size_t)b_stage;
+            for (int i = 0; i < nk; i++) {
+                const int s = i % S;
+                if (i >= S && !mbar_wait_ns(empty_bar(s), (uint32_t)((i / S) - 1) & 1u, kGemmWaitNs)) {
+                    fail = true;
+                    break;
+                }
+                mbar_arrive_expect_tx(full_bar(s), (uint32_t)b_stage);
+                bulk_load_g2s(b_base + (uint32_t)(s * b_stage), src + (size_t)i * b_stage, (uint32_t)b_stage,
+                              full_bar(s), pol);
+            }
+        }
     } else if (lane == 0) {
         // ---- MMA issue ------------------------------------------------------------------
         const uint32_t idesc = (1u << 4)                        // D fp32
@@ -378,9 +392,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_w4a16_kernel(const GemmP
     if (fail && p.status) atomicOr(p.status, 1);
 
     // ---- epilogue: TMEM -> out ---------------------------------------------------------
+    // warp w reads TMEM lanes 32(w%4).. (its quadrant) for the 32-column chunks
+    // with index = w/4 (mod 2)
     const bool epi = warp < kAWarps;
-    const int r = warp * 32 + lane;
-    const int grow = row0 + r;
+    const int er = (warp & 3) * 32 + lane;
+    const int grow = row0 + er;
     float* part = reinterpret_cast<float*>(sm);  // split-K partial tile [T][128], reuses the rings
     if (epi) {
         pdl_wait();
@@ -388,8 +404,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_w4a16_kernel(const GemmP
         if (!ok && p.status) atomicOr(p.status, 1);
         __syncwarp();  // tcgen05.ld is warp-aligned
         tc_fence_after();
-        const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
-        for (int c0 = 0; c0 < T; c0 += 32) {
+        const uint32_t trow = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+        for (int c0 = (warp >> 2) * 32; c0 < T; c0 += 64) {
             uint32_t v[32];
             tmem_ld32(trow + (uint32_t)c0, v);
             tmem_wait_ld();
@@ -410,7 +426,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_w4a16_kernel(const GemmP
             } else {
 #pragma unroll
                 for (int j = 0; j < 32; j++)
-                    if (c0 + j < T) part[(c0 + j) * kGemmRows + r] = __uint_as_float(v[j]);
+                    if (c0 + j < T) part[(c0 + j) * kGemmRows + er] = __uint_as_float(v[j]);
             }
         }
     }
@@ -449,6 +465,7 @@ struct GemmPlan {
     int t_tile, n_tt, row_tiles, ks, stages;
     uint32_t tmem_cols;
     size_t smem;
+    size_t ws_bytes;
 };
 
 static int sm_count_gemm() {
@@ -462,12 +479,11 @@ static size_t gemm_smem(int t_tile, int stages) {
     return 1024 + (size_t)stages * (kAStageBytes + t_tile * 128) + 16 * (size_t)stages + 16;
 }
 
-static GemmPlan plan_gemm(int n_out, int n_in, int m, bool xf32) {
+static GemmPlan plan_gemm(int n_out, int n_in, int m) {
     GemmPlan pl{};
-    const int tmax = xf32 ? kMaxTileF32 : kMaxTileBf16;
-    pl.n_tt = (m + tmax - 1) / tmax;
+    pl.n_tt = (m + kMaxTile - 1) / kMaxTile;
     const int per = (m + pl.n_tt - 1) / pl.n_tt;             // balance the token tiles
-    pl.t_tile = std::min(tmax, (per + 15) / 16 * 16);
+    pl.t_tile = std::min(kMaxTile, (per + 15) / 16 * 16);
     pl.row_tiles = (n_out + kGemmRows - 1) / kGemmRows;
     const int stage_bytes = kAStageBytes + pl.t_tile * 128;
     pl.stages = std::min(8, (int)((kGemmSmemMax - 1024 - 256) / stage_bytes));
@@ -481,18 +497,25 @@ static GemmPlan plan_gemm(int n_out, int n_in, int m, bool xf32) {
     int ks = 1;
     if (ctas < sms) ks = std::min({8, nkb, std::max(1, sms / ctas)});
     pl.ks = ks;
+    pl.ws_bytes = (size_t)pl.n_tt * pl.t_tile * (size_t)n_in * 2;
     return pl;
 }
 
-template <bool XF32>
+static cudaLaunchAttribute pdl_attribute() {
+    cudaLaunchAttribute a;
+    a.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    a.val.programmaticStreamSerializationAllowed = 1;
+    return a;
+}
+
 static int launch_gemm(const GemmParams& prm, const GemmPlan& pl, cudaStream_t st) {
     // the shared-memory opt-in is a per-device function attribute
     static bool attr_done[64] = {false};
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return HQ4_ERR_LAUNCH;
     if (!attr_done[dev]) {
-        if (cudaFuncSetAttribute(gemm_w4a16_kernel<XF32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 kGemmSmemMax) != cudaSuccess)
+        if (cudaFuncSetAttribute(gemm_w4a16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmemMax) !=
+            cudaSuccess)
             return HQ4_ERR_LAUNCH;
         attr_done[dev] = true;
     }
@@ -502,9 +525,7 @@ static int launch_gemm(const GemmParams& prm, const GemmPlan& pl, cudaStream_t s
         return HQ4_ERR_SHAPE;
     cudaLaunchAttribute attr[2];
     int na = 0;
-    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[na].val.programmaticStreamSerializationAllowed = 1;
-    na++;
+    attr[na++] = pdl_attribute();
     if (pl.ks > 1) {
         attr[na].id = cudaLaunchAttributeClusterDimension;
         attr[na].val.clusterDim.x = 1;
@@ -519,29 +540,60 @@ static int launch_gemm(const GemmParams& prm, const GemmPlan& pl, cudaStream_t s
     lc.stream = st;
     lc.attrs = attr;
     lc.numAttrs = na;
-    return cudaLaunchKernelEx(&lc, gemm_w4a16_kernel<XF32>, prm) == cudaSuccess ? HQ4_OK : HQ4_ERR_LAUNCH;
+    return cudaLaunchKernelEx(&lc, gemm_w4a16_kernel, prm) == cudaSuccess ? HQ4_OK : HQ4_ERR_LAUNCH;
+}
+
+static int launch_xprep(const void* x, bool xf32, unsigned char* ws, int m, const GemmPlan& pl, int n_in,
+                        int* status, cudaStream_t st) {
+    const int m_pad = pl.n_tt * pl.t_tile;
+    const long long total = (long long)m_pad * (n_in >> 3);
+    const int blocks = (int)std::min<long long>((total + kPrepThreads - 1) / kPrepThreads, 4L * sm_count_gemm());
+    cudaLaunchAttribute attr[1] = {pdl_attribute()};
+    cudaLaunchConfig_t lc = {};
+    lc.gridDim = dim3((unsigned)blocks);
+    lc.blockDim = dim3(kPrepThreads);
+    lc.stream = st;
+    lc.attrs = attr;
+    lc.numAttrs = 1;
+    cudaError_t e = xf32 ? cudaLaunchKernelEx(&lc, gemm_xprep_kernel<true>, x, ws, m, m_pad, n_in, pl.t_tile, status)
+                         : cudaLaunchKernelEx(&lc, gemm_xprep_kernel<false>, x, ws, m, m_pad, n_in, pl.t_tile, status);
+    return e == cudaSuccess ? HQ4_OK : HQ4_ERR_LAUNCH;
 }
 
 }  // namespace hq4
 
 using namespace hq4;
 
+static bool gemm_shape_ok(int n_out, int n_in, int gs, int m) {
+    return n_out > 0 && n_in > 0 && m > 0 && gs >= 64 && gs % 64 == 0 && (gs & (gs - 1)) == 0 && n_in % gs == 0;
+}
+
+extern "C" long long hq4_gemm_workspace_bytes(int n_out, int n_in, int m) {
+    if (n_out <= 0 || n_in <= 0 || m <= 0 || n_in % 64) return HQ4_ERR_SHAPE;
+    return (long long)plan_gemm(n_out, n_in, m).ws_bytes;
+}
+
 extern "C" int hq4_gemm_w4a16(const uint32_t* w, const uint16_t* scales, const uint16_t* biases, const void* x,
                               int x_is_f32, float* out, int n_out, int n_in, int gs, int m,
-                              const float* row_add, const float* residual, void* stream) {
+                              const float* row_add, const float* residual, void* workspace,
+                              long long workspace_bytes, void* stream) {
     if (int rc = check_device_cap()) return rc;
-    if (n_out <= 0 || n_in <= 0 || m <= 0 || gs < 64 || gs % 64 || n_in % gs) return HQ4_ERR_SHAPE;
-    if ((gs & (gs - 1)) != 0) return HQ4_ERR_SHAPE;
+    if (!gemm_shape_ok(n_out, n_in, gs, m)) return HQ4_ERR_SHAPE;
     if (((uintptr_t)w & 31) || ((uintptr_t)x & 15) || ((uintptr_t)out & 3) || ((uintptr_t)scales & 1) ||
-        ((uintptr_t)biases & 1))
+        ((uintptr_t)biases & 1) || ((uintptr_t)workspace & 127))
         return HQ4_ERR_ALIGN;
-    const bool xf32 = x_is_f32 != 0;
-    const GemmPlan pl = plan_gemm(n_out, n_in, m, xf32);
+    const GemmPlan pl = plan_gemm(n_out, n_in, m);
+    if (!workspace || workspace_bytes < (long long)pl.ws_bytes) return HQ4_ERR_SHAPE;
+    int* status = status_word();
+    if (!status) return HQ4_ERR_LAUNCH;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    unsigned char* ws = static_cast<unsigned char*>(workspace);
+    if (int rc = launch_xprep(x, x_is_f32 != 0, ws, m, pl, n_in, status, st)) return rc;
     GemmParams prm{};
     prm.w = w;
     prm.sc = scales;
     prm.bi = biases;
-    prm.x = x;
+    prm.xw = ws;
     prm.out = out;
     prm.row_add = row_add;
     prm.residual = residual;
@@ -557,15 +609,14 @@ extern "C" int hq4_gemm_w4a16(const uint32_t* w, const uint16_t* scales, const u
     prm.t_tile = pl.t_tile;
     prm.stages = pl.stages;
     prm.tmem_cols = pl.tmem_cols;
-    prm.status = status_word();
-    if (!prm.status) return HQ4_ERR_LAUNCH;
-    cudaStream_t st = static_cast<cudaStream_t>(stream);
-    return xf32 ? launch_gemm<true>(prm, pl, st) : launch_gemm<false>(prm, pl, st);
+    prm.status = status;
+    return launch_gemm(prm, pl, st);
 }
 
 extern "C" int hq4_gemm_plan(int n_out, int n_in, int m, int x_is_f32, int* info) {
+    (void)x_is_f32;
     if (n_out <= 0 || n_in <= 0 || m <= 0 || n_in % 64 || !info) return HQ4_ERR_SHAPE;
-    const GemmPlan pl = plan_gemm(n_out, n_in, m, x_is_f32 != 0);
+    const GemmPlan pl = plan_gemm(n_out, n_in, m);
     info[0] = pl.row_tiles;
     info[1] = pl.ks;
     info[2] = pl.n_tt;

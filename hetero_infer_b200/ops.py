@@ -103,10 +103,30 @@ def q4_dequant(w: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor, row0
     return out
 
 
+_WORKSPACES = {}
+
+
+def gemm_workspace(n_out: int, n_in: int, m: int, device: torch.device) -> torch.Tensor:
+    """A grow-only per-device workspace large enough for hq4_gemm_w4a16 on
+    this shape.  Callers that capture CUDA graphs should take it before
+    capturing and pass it explicitly."""
+    lib = _lib.load()
+    need = int(lib.hq4_gemm_workspace_bytes(n_out, n_in, m))
+    if need < 0:
+        raise RuntimeError(f"hq4_gemm_workspace_bytes({n_out}, {n_in}, {m}) = {need}")
+    key = torch.device(device).index if torch.device(device).index is not None else torch.cuda.current_device()
+    ws = _WORKSPACES.get(key)
+    if ws is None or ws.numel() < need:
+        ws = torch.empty(max(need, 1 << 20), dtype=torch.uint8, device=torch.device("cuda", key))
+        _WORKSPACES[key] = ws
+    return ws
+
+
 def q4_gemm(w: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor, x: torch.Tensor,
             group_size: int = 64, row_add: Optional[torch.Tensor] = None,
             residual: Optional[torch.Tensor] = None,
-            out: Optional[torch.Tensor] = None) -> torch.Tensor:
+            out: Optional[torch.Tensor] = None,
+            workspace: Optional[torch.Tensor] = None) -> torch.Tensor:
     """W4A16 GEMM on the tcgen05 tensor cores (hq4_gemm_w4a16):
     ``out[m, n_out] = x[m, n_in] @ dequant(w).T`` with x bf16 or fp32 and an
     fp32 result, for token counts where the product is a dense contraction."""
@@ -133,9 +153,13 @@ def q4_gemm(w: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor, x: torc
     if residual is not None:
         _need_cuda(residual, "residual", torch.float32)
         rs = residual.data_ptr()
+    if workspace is None:
+        workspace = gemm_workspace(n_out, n_in, m, x.device)
+    _need_cuda(workspace, "workspace", torch.uint8)
     rc = lib.hq4_gemm_w4a16(w.data_ptr(), scales.data_ptr(), biases.data_ptr(), xf.data_ptr(),
                             1 if xf.dtype == torch.float32 else 0, out.data_ptr(), n_out, n_in,
-                            group_size, m, ra or None, rs or None, _stream_ptr(x.device))
+                            group_size, m, ra or None, rs or None, workspace.data_ptr(), workspace.numel(),
+                            _stream_ptr(x.device))
     _lib.check(rc, "hq4_gemm_w4a16")
     return out.reshape(*x.shape[:-1], n_out)
 

@@ -82,10 +82,20 @@ int hq4_dequant(const uint32_t* w, const uint16_t* scales, const uint16_t* biase
  * converted to fp16 (exact for bf16 x with |x| < 65520; larger magnitudes set
  * status bit 2); products and sums are fp32.  gs must be a power of two >= 64
  * dividing n_in (the reference's AVX2 build has the same gs % 64 rule,
- * q4gemv.c:234-240), else -1.  Deterministic; allocates nothing. */
+ * q4gemv.c:234-240), else -1.
+ * `workspace` (caller-owned, 128-byte aligned, at least
+ * hq4_gemm_workspace_bytes(n_out, n_in, m) bytes, else -1) receives the fp16
+ * activations in the tensor cores' tile layout; two calls in flight at once
+ * must not share it.  Deterministic; allocates nothing. */
 int hq4_gemm_w4a16(const uint32_t* w, const uint16_t* scales, const uint16_t* biases, const void* x,
                    int x_is_f32, float* out, int n_out, int n_in, int gs, int m,
-                   const float* row_add, const float* residual, void* stream);
+                   const float* row_add, const float* residual, void* workspace,
+                   long long workspace_bytes, void* stream);
+
+/* Workspace bytes hq4_gemm_w4a16 needs for a shape (host only; -1 for a bad
+ * shape).  No reference counterpart: the reference dequantises into a
+ * NumPy buffer it allocates per call (cpu_model.py:125-134). */
+long long hq4_gemm_workspace_bytes(int n_out, int n_in, int m);
 
 /* Launch plan hq4_gemm_w4a16 would use (no launch): info[0..7] = row tiles,
  * K-split cluster size, token tiles, tokens per tile, pipeline stages, shared

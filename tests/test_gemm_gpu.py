@@ -121,11 +121,16 @@ def test_gemm_error_codes(cuda):
     dw, ds, db, x = _case(256, 512, 8, 64, seed=1, x_dtype=torch.bfloat16)
     out = torch.empty(8, 256, device="cuda")
     st = torch.cuda.current_stream().cuda_stream
-    call = lambda xp, gs, n_in=512: lib.hq4_gemm_w4a16(dw.data_ptr(), ds.data_ptr(), db.data_ptr(), xp, 0,
-                                                       out.data_ptr(), 256, n_in, gs, 8, None, None, st)
+    need = lib.hq4_gemm_workspace_bytes(256, 512, 8)
+    assert need == 16 * 512 * 2          # one 16-token tile of fp16 activations
+    ws = torch.empty(need, dtype=torch.uint8, device="cuda")
+    call = lambda xp, gs, n_in=512, wsb=need: lib.hq4_gemm_w4a16(
+        dw.data_ptr(), ds.data_ptr(), db.data_ptr(), xp, 0, out.data_ptr(), 256, n_in, gs, 8, None, None,
+        ws.data_ptr(), wsb, st)
     assert call(x.data_ptr(), 32) == -1          # gs below 64 (q4gemv.c:234-240 AVX2 rule)
     assert call(x.data_ptr(), 96) == -1          # not a power of two
     assert call(x.data_ptr(), 64, n_in=500) == -1
+    assert call(x.data_ptr(), 64, wsb=need - 1) == -1   # workspace too small
     assert call(x.data_ptr() + 2, 64) == -2      # x not 16-byte aligned
     assert call(x.data_ptr(), 64) == 0
     torch.cuda.synchronize()
@@ -147,3 +152,25 @@ def test_gemm_range_flag(cuda):
     ops.q4_gemm(dw, ds, db, x, 64)
     torch.cuda.synchronize()
     assert lib.hq4_device_status(1) & 4
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("shape", [(18944, 3584, 256), (3584, 18944, 256), (2048, 1024, 200), (4096, 2048, 40)])
+def test_gemm_back_to_back_calls(cuda, shape):
+    """Calls queued back to back on one stream (the next launch overlapping the
+    previous one's tail), rotating weights, one shared workspace: every
+    output equals its own exact product."""
+    import torch
+    from hetero_infer_b200 import ops
+    n_out, n_in, m = shape
+    cases = [_case(n_out, n_in, m, 64, seed=300 + j, x_dtype=torch.bfloat16) for j in range(3)]
+    ws = ops.gemm_workspace(n_out, n_in, m, torch.device("cuda"))
+    outs = []
+    for rep in range(2):
+        for dw, ds, db, x in cases:
+            outs.append(ops.q4_gemm(dw, ds, db, x, 64, workspace=ws))
+    torch.cuda.synchronize()
+    for j, y in enumerate(outs):
+        dw, ds, db, x = cases[j % 3]
+        exact, _ = _refs(dw, ds, db, x, 64)
+        assert rel_l2(y, exact) <= EXACT_TOL, f"call {j}"
