@@ -217,9 +217,20 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
     return t;
 }
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+        " selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(done) : "r"(bar), "r"(parity) : "memory");
+    return done != 0;
+}
+// Wall-clock-bounded wait.  The timer is read only once the barrier has
+// been found incomplete (reading %globaltimer is slow), and each further
+// try_wait may suspend the thread in hardware (up to ~1 ms) until the phase
+// completes.
 __device__ __forceinline__ bool mbar_wait_ns(uint32_t bar, uint32_t parity, uint64_t limit_ns) {
-    // each try_wait may suspend the thread in hardware (up to ~1 ms) until the
-    // phase completes, so a waiting warp does not take issue slots
+    if (mbar_try(bar, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
     for (;;) {
         uint32_t done;
@@ -228,6 +239,28 @@ __device__ __forceinline__ bool mbar_wait_ns(uint32_t bar, uint32_t parity, uint
             " selp.u32 %0, 1, 0, p;\n}\n"
             : "=r"(done) : "r"(bar), "r"(parity), "r"(1000000u) : "memory");
         if (done) return true;
+        if (globaltimer_ns() - t0 > limit_ns) return false;
+    }
+}
+// Tight poll for the thread on the critical path (the MMA issuer): plain
+// try_wait, the timer read once every 1024 polls.
+__device__ __forceinline__ bool mbar_wait_spin(uint32_t bar, uint32_t parity, uint64_t limit_ns) {
+    if (mbar_try(bar, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t n = 1;; n++) {
+        if (mbar_try(bar, parity)) return true;
+        if ((n & 1023) == 0 && globaltimer_ns() - t0 > limit_ns) return false;
+    }
+}
+// The same wait for helper threads that are usually far ahead (loaders, the
+// MMA issuer): poll, then sleep `nap_ns` between polls so the waiting warp
+// leaves the issue slots to the warps sharing its scheduler.
+__device__ __forceinline__ bool mbar_wait_nap(uint32_t bar, uint32_t parity, uint64_t limit_ns, uint32_t nap_ns) {
+    if (mbar_try(bar, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    for (;;) {
+        __nanosleep(nap_ns);
+        if (mbar_try(bar, parity)) return true;
         if (globaltimer_ns() - t0 > limit_ns) return false;
     }
 }

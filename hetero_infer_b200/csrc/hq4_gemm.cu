@@ -12,21 +12,24 @@
 //     per (token tile, 64-wide k-block) one contiguous [T][64] fp16 block,
 //     K-major with the 128-byte swizzle.  A B stage is then one bulk copy.
 //  2. the GEMM.  One CTA owns 128 weight rows (the MMA's M) x T <= 256 tokens
-//     (its N) x a contiguous range of k-blocks:
+//     (its N) x a contiguous range of k-blocks, in super-blocks of 4 k-blocks:
+//       warp 8     streams each super-block's packed weights (128 rows x 128
+//                  bytes, 128-byte swizzle) and its scale and bias tiles into
+//                  a ring in shared memory with 2D TMA (cp.async.bulk.tensor);
+//       warp 9     streams the prepared activation blocks into the B stages
+//                  (cp.async.bulk);
 //       warps 0-7  dequantise: two threads per weight row, each turning 16
-//                  packed bytes of a k-block into 32 fp16 values (q as fp16
-//                  through the 0x6400 exponent trick, then one fma with the
-//                  group's scale and bias: a single rounding of q*s+b),
-//                  written K-major with the 128-byte swizzle; packed words are
-//                  prefetched in registers 4 k-blocks at a time, kSbPre
-//                  such groups ahead.  After the
-//                  mainloop the same warps read the fp32 accumulator out of
-//                  TMEM (warp w owns lanes 32(w%4)..+31).
-//       warp 8     one thread streams the workspace blocks into the B stages
-//                  (cp.async.bulk, completing on the stage's mbarrier).
-//       warp 9     allocates TMEM and, from one thread, issues
-//                  tcgen05.mma.cta_group::1.kind::f16 (K=16 per instruction)
-//                  once a stage is full, releasing it through tcgen05.commit.
+//                  packed bytes of a k-block (read from the ring) into 32
+//                  fp16 values (q as fp16 through exponent tricks, then one
+//                  fma with the group's scale and bias: a single rounding of
+//                  q*s+b), stored straight into the A operand in TMEM
+//                  (tcgen05.st); no global loads, no shared-memory round trip
+//                  for A.  After the mainloop the same warps read the fp32
+//                  accumulator out of TMEM (warp w owns lanes 32(w%4)..+31);
+//       warp 10    allocates TMEM and, from one thread, issues
+//                  tcgen05.mma.cta_group::1.kind::f16 with A in TMEM and B in
+//                  shared memory (K=16 per instruction) once a stage is full,
+//                  releasing it through tcgen05.commit.
 //
 // Inside a 64-wide k-block the k order is permuted identically for weights
 // and activations (word j of a row holds k = 8j..8j+7; its values are stored
@@ -46,7 +49,10 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
+#include <cuda.h>
+
 #include <algorithm>
+#include <mutex>
 
 #include "hq4_common.cuh"
 #include "hq4.h"
@@ -58,36 +64,41 @@ int* status_word();
 
 constexpr int kGemmRows = 128;                          // MMA M
 constexpr int kAWarps = 8;                              // dequant + epilogue
-constexpr int kLoadWarp = kAWarps;                      // warp 8: B-stage bulk copies
+constexpr int kLoadWarp = kAWarps;                      // warp 8: all TMA / bulk copies, in order
 constexpr int kMmaWarp = kAWarps + 1;                   // warp 9: TMEM + MMA issue
 constexpr int kGemmThreads = (kAWarps + 2) * 32;
-constexpr int kAStageBytes = kGemmRows * 128;           // 128 rows x 64 fp16
-constexpr int kSbPre = 3;                               // super-blocks (4 k-blocks) in flight per thread
+constexpr int kWTileBytes = kGemmRows * 128;            // packed super-block: 128 rows x 4 k-blocks
+constexpr int kSTileBytes = kGemmRows * 16;             // 8 groups of fp16 scales per row
+constexpr int kWSlotBytes = kWTileBytes + 2 * kSTileBytes;
+constexpr int kTmemCols = 512;
 constexpr uint64_t kGemmWaitNs = 1000000000ull;         // 1 s: a correct kernel never waits this long
 constexpr int kMaxTile = 256;
 constexpr int kGemmSmemMax = 220 * 1024;
 constexpr int kPrepThreads = 256;
 
 struct GemmParams {
-    const uint32_t* w;
-    const uint16_t* sc;
-    const uint16_t* bi;
     const unsigned char* xw;   // prepared activations (workspace)
     float* out;
     const float* row_add;
     const float* residual;
     int n_out, n_in, m;
-    int n_sg;       // groups per row
     int gs_shift;   // log2(gs / 64)
     int nkb;        // k-blocks per row (n_in / 64)
     int ks;         // CTAs of a cluster along K
     int t_tile;     // tokens per CTA (multiple of 16)
-    int stages;
-    uint32_t tmem_cols;
+    int stages;     // B (shared memory) k-block stages
+    int astages;    // A (TMEM) super-block stages, 128 columns each
+    int nacc;       // independent TMEM accumulators the MMAs rotate over
+    int acc_stride; // TMEM columns per accumulator (t_tile rounded up to 32)
+    int wslots;     // packed super-block slots
+    int sb_tma;     // scales/biases by TMA (else the dequant threads load them)
+    int n_sg;
+    const uint16_t* sc;
+    const uint16_t* bi;
     int* status;
 };
 
-// ---- tcgen05 / TMEM wrappers --------------------------------------------------
+// ---- tcgen05 / TMEM / TMA wrappers ----------------------------------------------
 __device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem),
                  "r"(ncols)
@@ -105,14 +116,14 @@ __device__ __forceinline__ void tc_fence_after() {
 __device__ __forceinline__ void tc_fence_before() {
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
 }
-// D[tmem] (+)= A[smem] . B[smem]^T, fp16 operands, fp32 accumulator.
-__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
-                                         uint32_t accumulate) {
+// D[tmem] (+)= A[tmem] . B[smem]^T, fp16 operands, fp32 accumulator.
+__device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t accumulate) {
     const uint32_t z = 0;
     asm volatile(
         "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-        " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n}\n" ::"r"(d_tmem),
-        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(z), "r"(z), "r"(z), "r"(z)
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n}\n" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(z), "r"(z), "r"(z), "r"(z)
         : "memory");
 }
 // Arrive once on an mbarrier when every tcgen05.mma issued so far has completed.
@@ -134,6 +145,18 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
 __device__ __forceinline__ void tmem_wait_ld() {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
+// 16 consecutive TMEM columns of this warp's 32 lanes <- 16 registers per thread.
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+            taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]),
+        "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+        : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() {
+    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
 __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
@@ -141,6 +164,16 @@ __device__ __forceinline__ float ld_cluster_f32(uint32_t addr) {
     float v;
     asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
     return v;
+}
+// 2D tensor copy global -> this CTA's shared memory (no multicast), completing
+// on the mbarrier `bar`; (x, y) is the box origin in elements.
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* tm, int x, int y, uint32_t bar,
+                                            uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(tm)), "r"(x), "r"(y), "r"(bar), "l"(policy)
+        : "memory");
 }
 
 // Shared-memory matrix descriptor: K-major, 128-byte swizzle, rows of 128 B
@@ -157,6 +190,13 @@ __device__ __forceinline__ uint32_t sw128_off(int r, int c) {
 
 __device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
 __device__ __forceinline__ __half2 bits_h2(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
+// fp16 number idx (0..7) of an 8-value row, replicated into both halves.
+__device__ __forceinline__ __half2 half_at(const uint4& v, int idx) {
+    const uint32_t lo = (idx & 2) ? v.y : v.x, hi = (idx & 2) ? v.w : v.z;
+    const uint32_t wd = (idx & 4) ? hi : lo;
+    const uint32_t h = (idx & 1) ? (wd >> 16) : (wd & 0xFFFFu);
+    return bits_h2(h | (h << 16));
+}
 
 // 8 nibbles of w -> fp16 q*s+b in the order n0,n4,n1,n5,n2,n6,n3,n7.
 // A nibble in bits 0-3 of a 16-bit half OR-ed into 0x6400 (1024.0) reads as
@@ -230,18 +270,25 @@ __global__ void __launch_bounds__(kPrepThreads) gemm_xprep_kernel(const void* __
 }
 
 // ---- the GEMM -------------------------------------------------------------------------
-__global__ void __launch_bounds__(kGemmThreads, 1) gemm_w4a16_kernel(const GemmParams p) {
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_w4a16_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_s,
+                      const __grid_constant__ CUtensorMap tm_b, const GemmParams p) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t base = (raw + 1023u) & ~1023u;  // SW128 atoms need 1024-byte alignment
     unsigned char* sm = smem_raw + (base - raw);
-    const int S = p.stages, T = p.t_tile;
+    const int S = p.stages, T = p.t_tile, DW = p.wslots, SA = p.astages;
     const int b_stage = T * 128;
-    const uint32_t a_base = base, b_base = base + (uint32_t)(S * kAStageBytes);
+    const uint32_t w_base = base;                                  // packed super-block ring
+    const uint32_t b_base = base + (uint32_t)(DW * kWSlotBytes);   // activation stages
     const uint32_t bar0 = b_base + (uint32_t)(S * b_stage);
-    auto full_bar = [&](int s) { return bar0 + 8u * (uint32_t)s; };
-    auto empty_bar = [&](int s) { return bar0 + 8u * (uint32_t)(S + s); };
-    const uint32_t accum_bar = bar0 + 16u * (uint32_t)S;
+    auto full_bar = [&](int s) { return bar0 + 8u * (uint32_t)s; };                 // B stage filled
+    auto empty_bar = [&](int s) { return bar0 + 8u * (uint32_t)(S + s); };          // B stage consumed
+    auto wfull_bar = [&](int j) { return bar0 + 8u * (uint32_t)(2 * S + j); };
+    auto wempty_bar = [&](int j) { return bar0 + 8u * (uint32_t)(2 * S + DW + j); };
+    auto afull_bar = [&](int a) { return bar0 + 8u * (uint32_t)(2 * S + 2 * DW + a); };
+    auto aempty_bar = [&](int a) { return bar0 + 8u * (uint32_t)(2 * S + 2 * DW + SA + a); };
+    const uint32_t accum_bar = bar0 + 8u * (uint32_t)(2 * S + 2 * DW + 2 * SA);
     const uint32_t tmem_slot = accum_bar + 8u;
     volatile uint32_t* tmem_slot_ptr = reinterpret_cast<volatile uint32_t*>(sm + (tmem_slot - base));
 
@@ -250,122 +297,157 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_w4a16_kernel(const GemmP
     const int kr = blockIdx.y;  // K-split rank (= cluster rank: the cluster spans grid y)
     const int tt = blockIdx.z, tok0 = tt * T;
     const int mt = min(T, p.m - tok0);
-    const int kb0 = (int)((long long)kr * p.nkb / p.ks), kb1 = (int)((long long)(kr + 1) * p.nkb / p.ks);
-    const int nk = kb1 - kb0;
+    // K range in whole super-blocks, so each super-block's groups sit in one
+    // 8-group scale tile
+    const int nsb_all = (p.nkb + 3) >> 2;
+    const int sb0 = (int)((long long)kr * nsb_all / p.ks), sb1 = (int)((long long)(kr + 1) * nsb_all / p.ks);
+    const int kb0 = 4 * sb0, kb1 = min(p.nkb, 4 * sb1);
+    const int nk = kb1 - kb0, nsb = sb1 - sb0;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; s++) {
-            mbar_init(full_bar(s), kAWarps + 1);  // one arrive per dequant warp + the copy's expect_tx
-            mbar_init(empty_bar(s), 1);
+            mbar_init(full_bar(s), 1);            // the copy's expect_tx
+            mbar_init(empty_bar(s), 1);           // MMA commit
+        }
+        for (int j = 0; j < DW; j++) {
+            mbar_init(wfull_bar(j), 1);           // the TMA's expect_tx
+            mbar_init(wempty_bar(j), kAWarps);    // one arrive per dequant warp
+        }
+        for (int a = 0; a < SA; a++) {
+            mbar_init(afull_bar(a), kAWarps);     // one arrive per dequant warp
+            mbar_init(aempty_bar(a), 1);          // MMA commit
         }
         mbar_init(accum_bar, 1);
     }
     if (warp == kMmaWarp) {
-        tmem_alloc(tmem_slot, p.tmem_cols);
+        tmem_alloc(tmem_slot, kTmemCols);
         tmem_relinquish();
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
+    // TMEM: A stages at columns [0, 128 SA), then nacc accumulators of
+    // acc_stride columns.  Consecutive MMAs go to different accumulators so
+    // small-N MMAs do not wait on one another's accumulation; the epilogue
+    // adds the accumulators in a fixed order.
     const uint32_t tmem = *tmem_slot_ptr;
+    const uint32_t acc_col = (uint32_t)(128 * SA);
+    const int NACC = p.nacc, ACS = p.acc_stride;
     pdl_launch_dependents();
 
     bool fail = false;
     if (warp < kAWarps) {
-        // ---- dequantise weights -------------------------------------------------------------
-        // Every dequant thread takes part in every k-block, in order (each
-        // waits for consecutive completions of each stage barrier, so none can
-        // be satisfied by an older phase of the same parity).  Thread (r, h):
-        // weight row r, words 4h..4h+3 of each k-block; warps 0-3 are h = 0,
-        // warps 4-7 h = 1.  Packed words are fetched a super-block (4
-        // k-blocks) at a time, so the two threads of a row request its 128
-        // contiguous bytes together -- one burst per row, as DRAM wants.
+        // ---- dequantise weights into the TMEM A stages ----------------------------------
+        // Thread (r, h): weight row r, words 4h..4h+3 of each k-block (warps
+        // 0-3 are h = 0, warps 4-7 h = 1; warp w writes TMEM lanes of
+        // quadrant w % 4 = its rows).  Every dequant thread takes part in
+        // every k-block, in order.
         const int h = warp >> 2;
         const int r = (warp & 3) * 32 + lane;
-        const int grow = row0 + r;
-        const bool rok = grow < p.n_out;
-        const size_t wpr = (size_t)(p.n_in >> 3);
-        const uint32_t* wrow = p.w + (size_t)(rok ? grow : 0) * wpr + 4 * h;
-        const uint16_t* srow = p.sc + (size_t)(rok ? grow : 0) * p.n_sg;
-        const uint16_t* brow = p.bi + (size_t)(rok ? grow : 0) * p.n_sg;
-        // gs = 64 with 8-byte aligned scale rows: 4 scales (biases) in one load
-        const bool vec_sb = p.gs_shift == 0 && (p.n_sg & 3) == 0 && (kb0 & 3) == 0 &&
-                            (((uintptr_t)p.sc | (uintptr_t)p.bi) & 7) == 0;
-        const int nsb = (nk + 3) >> 2;  // super-blocks in this CTA's K range
-        uint32_t q[kSbPre][16];
-        unsigned short sv[kSbPre][4], bv[kSbPre][4];
-        // Loads go straight into the ring registers, unconditionally: past
-        // the end of the range (or for a row past n_out) the address is
-        // clamped to valid data that is then not used.
-        auto fetch = [&](int sb, uint32_t (&qq)[16], unsigned short (&ss)[4], unsigned short (&bb)[4]) {
-            const int kbs = kb0 + 4 * min(sb, nsb - 1);  // first k-block of the super-block
-#pragma unroll
-            for (int u = 0; u < 4; u++) {
-                const int kb = min(kbs + u, kb1 - 1);
-                ldg128_into(wrow + (size_t)kb * 8, qq[4 * u], qq[4 * u + 1], qq[4 * u + 2], qq[4 * u + 3]);
+        const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+        for (int j = 0; j < nsb && !fail; j++) {
+            const int slot = j % DW, a = j % SA;
+            if (!mbar_wait_ns(wfull_bar(slot), (uint32_t)(j / DW) & 1u, kGemmWaitNs)) {
+                fail = true;
+                break;
             }
-            if (vec_sb && kbs + 3 < kb1) {
-                ldg_u16x4_into(srow + kbs, ss[0], ss[1], ss[2], ss[3]);
-                ldg_u16x4_into(brow + kbs, bb[0], bb[1], bb[2], bb[3]);
+            const unsigned char* wt = sm + (w_base - base) + (size_t)slot * kWSlotBytes;
+            const int kbf = kb0 + 4 * j;
+            int g_start;
+            uint4 s8, b8;
+            if (p.sb_tma) {
+                g_start = (kbf >> p.gs_shift) & ~7;
+                s8 = *reinterpret_cast<const uint4*>(wt + kWTileBytes + r * 16);
+                b8 = *reinterpret_cast<const uint4*>(wt + kWTileBytes + kSTileBytes + r * 16);
             } else {
+                // scale rows whose stride TMA cannot take: this row's (up to)
+                // 4 groups of the super-block straight from global memory
+                g_start = kbf >> p.gs_shift;
+                const int grow_c = min(row0 + r, p.n_out - 1);
+                const uint16_t* sr = p.sc + (size_t)grow_c * p.n_sg;
+                const uint16_t* br = p.bi + (size_t)grow_c * p.n_sg;
+                uint32_t sw[4], bw[4];
 #pragma unroll
                 for (int u = 0; u < 4; u++) {
-                    const int g = min(kbs + u, kb1 - 1) >> p.gs_shift;
-                    ldg_u16_into(srow + g, ss[u]);
-                    ldg_u16_into(brow + g, bb[u]);
+                    const int g = min(g_start + u, p.n_sg - 1);
+                    sw[u] = ldg_u16(sr + g);
+                    bw[u] = ldg_u16(br + g);
                 }
+                s8 = make_uint4(sw[0] | (sw[1] << 16), sw[2] | (sw[3] << 16), 0, 0);
+                b8 = make_uint4(bw[0] | (bw[1] << 16), bw[2] | (bw[3] << 16), 0, 0);
             }
-        };
+            uint4 wv[4];
 #pragma unroll
-        for (int d = 0; d < kSbPre; d++) fetch(d, q[d], sv[d], bv[d]);
-        for (int sbb = 0; sbb < nsb && !fail; sbb += kSbPre) {
+            for (int u = 0; u < 4; u++) wv[u] = *reinterpret_cast<const uint4*>(wt + sw128_off(r, 2 * u + h));
+            // the TMEM A stage must have been consumed by the MMAs of super-block j - SA
+            if (j >= SA && !mbar_wait_ns(aempty_bar(a), (uint32_t)((j / SA) - 1) & 1u, kGemmWaitNs)) {
+                fail = true;
+                break;
+            }
+            tc_fence_after();
 #pragma unroll
-            for (int d = 0; d < kSbPre; d++) {
-                const int sb = sbb + d;
-                if (sb < nsb && !fail) {
-#pragma unroll
-                    for (int u = 0; u < 4; u++) {
-                        const int i = 4 * sb + u;  // local k-block
-                        if (i < nk && !fail) {
-                            const int s = i % S;
-                            if (i >= S &&
-                                !mbar_wait_ns(empty_bar(s), (uint32_t)((i / S) - 1) & 1u, kGemmWaitNs)) {
-                                fail = true;
-                            } else {
-                                const __half2 s2 = __half2half2(__ushort_as_half(sv[d][u]));
-                                const __half2 b2 = __half2half2(__ushort_as_half(bv[d][u]));
-                                unsigned char* dst = sm + (a_base - base) + (size_t)s * kAStageBytes;
-#pragma unroll
-                                for (int c = 0; c < 4; c++) {
-                                    const uint4 v = rok ? dequant_word(q[d][4 * u + c], s2, b2)
-                                                        : make_uint4(0, 0, 0, 0);
-                                    *reinterpret_cast<uint4*>(dst + sw128_off(r, 4 * h + c)) = v;
-                                }
-                                fence_proxy_async_smem();
-                                __syncwarp();
-                                if (lane == 0) mbar_arrive(full_bar(s));
-                            }
-                        }
-                    }
-                    fetch(sb + kSbPre, q[d], sv[d], bv[d]);
-                }
+            for (int u = 0; u < 4; u++) {  // all 4 k-blocks (past the range: unused columns)
+                const int gi = ((kbf + u) >> p.gs_shift) - g_start;
+                const __half2 s2 = half_at(s8, min(gi, 7)), b2 = half_at(b8, min(gi, 7));
+                uint32_t v[16];
+                const uint4 d0 = dequant_word(wv[u].x, s2, b2), d1 = dequant_word(wv[u].y, s2, b2);
+                const uint4 d2 = dequant_word(wv[u].z, s2, b2), d3 = dequant_word(wv[u].w, s2, b2);
+                v[0] = d0.x; v[1] = d0.y; v[2] = d0.z; v[3] = d0.w;
+                v[4] = d1.x; v[5] = d1.y; v[6] = d1.z; v[7] = d1.w;
+                v[8] = d2.x; v[9] = d2.y; v[10] = d2.z; v[11] = d2.w;
+                v[12] = d3.x; v[13] = d3.y; v[14] = d3.z; v[15] = d3.w;
+                tmem_st16(tmem + lane_base + (uint32_t)(a * 128 + u * 32 + 16 * h), v);
+            }
+            tmem_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(afull_bar(a));
+                mbar_arrive(wempty_bar(slot));  // this warp is done reading the slot
             }
         }
     } else if (warp == kLoadWarp) {
-        // ---- B stages: one bulk copy of a prepared block each ---------------------------
+        // ---- one loader, issuing in consumption order --------------------------------
+        // per super-block j: its packed weights, scales and biases (2D TMA),
+        // then the prepared activation blocks of its k-blocks (bulk copies).
+        // One queue in consumption order keeps an activation copy from
+        // waiting behind weight loads issued for later super-blocks.
         if (lane == 0) {
-            pdl_wait();  // the workspace is written by the preparation kernel
-            const uint64_t pol = l2_policy_evict_last();
+            const uint64_t pol_w = l2_policy_evict_first();
+            const uint64_t pol_x = l2_policy_evict_last();
             const unsigned char* src = p.xw + ((size_t)tt * p.nkb + kb0) * (size_t)b_stage;
-            for (int i = 0; i < nk; i++) {
-                const int s = i % S;
-                if (i >= S && !mbar_wait_ns(empty_bar(s), (uint32_t)((i / S) - 1) & 1u, kGemmWaitNs)) {
+            bool waited = false;
+            for (int j = 0; j < nsb && !fail; j++) {
+                const int slot = j % DW;
+                if (j >= DW && !mbar_wait_nap(wempty_bar(slot), (uint32_t)((j / DW) - 1) & 1u, kGemmWaitNs, 64)) {
                     fail = true;
                     break;
                 }
-                mbar_arrive_expect_tx(full_bar(s), (uint32_t)b_stage);
-                bulk_load_g2s(b_base + (uint32_t)(s * b_stage), src + (size_t)i * b_stage, (uint32_t)b_stage,
-                              full_bar(s), pol);
+                const uint32_t dst = w_base + (uint32_t)(slot * kWSlotBytes);
+                const int kbf = kb0 + 4 * j;
+                const int g_start = (kbf >> p.gs_shift) & ~7;
+                mbar_arrive_expect_tx(wfull_bar(slot), (uint32_t)(p.sb_tma ? kWSlotBytes : kWTileBytes));
+                tma_load_2d(dst, &tm_w, kbf * 8, row0, wfull_bar(slot), pol_w);
+                if (p.sb_tma) {
+                    tma_load_2d(dst + kWTileBytes, &tm_s, g_start, row0, wfull_bar(slot), pol_w);
+                    tma_load_2d(dst + kWTileBytes + kSTileBytes, &tm_b, g_start, row0, wfull_bar(slot), pol_w);
+                }
+                if (!waited) {
+                    pdl_wait();  // the activation workspace is written by the preparation kernel
+                    waited = true;
+                }
+                for (int u = 0; u < 4; u++) {
+                    const int i = 4 * j + u;
+                    if (i >= nk) break;
+                    const int s = i % S;
+                    if (i >= S && !mbar_wait_nap(empty_bar(s), (uint32_t)((i / S) - 1) & 1u, kGemmWaitNs, 64)) {
+                        fail = true;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(full_bar(s), (uint32_t)b_stage);
+                    bulk_load_g2s(b_base + (uint32_t)(s * b_stage), src + (size_t)i * b_stage, (uint32_t)b_stage,
+                                  full_bar(s), pol_x);
+                }
             }
         }
     } else if (lane == 0) {
@@ -373,19 +455,47 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_w4a16_kernel(const GemmP
         const uint32_t idesc = (1u << 4)                        // D fp32
                                | ((uint32_t)(T >> 3) << 17)     // N
                                | ((uint32_t)(kGemmRows >> 4) << 24);  // M
-        for (int i = 0; i < nk; i++) {
-            const int s = i % S;
-            if (!mbar_wait_ns(full_bar(s), (uint32_t)(i / S) & 1u, kGemmWaitNs)) {
+        // stage / phase counters instead of divisions: this loop paces the MMAs
+        int a = 0, s = 0, acc = 0;
+        uint32_t pa = 0, pb = 0;
+        bool first = true;
+        uint32_t dcol = tmem + acc_col;  // current accumulator
+        for (int j = 0; j < nsb && !fail; j++) {
+            if (!mbar_wait_spin(afull_bar(a), pa, kGemmWaitNs)) {
                 fail = true;
                 break;
             }
-            tc_fence_after();
-            const uint64_t ad = sw128_desc(a_base + (uint32_t)(s * kAStageBytes));
-            const uint64_t bd = sw128_desc(b_base + (uint32_t)(s * b_stage));
+            const uint32_t abase = tmem + (uint32_t)(a * 128);
+            const int nu = min(4, nk - 4 * j);
+            for (int u = 0; u < nu; u++) {
+                if (!mbar_wait_spin(full_bar(s), pb, kGemmWaitNs)) {
+                    fail = true;
+                    break;
+                }
+                tc_fence_after();
+                const uint64_t bd = sw128_desc(b_base + (uint32_t)(s * b_stage));
+                const uint32_t acol = abase + (uint32_t)(u * 32);
 #pragma unroll
-            for (int kk = 0; kk < 4; kk++)  // 16 k per instruction: +32 bytes = +2 descriptor units
-                umma_f16(tmem, ad + 2u * kk, bd + 2u * kk, idesc, (i | kk) != 0);
-            umma_commit(empty_bar(s));
+                for (int kk = 0; kk < 4; kk++) {  // 16 k per instruction: A +8 TMEM columns, B +32 bytes
+                    umma_f16_ts(dcol, acol + 8u * kk, bd + 2u * kk, idesc, first ? 0u : 1u);
+                    dcol += (uint32_t)ACS;
+                    if (++acc == NACC) {
+                        acc = 0;
+                        dcol = tmem + acc_col;
+                        first = false;
+                    }
+                }
+                umma_commit(empty_bar(s));
+                if (++s == S) {
+                    s = 0;
+                    pb ^= 1u;
+                }
+            }
+            umma_commit(aempty_bar(a));
+            if (++a == SA) {
+                a = 0;
+                pa ^= 1u;
+            }
         }
         umma_commit(accum_bar);
     }
@@ -404,11 +514,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_w4a16_kernel(const GemmP
         if (!ok && p.status) atomicOr(p.status, 1);
         __syncwarp();  // tcgen05.ld is warp-aligned
         tc_fence_after();
-        const uint32_t trow = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+        const uint32_t trow = tmem + acc_col + ((uint32_t)((warp & 3) * 32) << 16);
         for (int c0 = (warp >> 2) * 32; c0 < T; c0 += 64) {
             uint32_t v[32];
             tmem_ld32(trow + (uint32_t)c0, v);
             tmem_wait_ld();
+            for (int c = 1; c < NACC; c++) {  // accumulators in a fixed order
+                uint32_t w2[32];
+                tmem_ld32(trow + (uint32_t)(c * ACS + c0), w2);
+                tmem_wait_ld();
+#pragma unroll
+                for (int q = 0; q < 32; q++) v[q] = __float_as_uint(__uint_as_float(v[q]) + __uint_as_float(w2[q]));
+            }
             if (p.ks == 1) {
                 if (ok && grow < p.n_out) {
                     const float add = p.row_add ? p.row_add[grow] : 0.0f;
@@ -456,14 +573,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_w4a16_kernel(const GemmP
     __syncthreads();
     if (warp == kMmaWarp) {
         __syncwarp();
-        tmem_dealloc(tmem, p.tmem_cols);
+        tmem_dealloc(tmem, kTmemCols);
     }
 }
 
 // ---- host side --------------------------------------------------------------------------
 struct GemmPlan {
-    int t_tile, n_tt, row_tiles, ks, stages;
-    uint32_t tmem_cols;
+    int t_tile, n_tt, row_tiles, ks, stages, astages, wslots, nacc, acc_stride;
     size_t smem;
     size_t ws_bytes;
 };
@@ -475,8 +591,9 @@ static int sm_count_gemm() {
     return n;
 }
 
-static size_t gemm_smem(int t_tile, int stages) {
-    return 1024 + (size_t)stages * (kAStageBytes + t_tile * 128) + 16 * (size_t)stages + 16;
+static size_t gemm_smem(int t_tile, int stages, int wslots, int astages) {
+    return 1024 + (size_t)wslots * kWSlotBytes + (size_t)stages * t_tile * 128 +
+           8 * (size_t)(2 * stages + 2 * wslots + 2 * astages + 1) + 16;
 }
 
 static GemmPlan plan_gemm(int n_out, int n_in, int m) {
@@ -485,17 +602,40 @@ static GemmPlan plan_gemm(int n_out, int n_in, int m) {
     const int per = (m + pl.n_tt - 1) / pl.n_tt;             // balance the token tiles
     pl.t_tile = std::min(kMaxTile, (per + 15) / 16 * 16);
     pl.row_tiles = (n_out + kGemmRows - 1) / kGemmRows;
-    const int stage_bytes = kAStageBytes + pl.t_tile * 128;
-    pl.stages = std::min(8, (int)((kGemmSmemMax - 1024 - 256) / stage_bytes));
-    pl.smem = gemm_smem(pl.t_tile, pl.stages);
-    uint32_t c = 32;
-    while ((int)c < pl.t_tile) c <<= 1;
-    pl.tmem_cols = c;
+    // TMEM (512 columns): 128 per A stage + nacc accumulators of t_tile
+    // rounded up to 32
+    pl.acc_stride = (pl.t_tile + 31) / 32 * 32;
+    if (pl.acc_stride <= 32) {
+        pl.astages = 3;
+        pl.nacc = 4;
+    } else if (pl.acc_stride <= 64) {
+        pl.astages = 2;
+        pl.nacc = 4;
+    } else if (pl.acc_stride <= 128) {
+        pl.astages = 2;
+        pl.nacc = 2;
+    } else {
+        pl.astages = 2;
+        pl.nacc = 1;
+    }
+    // the loader runs min(weight slots, activation stages / 4) super-blocks
+    // ahead: give both rings that depth, as deep as shared memory allows
+    pl.wslots = 6;
+    pl.stages = 24;
+    while (gemm_smem(pl.t_tile, pl.stages, pl.wslots, pl.astages) > (size_t)kGemmSmemMax) {
+        if (pl.stages > 4 * pl.wslots - 4 || pl.wslots <= 2) {
+            if (pl.stages > 4) pl.stages -= 4;
+            else break;
+        } else {
+            pl.wslots--;
+        }
+    }
+    pl.smem = gemm_smem(pl.t_tile, pl.stages, pl.wslots, pl.astages);
     const int sms = sm_count_gemm();
     const int ctas = pl.row_tiles * pl.n_tt;
-    const int nkb = n_in / 64;
+    const int nsb = (n_in / 64 + 3) / 4;
     int ks = 1;
-    if (ctas < sms) ks = std::min({8, nkb, std::max(1, sms / ctas)});
+    if (ctas < sms) ks = std::min({8, nsb, std::max(1, sms / ctas)});
     pl.ks = ks;
     pl.ws_bytes = (size_t)pl.n_tt * pl.t_tile * (size_t)n_in * 2;
     return pl;
@@ -508,7 +648,93 @@ static cudaLaunchAttribute pdl_attribute() {
     return a;
 }
 
-static int launch_gemm(const GemmParams& prm, const GemmPlan& pl, cudaStream_t st) {
+// ---- tensor maps (cuTensorMapEncodeTiled through the runtime's driver entry point)
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static bool tried = false;
+    if (!tried) {
+        tried = true;
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &f, 12000, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(f);
+    }
+    return fn;
+}
+
+// rows x cols 2D map of `elem`-byte elements, box (box_cols x 128 rows)
+static bool make_map(CUtensorMap* tm, const void* ptr, CUtensorMapDataType dt, int elem, long long rows,
+                     long long cols, int box_cols, bool swizzle128) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)(cols * elem)};
+    cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)kGemmRows};
+    cuuint32_t estr[2] = {1, 1};
+    return fn(tm, dt, 2, const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+              swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+struct WeightMaps {
+    const void* w;
+    const void* s;
+    const void* b;
+    int n_out, n_in, n_sg, dev;
+    bool sb_tma;
+    CUtensorMap tw, ts, tb;
+};
+
+// The three maps of a weight matrix, cached by (pointers, shape, device).
+static bool weight_maps(const uint32_t* w, const uint16_t* sc, const uint16_t* bi, int n_out, int n_in, int n_sg,
+                        WeightMaps* outm) {
+    static std::mutex mu;
+    static WeightMaps cache[64];
+    static int used = 0, next = 0;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return false;
+    std::lock_guard<std::mutex> g(mu);
+    for (int i = 0; i < used; i++) {
+        const WeightMaps& c = cache[i];
+        if (c.w == w && c.s == sc && c.b == bi && c.n_out == n_out && c.n_in == n_in && c.n_sg == n_sg &&
+            c.dev == dev) {
+            *outm = c;
+            return true;
+        }
+    }
+    WeightMaps m{};
+    m.w = w;
+    m.s = sc;
+    m.b = bi;
+    m.n_out = n_out;
+    m.n_in = n_in;
+    m.n_sg = n_sg;
+    m.dev = dev;
+    // scale tiles by TMA need a row stride (n_sg * 2 bytes) and base that are
+    // multiples of 16 bytes
+    m.sb_tma = n_sg % 8 == 0 && (((uintptr_t)sc | (uintptr_t)bi) & 15) == 0;
+    if (!make_map(&m.tw, w, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, n_out, n_in / 8, 32, true)) return false;
+    if (m.sb_tma) {
+        if (!make_map(&m.ts, sc, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, n_out, n_sg, 8, false) ||
+            !make_map(&m.tb, bi, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, n_out, n_sg, 8, false))
+            return false;
+    } else {
+        m.ts = m.tw;  // unused
+        m.tb = m.tw;
+    }
+    const int at = used < 64 ? used++ : (next++ & 63);
+    cache[at] = m;
+    *outm = m;
+    return true;
+}
+
+static int launch_gemm(const WeightMaps& wm, const GemmParams& prm, const GemmPlan& pl, cudaStream_t st) {
     // the shared-memory opt-in is a per-device function attribute
     static bool attr_done[64] = {false};
     int dev = 0;
@@ -519,9 +745,10 @@ static int launch_gemm(const GemmParams& prm, const GemmPlan& pl, cudaStream_t s
             return HQ4_ERR_LAUNCH;
         attr_done[dev] = true;
     }
-    // split-K partial tile [t_tile][128] fp32 lives in the (drained) rings
-    if ((size_t)pl.t_tile * kGemmRows * 4 > (size_t)pl.stages * (kAStageBytes + pl.t_tile * 128) ||
-        pl.smem > (size_t)kGemmSmemMax)
+    // split-K partial tile [t_tile][128] fp32 lives in the (drained) rings;
+    // A stages + accumulator fit the 512 TMEM columns
+    if ((size_t)pl.t_tile * kGemmRows * 4 > (size_t)pl.wslots * kWSlotBytes + (size_t)pl.stages * pl.t_tile * 128 ||
+        pl.smem > (size_t)kGemmSmemMax || 128 * pl.astages + pl.nacc * pl.acc_stride > kTmemCols)
         return HQ4_ERR_SHAPE;
     cudaLaunchAttribute attr[2];
     int na = 0;
@@ -540,7 +767,8 @@ static int launch_gemm(const GemmParams& prm, const GemmPlan& pl, cudaStream_t s
     lc.stream = st;
     lc.attrs = attr;
     lc.numAttrs = na;
-    return cudaLaunchKernelEx(&lc, gemm_w4a16_kernel, prm) == cudaSuccess ? HQ4_OK : HQ4_ERR_LAUNCH;
+    return cudaLaunchKernelEx(&lc, gemm_w4a16_kernel, wm.tw, wm.ts, wm.tb, prm) == cudaSuccess ? HQ4_OK
+                                                                                             : HQ4_ERR_LAUNCH;
 }
 
 static int launch_xprep(const void* x, bool xf32, unsigned char* ws, int m, const GemmPlan& pl, int n_in,
@@ -586,13 +814,12 @@ extern "C" int hq4_gemm_w4a16(const uint32_t* w, const uint16_t* scales, const u
     if (!workspace || workspace_bytes < (long long)pl.ws_bytes) return HQ4_ERR_SHAPE;
     int* status = status_word();
     if (!status) return HQ4_ERR_LAUNCH;
+    WeightMaps wm;
+    if (!weight_maps(w, scales, biases, n_out, n_in, n_in / gs, &wm)) return HQ4_ERR_LAUNCH;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     unsigned char* ws = static_cast<unsigned char*>(workspace);
     if (int rc = launch_xprep(x, x_is_f32 != 0, ws, m, pl, n_in, status, st)) return rc;
     GemmParams prm{};
-    prm.w = w;
-    prm.sc = scales;
-    prm.bi = biases;
     prm.xw = ws;
     prm.out = out;
     prm.row_add = row_add;
@@ -600,7 +827,6 @@ extern "C" int hq4_gemm_w4a16(const uint32_t* w, const uint16_t* scales, const u
     prm.n_out = n_out;
     prm.n_in = n_in;
     prm.m = m;
-    prm.n_sg = n_in / gs;
     int sh = 0;
     while ((64 << sh) < gs) sh++;
     prm.gs_shift = sh;
@@ -608,9 +834,16 @@ extern "C" int hq4_gemm_w4a16(const uint32_t* w, const uint16_t* scales, const u
     prm.ks = pl.ks;
     prm.t_tile = pl.t_tile;
     prm.stages = pl.stages;
-    prm.tmem_cols = pl.tmem_cols;
+    prm.astages = pl.astages;
+    prm.nacc = pl.nacc;
+    prm.acc_stride = pl.acc_stride;
+    prm.wslots = pl.wslots;
+    prm.sb_tma = wm.sb_tma ? 1 : 0;
+    prm.n_sg = n_in / gs;
+    prm.sc = scales;
+    prm.bi = biases;
     prm.status = status;
-    return launch_gemm(prm, pl, st);
+    return launch_gemm(wm, prm, pl, st);
 }
 
 extern "C" int hq4_gemm_plan(int n_out, int n_in, int m, int x_is_f32, int* info) {
@@ -623,7 +856,7 @@ extern "C" int hq4_gemm_plan(int n_out, int n_in, int m, int x_is_f32, int* info
     info[3] = pl.t_tile;
     info[4] = pl.stages;
     info[5] = (int)pl.smem;
-    info[6] = (int)pl.tmem_cols;
+    info[6] = pl.wslots;
     info[7] = kGemmThreads;
     return HQ4_OK;
 }

@@ -99,7 +99,8 @@ long long hq4_gemm_workspace_bytes(int n_out, int n_in, int m);
 
 /* Launch plan hq4_gemm_w4a16 would use (no launch): info[0..7] = row tiles,
  * K-split cluster size, token tiles, tokens per tile, pipeline stages, shared
- * memory bytes, TMEM columns, threads per CTA.  No reference counterpart. */
+ * memory bytes, packed-weight ring slots, threads per CTA.  No reference
+ * counterpart. */
 int hq4_gemm_plan(int n_out, int n_in, int m, int x_is_f32, int* info);
 
 /* ---- qwen2 stage forward (hetero/cpu_model.py:164-368) ---------------------
