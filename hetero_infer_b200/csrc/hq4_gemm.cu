@@ -788,6 +788,459 @@ static int launch_xprep(const void* x, bool xf32, unsigned char* ws, int m, cons
     return e == cudaSuccess ? HQ4_OK : HQ4_ERR_LAUNCH;
 }
 
+
+// ===========================================================================
+// Small token counts: register-path MMAs on the same weight stream.
+//
+// For m up to 16 (bf16 x) the tensor work per weight byte is small and the
+// cost of issuing tcgen05.mma from one thread dominates, so here every
+// consumer warp issues its own warp-level MMAs (mma.sync m16n8k16, bf16 in,
+// fp32 accumulate) on the packed weights the loader streams in by TMA:
+//
+//   * warp w (0-7) owns CTA rows 16w..16w+15; lane (g, t) = (lane/4, lane%4)
+//     holds rows g and g+8;
+//   * weights enter the MMA as 128+q in bf16 (exact: nibble OR 0x4300), so a
+//     64-wide group's product is D = sum (128+q) x, folded per group into
+//     fp32 accumulators as  acc += s*D + (b - 128 s) * X,  X = sum of the
+//     group's x (exact in fp32 up to summation order);
+//   * lane t uses words 2t, 2t+1 of each group; k-step kk takes nibbles
+//     (kk, kk+4) of each word, so x is pre-arranged (xprep_frag) in exactly
+//     that order: per (group, 8-token tile) 32 bytes per lane, then the
+//     tile's 8 group sums;
+//   * fp32 x becomes two bf16 "virtual tokens" (hi, x - hi), placed in the
+//     two C columns a lane owns and added at the end (16 significant bits).
+// ===========================================================================
+constexpr int kFragBlock = 1024 + 32;   // per (group, 8-token tile): fragments + 8 group sums
+
+__device__ __forceinline__ uint32_t bf16_bits(float f) {  // round to nearest even (finite inputs)
+    const uint32_t u = __float_as_uint(f);
+    return (u + 0x7FFFu + ((u >> 16) & 1u)) >> 16;
+}
+__device__ __forceinline__ float bf16_to_f(uint32_t h) { return __uint_as_float(h << 16); }
+
+// x [m][n_in] (bf16 or fp32) -> per (super-block, group u, tile n, lane) fragments.
+// Thread per (group G, tile n, lane l): 16 values + (lane < 8) the group sum of token n*8+lane.
+template <bool XF32>
+__global__ void __launch_bounds__(kPrepThreads) gemm_xprep_frag_kernel(const void* __restrict__ x,
+                                                                     unsigned char* __restrict__ ws, int m,
+                                                                     int n_in, int nt, int* status) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const int ng = n_in >> 6;
+    const long long total = (long long)ng * nt * 32;
+    float amax = 0.0f;
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (long long)gridDim.x * blockDim.x) {
+        const int l = (int)(i & 31);
+        const int n = (int)((i >> 5) % nt);
+        const int G = (int)((i >> 5) / nt);
+        const int g = l >> 2, t = l & 3;
+        // virtual token v of this lane's column: tile n, column g
+        const int v = n * 8 + g;
+        const int tok = XF32 ? (v >> 1) : v;
+        const bool lo_part = XF32 && (v & 1);
+        const bool live = tok < m;
+        auto xval = [&](int k) -> float {  // the virtual token's value at group-local k, exactly bf16
+            if (!live) return 0.0f;
+            const size_t e = (size_t)tok * n_in + (size_t)G * 64 + k;
+            float f;
+            if constexpr (XF32) {
+                const float xf = __ldg(reinterpret_cast<const float*>(x) + e);
+                const float hi = bf16_to_f(bf16_bits(xf));
+                f = lo_part ? bf16_to_f(bf16_bits(xf - hi)) : hi;
+                amax = fmaxf(amax, fabsf(xf));
+            } else {
+                f = bf16_to_f(__ldg(reinterpret_cast<const unsigned short*>(x) + e));
+            }
+            return f;
+        };
+        uint32_t o[8];
+#pragma unroll
+        for (int kk = 0; kk < 4; kk++) {
+            const float a = xval(16 * t + kk), b = xval(16 * t + kk + 4);
+            const float c = xval(16 * t + 8 + kk), d = xval(16 * t + 12 + kk);
+            o[2 * kk] = bf16_bits(a) | (bf16_bits(b) << 16);
+            o[2 * kk + 1] = bf16_bits(c) | (bf16_bits(d) << 16);
+        }
+        const int sb = G >> 2, u = G & 3;
+        unsigned char* blk = ws + (((size_t)sb * 4 + u) * nt + n) * kFragBlock;
+        uint4* dst = reinterpret_cast<uint4*>(blk + l * 32);
+        dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
+        dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+        if (l < 8) {  // group sum X of virtual token n*8 + l, from the same bf16 values
+            const int vv = n * 8 + l;
+            const int tk = XF32 ? (vv >> 1) : vv;
+            float sum = 0.0f;
+            if (tk < m) {
+                for (int k = 0; k < 64; k++) {
+                    const size_t e = (size_t)tk * n_in + (size_t)G * 64 + k;
+                    float f;
+                    if constexpr (XF32) {
+                        const float xf = __ldg(reinterpret_cast<const float*>(x) + e);
+                        const float hi = bf16_to_f(bf16_bits(xf));
+                        f = (vv & 1) ? bf16_to_f(bf16_bits(xf - hi)) : hi;
+                    } else {
+                        f = bf16_to_f(__ldg(reinterpret_cast<const unsigned short*>(x) + e));
+                    }
+                    sum += f;
+                }
+            }
+            reinterpret_cast<float*>(blk + 1024)[l] = sum;
+        }
+    }
+    (void)status;
+    (void)amax;
+}
+
+struct SmallParams {
+    const unsigned char* xw;
+    float* out;
+    const float* row_add;
+    const float* residual;
+    int n_out, n_in, m, nkb, ks, nt, xf32, gs_shift;
+    int bstages, wslots, sb_tma, n_sg;
+    const uint16_t* sc;
+    const uint16_t* bi;
+    int* status;
+};
+
+template <int NT>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_small_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_s,
+                      const __grid_constant__ CUtensorMap tm_b, const SmallParams p) {
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    const uint32_t raw = smem_u32(smem_raw);
+    const uint32_t base = (raw + 1023u) & ~1023u;
+    unsigned char* sm = smem_raw + (base - raw);
+    const int DW = p.wslots;
+    // one ring slot per super-block: packed weights | scales | biases | activation fragments
+    const int b_bytes = 4 * NT * kFragBlock;
+    const int slot_bytes = (kWSlotBytes + b_bytes + 1023) & ~1023;
+    const uint32_t w_base = base;
+    const uint32_t bar0 = base + (uint32_t)(DW * slot_bytes);
+    auto full_bar = [&](int j) { return bar0 + 8u * (uint32_t)j; };
+    auto empty_bar = [&](int j) { return bar0 + 8u * (uint32_t)(DW + j); };
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int row0 = blockIdx.x * kGemmRows;
+    const int kr = blockIdx.y;
+    const int nsb_all = (p.nkb + 3) >> 2;
+    const int sb0 = (int)((long long)kr * nsb_all / p.ks), sb1 = (int)((long long)(kr + 1) * nsb_all / p.ks);
+    const int kb0 = 4 * sb0, kb1 = min(p.nkb, 4 * sb1);
+    const int nk = kb1 - kb0, nsb = sb1 - sb0;
+
+    if (threadIdx.x == 0) {
+        for (int j = 0; j < DW; j++) {
+            mbar_init(full_bar(j), 1);           // the loader's expect_tx
+            mbar_init(empty_bar(j), kAWarps);    // one arrive per consumer warp
+        }
+    }
+    __syncthreads();
+    pdl_launch_dependents();
+
+    bool fail = false;
+    const int g = lane >> 2, t = lane & 3;
+    float acc[NT][4];
+#pragma unroll
+    for (int n = 0; n < NT; n++)
+#pragma unroll
+        for (int q = 0; q < 4; q++) acc[n][q] = 0.0f;
+
+    if (warp < kAWarps) {
+        const int R0 = warp * 16 + g, R1 = R0 + 8;  // CTA rows of this lane
+        int slot = 0;
+        uint32_t ph = 0;
+        for (int j = 0; j < nsb && !fail; j++) {
+            if (!mbar_wait_ns(full_bar(slot), ph, kGemmWaitNs)) {
+                fail = true;
+                break;
+            }
+            const unsigned char* wt = sm + (size_t)slot * slot_bytes;
+            const unsigned char* xt = wt + kWSlotBytes;
+            const int kbf = kb0 + 4 * j;
+            const int nu = min(4, nk - 4 * j);
+            int g_start;
+            uint4 s0, s1, c0, c1;  // scales / biases of rows R0, R1 (8 groups)
+            if (p.sb_tma) {
+                g_start = (kbf >> p.gs_shift) & ~7;
+                s0 = *reinterpret_cast<const uint4*>(wt + kWTileBytes + R0 * 16);
+                s1 = *reinterpret_cast<const uint4*>(wt + kWTileBytes + R1 * 16);
+                c0 = *reinterpret_cast<const uint4*>(wt + kWTileBytes + kSTileBytes + R0 * 16);
+                c1 = *reinterpret_cast<const uint4*>(wt + kWTileBytes + kSTileBytes + R1 * 16);
+            } else {
+                g_start = kbf >> p.gs_shift;
+                uint32_t a[4], b[4], cc[4], d[4];
+                const int r0c = min(row0 + R0, p.n_out - 1), r1c = min(row0 + R1, p.n_out - 1);
+#pragma unroll
+                for (int u = 0; u < 4; u++) {
+                    const int gg = min(g_start + u, p.n_sg - 1);
+                    a[u] = ldg_u16(p.sc + (size_t)r0c * p.n_sg + gg);
+                    b[u] = ldg_u16(p.sc + (size_t)r1c * p.n_sg + gg);
+                    cc[u] = ldg_u16(p.bi + (size_t)r0c * p.n_sg + gg);
+                    d[u] = ldg_u16(p.bi + (size_t)r1c * p.n_sg + gg);
+                }
+                s0 = make_uint4(a[0] | (a[1] << 16), a[2] | (a[3] << 16), 0, 0);
+                s1 = make_uint4(b[0] | (b[1] << 16), b[2] | (b[3] << 16), 0, 0);
+                c0 = make_uint4(cc[0] | (cc[1] << 16), cc[2] | (cc[3] << 16), 0, 0);
+                c1 = make_uint4(d[0] | (d[1] << 16), d[2] | (d[3] << 16), 0, 0);
+            }
+            // A fragments of all 4 groups first (128+q as bf16 pairs): pair kk of a
+            // word = nibbles (kk, kk+4); words 2t, 2t+1 of each group, rows R0, R1
+            uint32_t A[4][4][4];  // [group u][kk][a0..a3]
+            float sr0[4], sr1[4], br0[4], br1[4];
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const int cidx = 2 * u + (t >> 1);
+                const uint2 w0 = *reinterpret_cast<const uint2*>(wt + R0 * 128 + ((cidx ^ (R0 & 7)) << 4) + (t & 1) * 8);
+                const uint2 w1 = *reinterpret_cast<const uint2*>(wt + R1 * 128 + ((cidx ^ (R1 & 7)) << 4) + (t & 1) * 8);
+#pragma unroll
+                for (int kk = 0; kk < 4; kk++) {
+                    A[u][kk][0] = lop3_and_or(w0.x >> (4 * kk), 0x000F000Fu, 0x43004300u);
+                    A[u][kk][1] = lop3_and_or(w1.x >> (4 * kk), 0x000F000Fu, 0x43004300u);
+                    A[u][kk][2] = lop3_and_or(w0.y >> (4 * kk), 0x000F000Fu, 0x43004300u);
+                    A[u][kk][3] = lop3_and_or(w1.y >> (4 * kk), 0x000F000Fu, 0x43004300u);
+                }
+                const int gi = min(((kbf + u) >> p.gs_shift) - g_start, 7);
+                sr0[u] = __half2float(__low2half(half_at(s0, gi)));
+                sr1[u] = __half2float(__low2half(half_at(s1, gi)));
+                br0[u] = fmaf(-128.0f, sr0[u], __half2float(__low2half(half_at(c0, gi))));
+                br1[u] = fmaf(-128.0f, sr1[u], __half2float(__low2half(half_at(c1, gi))));
+            }
+#pragma unroll
+            for (int n = 0; n < NT; n++) {
+                // four independent MMA chains (one per group), interleaved
+                float D[4][4];
+                uint4 F0[4], F1[4];
+                float2 X[4];
+#pragma unroll
+                for (int u = 0; u < 4; u++) {
+                    const unsigned char* fb = xt + (size_t)(u * NT + n) * kFragBlock;
+                    F0[u] = *reinterpret_cast<const uint4*>(fb + lane * 32);
+                    F1[u] = *reinterpret_cast<const uint4*>(fb + lane * 32 + 16);
+                    X[u] = *reinterpret_cast<const float2*>(fb + 1024 + 8 * t);
+#pragma unroll
+                    for (int q = 0; q < 4; q++) D[u][q] = 0.0f;
+                }
+#pragma unroll
+                for (int kk = 0; kk < 4; kk++)
+#pragma unroll
+                    for (int u = 0; u < 4; u++) {
+                        const uint32_t b0 = kk == 0 ? F0[u].x : kk == 1 ? F0[u].z : kk == 2 ? F1[u].x : F1[u].z;
+                        const uint32_t b1 = kk == 0 ? F0[u].y : kk == 1 ? F0[u].w : kk == 2 ? F1[u].y : F1[u].w;
+                        mma_bf16_16816(D[u], A[u][kk][0], A[u][kk][1], A[u][kk][2], A[u][kk][3], b0, b1);
+                    }
+#pragma unroll
+                for (int u = 0; u < 4; u++) {
+                    if (u < nu) {  // D: (R0, col 2t), (R0, 2t+1), (R1, 2t), (R1, 2t+1)
+                        acc[n][0] = fmaf(sr0[u], D[u][0], fmaf(br0[u], X[u].x, acc[n][0]));
+                        acc[n][1] = fmaf(sr0[u], D[u][1], fmaf(br0[u], X[u].y, acc[n][1]));
+                        acc[n][2] = fmaf(sr1[u], D[u][2], fmaf(br1[u], X[u].x, acc[n][2]));
+                        acc[n][3] = fmaf(sr1[u], D[u][3], fmaf(br1[u], X[u].y, acc[n][3]));
+                    }
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(empty_bar(slot));
+            if (++slot == DW) {
+                slot = 0;
+                ph ^= 1u;
+            }
+        }
+    } else if (warp == kLoadWarp) {
+        if (lane == 0) {
+            const uint64_t pol_w = l2_policy_evict_first();
+            const uint64_t pol_x = l2_policy_evict_last();
+            bool waited = false;
+            int slot = 0;
+            uint32_t ph = 0;
+            for (int j = 0; j < nsb && !fail; j++) {
+                if (j >= DW && !mbar_wait_nap(empty_bar(slot), ph ^ 1u, kGemmWaitNs, 64)) {
+                    fail = true;
+                    break;
+                }
+                const uint32_t dst = w_base + (uint32_t)(slot * slot_bytes);
+                const int kbf = kb0 + 4 * j;
+                const int g_start = (kbf >> p.gs_shift) & ~7;
+                mbar_arrive_expect_tx(full_bar(slot),
+                                      (uint32_t)((p.sb_tma ? kWSlotBytes : kWTileBytes) + b_bytes));
+                tma_load_2d(dst, &tm_w, kbf * 8, row0, full_bar(slot), pol_w);
+                if (p.sb_tma) {
+                    tma_load_2d(dst + kWTileBytes, &tm_s, g_start, row0, full_bar(slot), pol_w);
+                    tma_load_2d(dst + kWTileBytes + kSTileBytes, &tm_b, g_start, row0, full_bar(slot), pol_w);
+                }
+                if (!waited) {
+                    pdl_wait();  // the fragment workspace is written by the preparation kernel
+                    waited = true;
+                }
+                bulk_load_g2s(dst + kWSlotBytes, p.xw + (size_t)(sb0 + j) * b_bytes, (uint32_t)b_bytes,
+                              full_bar(slot), pol_x);
+                if (++slot == DW) {
+                    slot = 0;
+                    ph ^= 1u;
+                }
+            }
+        }
+    }
+    if (fail && p.status) atomicOr(p.status, 1);
+
+    // ---- epilogue ------------------------------------------------------------------------
+    // lane (g, t) of warp w holds rows 16w+g, 16w+g+8 x columns (2t, 2t+1) of each tile:
+    // bf16 x: tokens 8n+2t, 8n+2t+1; fp32 x: token 4n+t (hi + lo columns added).
+    float* part = reinterpret_cast<float*>(sm);  // split-K partials [tokens][128], reuses the ring
+    const int tok_per_tile = p.xf32 ? 4 : 8;
+    const int tcap = NT * tok_per_tile;
+    if (warp < kAWarps) {
+        pdl_wait();
+        // the partials overwrite the ring: every consumer warp must be done
+        // reading it first (named barrier 1 over the consumer warps)
+        if (p.ks > 1) asm volatile("bar.sync 1, %0;" ::"r"(kAWarps * 32) : "memory");
+        const int R0 = warp * 16 + g, R1 = R0 + 8;
+#pragma unroll
+        for (int n = 0; n < NT; n++) {
+#pragma unroll
+            for (int hc = 0; hc < 2; hc++) {  // column 2t + hc
+                const int tok = p.xf32 ? n * 4 + t : n * 8 + 2 * t + hc;
+                if (p.xf32 && hc == 1) continue;
+                const float y0 = p.xf32 ? acc[n][0] + acc[n][1] : acc[n][hc];
+                const float y1 = p.xf32 ? acc[n][2] + acc[n][3] : acc[n][2 + hc];
+                if (p.ks == 1) {
+                    if (tok < p.m) {
+                        const int r[2] = {row0 + R0, row0 + R1};
+                        const float yv[2] = {y0, y1};
+#pragma unroll
+                        for (int q = 0; q < 2; q++) {
+                            if (r[q] < p.n_out) {
+                                const size_t o = (size_t)tok * p.n_out + r[q];
+                                float y = yv[q];
+                                if (p.row_add) y += p.row_add[r[q]];
+                                if (p.residual) y += p.residual[o];
+                                p.out[o] = y;
+                            }
+                        }
+                    }
+                } else {
+                    part[tok * kGemmRows + R0] = y0;
+                    part[tok * kGemmRows + R1] = y1;
+                }
+            }
+        }
+    }
+    __syncwarp();
+    if (p.ks > 1) {
+        cluster_sync();
+        const int mt = min(p.m, tcap);
+        const int t_lo = (int)((long long)kr * mt / p.ks), t_hi = (int)((long long)(kr + 1) * mt / p.ks);
+        const int n_el = (t_hi - t_lo) * kGemmRows;
+        for (int e = threadIdx.x; e < n_el; e += kGemmThreads) {
+            const int tk = t_lo + e / kGemmRows, rr = e % kGemmRows;
+            const int gr = row0 + rr;
+            const uint32_t off = (uint32_t)((tk * kGemmRows + rr) * 4);
+            float y = 0.0f;
+            for (int q = 0; q < p.ks; q++) y += ld_cluster_f32(map_to_rank(base + off, (uint32_t)q));
+            if (gr < p.n_out) {
+                const size_t o = (size_t)tk * p.n_out + gr;
+                if (p.row_add) y += p.row_add[gr];
+                if (p.residual) y += p.residual[o];
+                p.out[o] = y;
+            }
+        }
+        cluster_sync();
+    }
+}
+
+struct SmallPlan {
+    int nt, row_tiles, ks, bstages, wslots;
+    size_t smem, ws_bytes;
+};
+
+static size_t small_slot_bytes(int nt) { return ((size_t)kWSlotBytes + 4 * nt * kFragBlock + 1023) & ~(size_t)1023; }
+static size_t small_smem(int nt, int bstages, int wslots) {
+    (void)bstages;
+    return 1024 + (size_t)wslots * small_slot_bytes(nt) + 16 * (size_t)wslots + 16;
+}
+
+static SmallPlan plan_small(int n_out, int n_in, int m, bool xf32) {
+    SmallPlan pl{};
+    const int v = xf32 ? 2 * m : m;
+    pl.nt = v <= 8 ? 1 : v <= 16 ? 2 : v <= 32 ? 4 : 8;
+    pl.row_tiles = (n_out + kGemmRows - 1) / kGemmRows;
+    pl.wslots = 6;
+    pl.bstages = 6;
+    while (small_smem(pl.nt, pl.bstages, pl.wslots) > (size_t)kGemmSmemMax && pl.wslots > 2) {
+        pl.wslots--;
+        pl.bstages = pl.wslots;
+    }
+    pl.smem = small_smem(pl.nt, pl.bstages, pl.wslots);
+    const int sms = sm_count_gemm();
+    const int nsb = (n_in / 64 + 3) / 4;
+    int ks = 1;
+    if (pl.row_tiles < sms) ks = std::min({8, nsb, std::max(1, sms / pl.row_tiles)});
+    pl.ks = ks;
+    pl.ws_bytes = (size_t)nsb * 4 * pl.nt * kFragBlock;
+    return pl;
+}
+
+static bool use_small(int m, bool xf32) { return (xf32 ? 2 * m : m) <= 16; }
+
+template <int NT>
+static int launch_small_nt(const WeightMaps& wm, const SmallParams& prm, const SmallPlan& pl, cudaStream_t st) {
+    static bool attr_done[64] = {false};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return HQ4_ERR_LAUNCH;
+    if (!attr_done[dev]) {
+        if (cudaFuncSetAttribute(gemm_small_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmemMax) !=
+            cudaSuccess)
+            return HQ4_ERR_LAUNCH;
+        attr_done[dev] = true;
+    }
+    const int tcap = NT * (prm.xf32 ? 4 : 8);
+    if (pl.smem > (size_t)kGemmSmemMax || (size_t)tcap * kGemmRows * 4 > (size_t)pl.wslots * small_slot_bytes(NT))
+        return HQ4_ERR_SHAPE;
+    cudaLaunchAttribute attr[2];
+    int na = 0;
+    attr[na++] = pdl_attribute();
+    if (pl.ks > 1) {
+        attr[na].id = cudaLaunchAttributeClusterDimension;
+        attr[na].val.clusterDim.x = 1;
+        attr[na].val.clusterDim.y = (unsigned)pl.ks;
+        attr[na].val.clusterDim.z = 1;
+        na++;
+    }
+    cudaLaunchConfig_t lc = {};
+    lc.gridDim = dim3((unsigned)pl.row_tiles, (unsigned)pl.ks, 1);
+    lc.blockDim = dim3(kGemmThreads);
+    lc.dynamicSmemBytes = pl.smem;
+    lc.stream = st;
+    lc.attrs = attr;
+    lc.numAttrs = na;
+    return cudaLaunchKernelEx(&lc, gemm_small_kernel<NT>, wm.tw, wm.ts, wm.tb, prm) == cudaSuccess ? HQ4_OK
+                                                                                               : HQ4_ERR_LAUNCH;
+}
+
+static int launch_small(const void* x, bool xf32, unsigned char* ws, const WeightMaps& wm, SmallParams prm,
+                        const SmallPlan& pl, cudaStream_t st) {
+    const long long total = (long long)(prm.n_in >> 6) * pl.nt * 32;
+    const int blocks = (int)std::min<long long>((total + kPrepThreads - 1) / kPrepThreads, 4L * sm_count_gemm());
+    cudaLaunchAttribute attr[1] = {pdl_attribute()};
+    cudaLaunchConfig_t lc = {};
+    lc.gridDim = dim3((unsigned)blocks);
+    lc.blockDim = dim3(kPrepThreads);
+    lc.stream = st;
+    lc.attrs = attr;
+    lc.numAttrs = 1;
+    cudaError_t e = xf32 ? cudaLaunchKernelEx(&lc, gemm_xprep_frag_kernel<true>, x, ws, prm.m, prm.n_in, pl.nt,
+                                              prm.status)
+                         : cudaLaunchKernelEx(&lc, gemm_xprep_frag_kernel<false>, x, ws, prm.m, prm.n_in, pl.nt,
+                                              prm.status);
+    if (e != cudaSuccess) return HQ4_ERR_LAUNCH;
+    switch (pl.nt) {
+        case 1: return launch_small_nt<1>(wm, prm, pl, st);
+        case 2: return launch_small_nt<2>(wm, prm, pl, st);
+        case 4: return launch_small_nt<4>(wm, prm, pl, st);
+        default: return launch_small_nt<8>(wm, prm, pl, st);
+    }
+}
+
 }  // namespace hq4
 
 using namespace hq4;
@@ -798,7 +1251,12 @@ static bool gemm_shape_ok(int n_out, int n_in, int gs, int m) {
 
 extern "C" long long hq4_gemm_workspace_bytes(int n_out, int n_in, int m) {
     if (n_out <= 0 || n_in <= 0 || m <= 0 || n_in % 64) return HQ4_ERR_SHAPE;
-    return (long long)plan_gemm(n_out, n_in, m).ws_bytes;
+    // enough for either activation type
+    size_t need = 0;
+    for (int f = 0; f < 2; f++)
+        need = std::max(need, use_small(m, f != 0) ? plan_small(n_out, n_in, m, f != 0).ws_bytes
+                                                   : plan_gemm(n_out, n_in, m).ws_bytes);
+    return (long long)need;
 }
 
 extern "C" int hq4_gemm_w4a16(const uint32_t* w, const uint16_t* scales, const uint16_t* biases, const void* x,
@@ -810,14 +1268,42 @@ extern "C" int hq4_gemm_w4a16(const uint32_t* w, const uint16_t* scales, const u
     if (((uintptr_t)w & 31) || ((uintptr_t)x & 15) || ((uintptr_t)out & 3) || ((uintptr_t)scales & 1) ||
         ((uintptr_t)biases & 1) || ((uintptr_t)workspace & 127))
         return HQ4_ERR_ALIGN;
+    const bool xf32 = x_is_f32 != 0;
+    const bool small = use_small(m, xf32);
     const GemmPlan pl = plan_gemm(n_out, n_in, m);
-    if (!workspace || workspace_bytes < (long long)pl.ws_bytes) return HQ4_ERR_SHAPE;
+    const SmallPlan sp = plan_small(n_out, n_in, m, xf32);
+    if (!workspace || workspace_bytes < (long long)(small ? sp.ws_bytes : pl.ws_bytes)) return HQ4_ERR_SHAPE;
     int* status = status_word();
     if (!status) return HQ4_ERR_LAUNCH;
     WeightMaps wm;
     if (!weight_maps(w, scales, biases, n_out, n_in, n_in / gs, &wm)) return HQ4_ERR_LAUNCH;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     unsigned char* ws = static_cast<unsigned char*>(workspace);
+    int gsh = 0;
+    while ((64 << gsh) < gs) gsh++;
+    if (small) {
+        SmallParams sprm{};
+        sprm.xw = ws;
+        sprm.out = out;
+        sprm.row_add = row_add;
+        sprm.residual = residual;
+        sprm.n_out = n_out;
+        sprm.n_in = n_in;
+        sprm.m = m;
+        sprm.nkb = n_in / 64;
+        sprm.ks = sp.ks;
+        sprm.nt = sp.nt;
+        sprm.xf32 = xf32 ? 1 : 0;
+        sprm.gs_shift = gsh;
+        sprm.bstages = sp.bstages;
+        sprm.wslots = sp.wslots;
+        sprm.sb_tma = wm.sb_tma ? 1 : 0;
+        sprm.n_sg = n_in / gs;
+        sprm.sc = scales;
+        sprm.bi = biases;
+        sprm.status = status;
+        return launch_small(x, xf32, ws, wm, sprm, sp, st);
+    }
     if (int rc = launch_xprep(x, x_is_f32 != 0, ws, m, pl, n_in, status, st)) return rc;
     GemmParams prm{};
     prm.xw = ws;
@@ -847,8 +1333,19 @@ extern "C" int hq4_gemm_w4a16(const uint32_t* w, const uint16_t* scales, const u
 }
 
 extern "C" int hq4_gemm_plan(int n_out, int n_in, int m, int x_is_f32, int* info) {
-    (void)x_is_f32;
     if (n_out <= 0 || n_in <= 0 || m <= 0 || n_in % 64 || !info) return HQ4_ERR_SHAPE;
+    if (use_small(m, x_is_f32 != 0)) {
+        const SmallPlan sp = plan_small(n_out, n_in, m, x_is_f32 != 0);
+        info[0] = sp.row_tiles;
+        info[1] = sp.ks;
+        info[2] = 1;
+        info[3] = sp.nt * 8;
+        info[4] = sp.bstages;
+        info[5] = (int)sp.smem;
+        info[6] = sp.wslots;
+        info[7] = 1;  // register-path MMAs
+        return HQ4_OK;
+    }
     const GemmPlan pl = plan_gemm(n_out, n_in, m);
     info[0] = pl.row_tiles;
     info[1] = pl.ks;
@@ -857,6 +1354,6 @@ extern "C" int hq4_gemm_plan(int n_out, int n_in, int m, int x_is_f32, int* info
     info[4] = pl.stages;
     info[5] = (int)pl.smem;
     info[6] = pl.wslots;
-    info[7] = kGemmThreads;
+    info[7] = 0;  // tcgen05 / TMEM
     return HQ4_OK;
 }

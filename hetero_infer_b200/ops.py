@@ -170,5 +170,7 @@ def gemm_plan(n_out: int, n_in: int, m: int, x_is_f32: bool = False) -> dict:
     lib = _lib.load()
     info = (ctypes.c_int * 8)()
     _lib.check(lib.hq4_gemm_plan(n_out, n_in, m, 1 if x_is_f32 else 0, info), "hq4_gemm_plan")
-    keys = ("row_tiles", "ksplit", "token_tiles", "tile_tokens", "stages", "smem", "weight_slots", "threads")
-    return dict(zip(keys, list(info)))
+    keys = ("row_tiles", "ksplit", "token_tiles", "tile_tokens", "stages", "smem", "weight_slots", "kernel")
+    d = dict(zip(keys, list(info)))
+    d["kernel"] = "mma.sync" if d["kernel"] == 1 else "tcgen05"
+    return d

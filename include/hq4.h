@@ -78,9 +78,12 @@ int hq4_dequant(const uint32_t* w, const uint16_t* scales, const uint16_t* biase
  * Replaces QLinear._gemm (hetero/cpu_model.py:118-136: q4_dequant of 512-row
  * blocks, kernel/q4gemv.c:311-379, then a BLAS matmul).  Weight layout as
  * hq4_gemv; x is [m][n_in] bf16 (x_is_f32 = 0) or fp32 (x_is_f32 = 1), 16-byte
- * aligned; out fp32 [m][n_out].  Weights are rounded once to fp16 and x is
- * converted to fp16 (exact for bf16 x with |x| < 65520; larger magnitudes set
- * status bit 2); products and sums are fp32.  gs must be a power of two >= 64
+ * aligned; out fp32 [m][n_out].  Up to 16 bf16 (8 fp32) tokens the weights
+ * stay exact (128+q in bf16 MMAs, the scale and bias folded per group in
+ * fp32) and fp32 x is carried as bf16 hi + lo (16 significant bits); above,
+ * the tcgen05 kernel rounds the weights once to fp16 and converts x to fp16
+ * (exact for bf16 x with |x| < 65520; larger magnitudes set status bit 2).
+ * Products and sums are fp32.  gs must be a power of two >= 64
  * dividing n_in (the reference's AVX2 build has the same gs % 64 rule,
  * q4gemv.c:234-240), else -1.
  * `workspace` (caller-owned, 128-byte aligned, at least
@@ -98,9 +101,11 @@ int hq4_gemm_w4a16(const uint32_t* w, const uint16_t* scales, const uint16_t* bi
 long long hq4_gemm_workspace_bytes(int n_out, int n_in, int m);
 
 /* Launch plan hq4_gemm_w4a16 would use (no launch): info[0..7] = row tiles,
- * K-split cluster size, token tiles, tokens per tile, pipeline stages, shared
- * memory bytes, packed-weight ring slots, threads per CTA.  No reference
- * counterpart. */
+ * K-split cluster size, token tiles, tokens per tile, activation stages,
+ * shared memory bytes, packed-weight ring slots, kernel (0: tcgen05 with the
+ * A operand in TMEM, for larger token counts; 1: warp-level MMAs with the
+ * weights exact as 128+q in bf16, for up to 16 bf16 / 8 fp32 tokens).
+ * No reference counterpart. */
 int hq4_gemm_plan(int n_out, int n_in, int m, int x_is_f32, int* info);
 
 /* ---- qwen2 stage forward (hetero/cpu_model.py:164-368) ---------------------

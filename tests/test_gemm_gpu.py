@@ -1,12 +1,14 @@
 """W4A16 tcgen05 GEMM (hq4_gemm_w4a16) on the GPU.
 
-Two references per case:
-* exact: the product it is defined to compute -- weights rounded once to fp16
-  (fp16(q*s+b)), activations converted to fp16 -- in float64 (torch on the
-  device).  Only fp32 accumulation order separates the two: <= 1e-5.
-* spec: the reference's float path, out = x . (q*s+b)^T in full precision
-  (hetero/cpu_model.py QLinear, kernel/q4gemv.c:113-139 per token).  The bar
-  is the north star's 1e-3 relative L2; fp16 weight rounding costs ~3e-4.
+Two kernels sit behind the entry point (hq4_gemm_plan says which):
+* register path (up to 16 bf16 / 8 fp32 tokens): weights exact, fp32 x as
+  bf16 hi + lo -- checked against the full-precision product (the
+  reference's float path, out = x . (q*s+b)^T, hetero/cpu_model.py QLinear,
+  kernel/q4gemv.c:113-139 per token) to 2e-5 (bf16 x) / 5e-5 (fp32 x);
+* tcgen05 path: weights rounded once to fp16, x to fp16 -- checked against
+  that exact fp16-operand product in float64 (<= 1e-5: only fp32
+  accumulation order differs) and against the full-precision product at the
+  north star's 1e-3 relative L2 (fp16 weight rounding costs ~3e-4).
 """
 import numpy as np
 import pytest
@@ -69,6 +71,9 @@ SHAPES = [
     (3584, 18944, 4, 64, "bf16"),
     (4608, 3584, 48, 256, "f32"),
     (3584, 3584, 128, 64, "f32"),
+    (1024, 2048, 6, 64, "f32"),           # register path, hi/lo tokens
+    (2048, 4096, 32, 64, "bf16"),         # tcgen05 path, 32 tokens
+    (3584, 18944, 7, 128, "f32"),         # register path, K split, gs 128
 ]
 
 
@@ -83,9 +88,13 @@ def test_gemm_matches_exact_and_reference(cuda, ci):
     y = ops.q4_gemm(dw, ds, db, x, gs)
     torch.cuda.synchronize()
     exact, spec = _refs(dw, ds, db, x, gs)
+    plan = ops.gemm_plan(n_out, n_in, m, xd == "f32")
     e1, e2 = rel_l2(y, exact), rel_l2(y, spec)
-    assert e1 <= EXACT_TOL, f"{SHAPES[ci]}: vs fp16-operand product {e1:.2e} (plan {ops.gemm_plan(n_out, n_in, m, xd == 'f32')})"
-    assert e2 <= SPEC_TOL, f"{SHAPES[ci]}: vs reference {e2:.2e}"
+    if plan["kernel"] == "mma.sync":
+        assert e2 <= (5e-5 if xd == "f32" else 2e-5), f"{SHAPES[ci]}: vs full precision {e2:.2e} ({plan})"
+    else:
+        assert e1 <= EXACT_TOL, f"{SHAPES[ci]}: vs fp16-operand product {e1:.2e} ({plan})"
+        assert e2 <= SPEC_TOL, f"{SHAPES[ci]}: vs reference {e2:.2e}"
     y2 = ops.q4_gemm(dw, ds, db, x, gs)
     torch.cuda.synchronize()
     assert torch.equal(y, y2), "not deterministic"
@@ -102,8 +111,8 @@ def test_gemm_row_add_residual_and_reference_oracle(cuda, oracle):
     ra = torch.randn(n_out, device="cuda")
     res = torch.randn(m, n_out, device="cuda")
     y = ops.q4_gemm(dw, ds, db, x, gs, row_add=ra, residual=res)
-    exact, _ = _refs(dw, ds, db, x, gs)
-    assert rel_l2(y, exact + ra.double() + res.double()) <= EXACT_TOL
+    _, spec = _refs(dw, ds, db, x, gs)
+    assert rel_l2(y, spec + ra.double() + res.double()) <= 2e-5
     w = dw.cpu().numpy().view(np.uint32)
     s = ds.cpu().numpy()
     b = db.cpu().numpy()
@@ -122,7 +131,7 @@ def test_gemm_error_codes(cuda):
     out = torch.empty(8, 256, device="cuda")
     st = torch.cuda.current_stream().cuda_stream
     need = lib.hq4_gemm_workspace_bytes(256, 512, 8)
-    assert need == 16 * 512 * 2          # one 16-token tile of fp16 activations
+    assert 0 < need <= 1 << 20
     ws = torch.empty(need, dtype=torch.uint8, device="cuda")
     call = lambda xp, gs, n_in=512, wsb=need: lib.hq4_gemm_w4a16(
         dw.data_ptr(), ds.data_ptr(), db.data_ptr(), xp, 0, out.data_ptr(), 256, n_in, gs, 8, None, None,
@@ -130,7 +139,7 @@ def test_gemm_error_codes(cuda):
     assert call(x.data_ptr(), 32) == -1          # gs below 64 (q4gemv.c:234-240 AVX2 rule)
     assert call(x.data_ptr(), 96) == -1          # not a power of two
     assert call(x.data_ptr(), 64, n_in=500) == -1
-    assert call(x.data_ptr(), 64, wsb=need - 1) == -1   # workspace too small
+    assert call(x.data_ptr(), 64, wsb=1024) == -1       # workspace too small
     assert call(x.data_ptr() + 2, 64) == -2      # x not 16-byte aligned
     assert call(x.data_ptr(), 64) == 0
     torch.cuda.synchronize()
@@ -139,11 +148,14 @@ def test_gemm_error_codes(cuda):
 
 @pytest.mark.gpu
 def test_gemm_range_flag(cuda):
-    """bf16 activations beyond fp16 range set status bit 2 (no silent inf)."""
+    """The tcgen05 path carries x in fp16: bf16 activations beyond fp16 range
+    set status bit 2 (no silent inf).  The register path keeps bf16 and
+    computes such inputs exactly, with no flag."""
     import torch
     from hetero_infer_b200 import _lib, ops
     lib = _lib.load()
-    dw, ds, db, x = _case(256, 512, 8, 64, seed=2, x_dtype=torch.bfloat16)
+    dw, ds, db, x = _case(256, 512, 80, 64, seed=2, x_dtype=torch.bfloat16)
+    assert ops.gemm_plan(256, 512, 80)["kernel"] == "tcgen05"
     lib.hq4_device_status(1)
     ops.q4_gemm(dw, ds, db, x, 64)
     torch.cuda.synchronize()
@@ -152,6 +164,13 @@ def test_gemm_range_flag(cuda):
     ops.q4_gemm(dw, ds, db, x, 64)
     torch.cuda.synchronize()
     assert lib.hq4_device_status(1) & 4
+    xs = x[:8].contiguous()
+    assert ops.gemm_plan(256, 512, 8)["kernel"] == "mma.sync"
+    y = ops.q4_gemm(dw, ds, db, xs, 64)
+    torch.cuda.synchronize()
+    assert lib.hq4_device_status(1) & 4 == 0
+    _, spec = _refs(dw, ds, db, xs, 64)
+    assert rel_l2(y, spec) <= 2e-5
 
 
 @pytest.mark.gpu
@@ -170,7 +189,8 @@ def test_gemm_back_to_back_calls(cuda, shape):
         for dw, ds, db, x in cases:
             outs.append(ops.q4_gemm(dw, ds, db, x, 64, workspace=ws))
     torch.cuda.synchronize()
+    small = ops.gemm_plan(n_out, n_in, m)["kernel"] == "mma.sync"
     for j, y in enumerate(outs):
         dw, ds, db, x = cases[j % 3]
-        exact, _ = _refs(dw, ds, db, x, 64)
-        assert rel_l2(y, exact) <= EXACT_TOL, f"call {j}"
+        exact, spec = _refs(dw, ds, db, x, 64)
+        assert rel_l2(y, spec if small else exact) <= (2e-5 if small else EXACT_TOL), f"call {j}"
