@@ -73,6 +73,18 @@ def measured_peak():
         return FALLBACK_HBM_GBS, "fallback"
 
 
+def measured_tensor_peak() -> float:
+    """Dense bf16 tensor-core peak in TFLOP/s: the burst cuBLAS figure from
+    MEASURED_PEAKS.json, else the fallback measurement on this pool."""
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return float(d["bf16_tflops"])
+    except (OSError, ValueError, KeyError):
+        return 1590.0
+
+
 def profiled_traffic():
     """DRAM bytes per GEMV launch of the layer step, from the committed ncu
     summary (profiles/gemv_m1_layer_step.md), or None."""
@@ -263,6 +275,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         if not args.no_extras:
             result["per_projection"] = per_projection(lib, dev, gen, stream, q4_on_device)
             result["gemv_3584x18944"] = result["per_projection"]["gate"]
+            result["gemm_w4a16"] = gemm_bench(lib, dev, gen, stream, q4_on_device)
             result["e2e"] = e2e_qlinear(args, dev, cuda_model, synth, np)
             if world == 1:
                 result["decode"] = decode_bench(dev)
@@ -286,6 +299,7 @@ def per_projection(lib, dev, gen, stream, q4_on_device, launches_per=200):
         ws = [q4_on_device(n, k) for _ in range(reps)]
         x = torch.randn(1, k, device=dev, generator=gen)
         y = torch.empty(1, n, device=dev)
+        torch.cuda.synchronize(dev)  # generated on the default stream, timed on `stream`
 
         def one(i):
             w, s, b = ws[i % reps]
@@ -315,6 +329,75 @@ def per_projection(lib, dev, gen, stream, q4_on_device, launches_per=200):
         out[name] = {"shape": f"{n}x{k}", "us": round(us, 3), "GB/s": round(gbs, 1),
                      "frac": round(gbs / peak, 4), "frac_of_8000": round(gbs / 8000.0, 4),
                      "bytes": nbytes}
+        del ws
+    return out
+
+
+def gemm_bench(lib, dev, gen, stream, q4_on_device, launches=60):
+    """Benchmark config 3: gate/up (18944x3584) and down (3584x18944) at
+    M = 1, 4, 16, 64, 256 tokens of bf16 activations through hq4_gemm_w4a16
+    (the register-path kernel up to 16 tokens, tcgen05/TMEM above), fp32
+    out; M = 1 also through the decode GEMV (x as fp32, exact).  Rotating
+    weight copies > L2; CUDA events around graph replays.  Roofline: HBM for
+    every M (algorithmic bytes = packed weights + scales/biases + x + out),
+    and the tensor peak (2 M N K flops) beside it."""
+    import torch
+    from hetero_infer_b200 import _lib, ops
+    hbm_peak, _ = measured_peak()
+    tc_peak = measured_tensor_peak()
+    out = {}
+    for name, n, k in (("gate_up", 18944, 3584), ("down", 3584, 18944)):
+        nbytes_w = n * k // 2 + n * (k // 64) * 4
+        reps = max(2, -(-400_000_000 // nbytes_w))
+        ws = [q4_on_device(n, k) for _ in range(reps)]
+        torch.cuda.synchronize(dev)
+        for m in (1, 4, 16, 64, 256):
+            x = torch.randn(m, k, device=dev, generator=gen).to(torch.bfloat16)
+            xf = x.float()
+            y = torch.empty(m, n, device=dev)
+            work = ops.gemm_workspace(n, k, m, dev)
+            torch.cuda.synchronize(dev)
+            plan = ops.gemm_plan(n, k, m)
+            variants = [("gemm", plan["kernel"])] + ([("gemv", "gemv_m1")] if m == 1 else [])
+            row = {}
+            for label, kern in variants:
+                def one(i):
+                    w, s_, b_ = ws[i % reps]
+                    if label == "gemm":
+                        _lib.check(lib.hq4_gemm_w4a16(w.data_ptr(), s_.data_ptr(), b_.data_ptr(), x.data_ptr(), 0,
+                                                      y.data_ptr(), n, k, GS, m, None, None, work.data_ptr(),
+                                                      work.numel(), stream.cuda_stream), "hq4_gemm_w4a16")
+                    else:
+                        _lib.check(lib.hq4_gemv(w.data_ptr(), s_.data_ptr(), b_.data_ptr(), xf.data_ptr(),
+                                                y.data_ptr(), n, k, GS, 1, stream.cuda_stream), "hq4_gemv")
+                with torch.cuda.stream(stream):
+                    for i in range(reps):
+                        one(i)
+                    torch.cuda.synchronize(dev)
+                    g = torch.cuda.CUDAGraph()
+                    with torch.cuda.graph(g, stream=stream):
+                        for i in range(reps * 2):
+                            one(i)
+                    g.replay()
+                    torch.cuda.synchronize(dev)
+                    n_rep = max(1, launches // (reps * 2))
+                    e0 = torch.cuda.Event(enable_timing=True)
+                    e1 = torch.cuda.Event(enable_timing=True)
+                    e0.record(stream)
+                    for _ in range(n_rep):
+                        g.replay()
+                    e1.record(stream)
+                torch.cuda.synchronize(dev)
+                us = e0.elapsed_time(e1) * 1e3 / (n_rep * reps * 2)
+                xb = m * k * (2 if label == "gemm" else 4)
+                nbytes = nbytes_w + xb + m * n * 4
+                gbs = nbytes / (us * 1e-6) / 1e9
+                tf = 2.0 * m * n * k / (us * 1e-6) / 1e12
+                row[label] = {"kernel": kern, "us": round(us, 3), "GB/s": round(gbs, 1),
+                              "hbm_frac": round(gbs / hbm_peak, 4), "TFLOP/s": round(tf, 1),
+                              "tensor_frac": round(tf / tc_peak, 4)}
+                del g
+            out[f"{name}_m{m}"] = row
         del ws
     return out
 
