@@ -198,6 +198,74 @@ __global__ void __launch_bounds__(kArgmaxThreads) argmax_kernel(const float* __r
     }
 }
 
+// One shard's greedy pick as a pair for an all-gather across ranks: the
+// numpy-order best of x[0..n) as (float bits, offset + index).
+__global__ void __launch_bounds__(kArgmaxThreads) argmax_pair_kernel(const float* __restrict__ x, int n,
+                                                                     int offset, int* __restrict__ pair) {
+    __shared__ float bv[kArgmaxThreads / 32];
+    __shared__ int bi[kArgmaxThreads / 32];
+    pdl_launch_dependents();
+    pdl_wait();
+    float best = -INFINITY;
+    int bidx = 0x7fffffff;
+    for (int i = threadIdx.x; i < n; i += kArgmaxThreads) {
+        const float v = x[i];
+        if (argmax_before(v, i, best, bidx)) {
+            best = v;
+            bidx = i;
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bidx, o);
+        if (argmax_before(ov, oi, best, bidx)) {
+            best = ov;
+            bidx = oi;
+        }
+    }
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (lane == 0) {
+        bv[warp] = best;
+        bi[warp] = bidx;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        best = bv[0];
+        bidx = bi[0];
+        for (int j = 1; j < kArgmaxThreads / 32; j++)
+            if (argmax_before(bv[j], bi[j], best, bidx)) {
+                best = bv[j];
+                bidx = bi[j];
+            }
+        pair[0] = __float_as_int(best);
+        pair[1] = offset + bidx;
+    }
+}
+
+// The global greedy token from `world` shard pairs (value bits, global
+// index): numpy argmax over the whole vocabulary (first NaN, else the largest
+// value, lowest index among equals).  Optionally also recorded in
+// history[slot].
+__global__ void pick_token_kernel(const int* __restrict__ pairs, int world, int* __restrict__ tok,
+                                  int* __restrict__ history, int slot) {
+    pdl_launch_dependents();
+    pdl_wait();
+    if (threadIdx.x != 0) return;
+    float best = -INFINITY;
+    int bidx = 0x7fffffff;
+    for (int w = 0; w < world; w++) {
+        const float v = __int_as_float(pairs[2 * w]);
+        const int i = pairs[2 * w + 1];
+        if (argmax_before(v, i, best, bidx)) {
+            best = v;
+            bidx = i;
+        }
+    }
+    *tok = bidx;
+    if (history) history[slot] = bidx;
+}
+
 __global__ void advance_kernel(int* pos, int delta) {
     pdl_launch_dependents();
     pdl_wait();
@@ -245,6 +313,20 @@ extern "C" int hq4_argmax(const float* x, int n, int* idx_out, int* history, int
     if (history && (!pos || hist_len <= 0)) return HQ4_ERR_SHAPE;
     return launch_pdl(argmax_kernel, dim3(1), dim3(kArgmaxThreads), 0, static_cast<cudaStream_t>(stream),
                       x, n, idx_out, history, hist_len, pos, val_out);
+}
+
+extern "C" int hq4_argmax_pair(const float* x, int n, int offset, int* pair, void* stream) {
+    if (int rc = check_device_cap()) return rc;
+    if (n <= 0 || !pair) return HQ4_ERR_SHAPE;
+    return launch_pdl(argmax_pair_kernel, dim3(1), dim3(kArgmaxThreads), 0, static_cast<cudaStream_t>(stream), x,
+                      n, offset, pair);
+}
+
+extern "C" int hq4_pick_token(const int* pairs, int world, int* tok, int* history, int slot, void* stream) {
+    if (int rc = check_device_cap()) return rc;
+    if (world <= 0 || !tok || (history && slot < 0)) return HQ4_ERR_SHAPE;
+    return launch_pdl(pick_token_kernel, dim3(1), dim3(32), 0, static_cast<cudaStream_t>(stream), pairs, world, tok,
+                      history, slot);
 }
 
 extern "C" int hq4_advance_position(int* pos, int delta, void* stream) {

@@ -279,6 +279,18 @@ class Stage:
 
     # -- pieces ------------------------------------------------------------
     def embed(self, ids) -> torch.Tensor:
+        if isinstance(ids, torch.Tensor) and ids.is_cuda:
+            # token ids already on the device (a sampled token): no host round
+            # trip; the kernel zeroes rows of out-of-range ids and flags them
+            if self.embed_table is None:
+                raise NotImplementedError("device token ids need the fp16 embedding table")
+            d_ids = ids.reshape(-1).to(torch.int32).contiguous()
+            n = d_ids.numel()
+            out = torch.empty((n, self.H), dtype=torch.float32, device=self.device)
+            self._check(self.lib.hq4_embed_f16(self.embed_table.data_ptr(), d_ids.data_ptr(), n, self.H,
+                                               self.embed_table.shape[0], out.data_ptr(), self._stream()),
+                        "hq4_embed_f16")
+            return out.view(*ids.shape, self.H)
         ids_np = np.asarray(ids).reshape(-1).astype(np.int32)
         n = ids_np.size
         out = torch.empty((n, self.H), dtype=torch.float32, device=self.device)

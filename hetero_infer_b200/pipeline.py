@@ -115,11 +115,36 @@ class PipelineRank:
       head(h32) -> (max value, global index) of this rank's vocabulary shard.
     """
 
-    def __init__(self, comm: Comm, compute, n_micro: int):
+    def __init__(self, comm: Comm, compute, n_micro: int, max_tokens: int = 4096):
         self.comm, self.c, self.n_micro = comm, compute, n_micro
         self.caches = [compute.new_cache() for _ in range(n_micro)]
-        self.tokens: List[List[int]] = [[] for _ in range(n_micro)]
         self.ticks = 0
+        # Device compute keeps the sampled tokens on the device (a history per
+        # microbatch, read back once by `tokens`); no host sync per tick.
+        self.on_device = getattr(compute, "device_tokens", False)
+        if self.on_device:
+            self.hist = torch.zeros((n_micro, max_tokens), dtype=torch.int32, device=comm.device)
+            self.count = [0] * n_micro
+        else:
+            self._tokens: List[List[int]] = [[] for _ in range(n_micro)]
+
+    @property
+    def tokens(self) -> List[List[int]]:
+        if self.on_device:
+            h = self.hist.cpu().numpy()
+            return [[int(v) for v in h[m, :self.count[m]]] for m in range(self.n_micro)]
+        return self._tokens
+
+    def _record(self, m: int, tok) -> None:
+        if self.on_device:
+            self.count[m] += 1
+        else:
+            self._tokens[m].append(tok)
+
+    def _last_token(self, m: int):
+        if self.on_device:
+            return self.hist[m, self.count[m] - 1:self.count[m]].view(1, 1)
+        return np.array([[self._tokens[m][-1]]])
 
     @property
     def first(self) -> bool:
@@ -129,13 +154,19 @@ class PipelineRank:
     def last(self) -> bool:
         return self.comm.rank == self.comm.world - 1
 
-    def _head(self, h_last) -> int:
+    def _head(self, h_last, m: int):
         """Broadcast the last stage's final hidden state, row-sharded head,
-        all-gather of (max, index) -> the token (identical on every rank)."""
+        all-gather of (max, index) -> the token of microbatch m (identical on
+        every rank).  Device compute: the token goes straight into the device
+        history; host compute: returned as an int."""
         H = self.c.hidden_dim
         buf = self.c.to_comm32(h_last) if self.last else torch.empty(H, dtype=torch.float32,
                                                                         device=self.comm.device)
         self.comm.broadcast(buf, self.comm.world - 1)
+        if self.on_device:
+            pairs = self.comm.all_gather(self.c.head_pair(buf))
+            self.c.pick_into(pairs, self.comm.world, self.hist[m], self.count[m])
+            return None
         val, idx = self.c.head(buf)
         pair = torch.tensor([val, float(idx)], dtype=torch.float64, device=self.comm.device)
         return pick_token(self.comm.all_gather(pair))
@@ -159,8 +190,7 @@ class PipelineRank:
                     wire_in = torch.empty((1, P, self.c.hidden_dim), dtype=self.c.wire_dtype,
                                           device=self.comm.device)
                     self.comm.exchange(None, wire_in)
-            tok = self._head(h if self.last else None)
-            self.tokens[m].append(tok)
+            self._record(m, self._head(h if self.last else None, m))
 
     def decode(self, n_steps: int) -> None:
         """n_steps more tokens for every microbatch, pipelined."""
@@ -180,17 +210,14 @@ class PipelineRank:
             out_prev = None
             h = None
             if mine >= 0:
-                if self.first:
-                    h = self.c.embed_forward(np.array([[self.tokens[mine][-1]]]), self.caches[mine])
-                else:
-                    h = self.c.forward(self.c.from_wire(recv), self.caches[mine])
+                src = self._last_token(mine) if self.first else recv
+                wire, h = self.c.decode_tick(mine, self.caches[mine], src, self.first, self.last)
                 if not self.last:
-                    out_prev = self.c.to_wire(h)
+                    out_prev = wire
             # head of the microbatch the last stage finished this tick
             done = adm[t - (W - 1)] if 0 <= t - (W - 1) < len(adm) else -1
             if done >= 0:
-                tok = self._head(h if self.last else None)
-                self.tokens[done].append(tok)
+                self._record(done, self._head(h if self.last else None, done))
         self.ticks += n_ticks
 
 
@@ -229,6 +256,9 @@ class DeviceCompute:
         self.logits = torch.empty(hi - lo, dtype=torch.float32, device=device)
         self.idx = torch.empty(1, dtype=torch.int32, device=device)
         self.val = torch.empty(1, dtype=torch.float32, device=device)
+        self.pair = torch.empty(2, dtype=torch.int32, device=device)
+        self.tok = torch.empty(1, dtype=torch.int32, device=device)
+        self._graphs = {}
         self.lib = _lib.load()
         self._check = _lib.check
 
@@ -241,6 +271,50 @@ class DeviceCompute:
     def forward(self, h, cache):
         return self.stage(h, cache, apply_head=False)
 
+    def decode_tick(self, m, cache, src, first: bool, last: bool):
+        """One decode token of microbatch m through this stage: token id (first
+        stage) or wire hidden state in, wire hidden state (or, on the last
+        stage, the final hidden row) out.  The first tick of a microbatch runs
+        eagerly and records the step as a CUDA graph (its KV cache and device
+        position are fixed per microbatch); later ticks copy the input into the
+        graph's buffer and replay it -- one launch instead of five per layer."""
+        g = self._graphs.get(m)
+        if g is None:
+            h = self.embed_forward(src, cache) if first else self.forward(self.from_wire(src), cache)
+            self._graphs[m] = self._capture(cache, first, last)
+            return (None if last else self.to_wire(h)), h
+        static_in, static_wire, static_h, graph = g
+        if cache.offset + 1 > cache.max_ctx:
+            raise ValueError(f"context {cache.offset + 1} exceeds max_ctx {cache.max_ctx}")
+        static_in.copy_(src.reshape(static_in.shape))
+        graph.replay()
+        cache.offset += 1  # the graph advanced the device position
+        return static_wire, static_h
+
+    def _capture(self, cache, first: bool, last: bool):
+        st = self.stage
+        H = self.hidden_dim
+        static_in = (torch.zeros((1, 1), dtype=torch.int32, device=self.device) if first
+                     else torch.zeros((1, 1, H), dtype=self.wire_dtype, device=self.device))
+        static_wire = None if last else torch.empty((1, 1, H), dtype=self.wire_dtype, device=self.device)
+        static_h = torch.empty((1, 1, H), dtype=torch.float32, device=self.device)
+        side = torch.cuda.Stream(self.device)
+        side.wait_stream(torch.cuda.current_stream(self.device))
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=side, capture_error_mode="thread_local"):
+            h = st.embed(static_in) if first else static_in.to(torch.float32)
+            h = h.reshape(1, H).contiguous()
+            for i in range(len(st.layers)):
+                st.layer_forward(i, h, cache, 1)
+            if len(st.layers):
+                st._check(st.lib.hq4_advance_position(cache.pos.data_ptr(), 1, st._stream()),
+                          "hq4_advance_position")
+            if static_wire is not None:
+                static_wire.copy_(h.view(1, 1, H).to(self.wire_dtype))
+            static_h.copy_(h.view(1, 1, H))
+        torch.cuda.current_stream(self.device).wait_stream(side)
+        return static_in, static_wire, static_h, graph
+
     def to_wire(self, h):
         return h.to(self.wire_dtype).contiguous()
 
@@ -249,6 +323,26 @@ class DeviceCompute:
 
     def to_comm32(self, h):
         return h.reshape(-1, self.hidden_dim)[-1].contiguous()
+
+    device_tokens = True
+
+    def head_pair(self, h32):
+        """This rank's shard of the vocabulary projection and its greedy pick as
+        an (value bits, global index) int32 pair on the device."""
+        st = torch.cuda.current_stream(self.device).cuda_stream
+        self._check(self.lib.hq4_gemv_norm(self.lm_w.data_ptr(), self.lm_s.data_ptr(), self.lm_b.data_ptr(),
+                                           h32.data_ptr(), self.logits.data_ptr(), self.hi - self.lo,
+                                           self.hidden_dim, self.gs, 1, self.norm_w.data_ptr(),
+                                           float(self.cfg["rms_norm_eps"]), 0, None, None, st), "head")
+        self._check(self.lib.hq4_argmax_pair(self.logits.data_ptr(), self.hi - self.lo, self.lo,
+                                             self.pair.data_ptr(), st), "argmax_pair")
+        return self.pair
+
+    def pick_into(self, pairs, world: int, history_row, slot: int):
+        """Global token from the gathered pairs, written to history_row[slot]."""
+        st = torch.cuda.current_stream(self.device).cuda_stream
+        self._check(self.lib.hq4_pick_token(pairs.data_ptr(), world, self.tok.data_ptr(), history_row.data_ptr(),
+                                            slot, st), "pick_token")
 
     def head(self, h32):
         from ._lib import expect
@@ -291,6 +385,10 @@ class OracleCompute:
 
     def forward(self, h, cache):
         return self.stage(h, cache, apply_head=False)
+
+    def decode_tick(self, m, cache, src, first: bool, last: bool):
+        h = self.embed_forward(src, cache) if first else self.forward(self.from_wire(src), cache)
+        return (None if last else self.to_wire(h)), h
 
     def to_wire(self, h):
         return torch.from_numpy(np.ascontiguousarray(np.asarray(h, dtype=np.float16)))

@@ -171,6 +171,18 @@ int hq4_argmax(const float* x, int n, int* idx_out, int* history, int hist_len, 
 int hq4_synth_embed_f16(long long seed, int vocab, int hidden, float std, uint16_t* out,
                         void* stream);
 
+/* One shard of a row-sharded greedy pick (hetero/backends.py:106-109 over a
+ * vocabulary split across ranks): pair[0] = float bits of the numpy-order best
+ * of x[0..n), pair[1] = offset + its index.  For an all-gather of pairs. */
+int hq4_argmax_pair(const float* x, int n, int offset, int* pair, void* stream);
+
+/* The greedy token from `world` gathered pairs (hq4_argmax_pair): numpy argmax
+ * over the whole vocabulary -- the first NaN, else the largest value with the
+ * lowest index.  Written to *tok and, when history is not NULL, to
+ * history[slot].  No reference counterpart (the reference samples one
+ * unsharded logits vector on the host). */
+int hq4_pick_token(const int* pairs, int world, int* tok, int* history, int slot, void* stream);
+
 /* *pos += delta on the device (advances the decode position inside a graph). */
 int hq4_advance_position(int* pos, int delta, void* stream);
 

@@ -90,3 +90,34 @@ def test_embed_rejects_out_of_range_ids(lib):
     assert lib.hq4_device_status(1) & 2
     assert lib.hq4_device_status(0) == 0
     assert lib.hq4_embed_f16(table.data_ptr(), ids.data_ptr(), 5, hidden, 0, out.data_ptr(), st) == -1
+
+
+@pytest.mark.gpu
+def test_argmax_pair_and_pick_token_match_numpy_over_shards(lib):
+    """Row-sharded greedy pick: per-shard pairs (value bits, global index) and
+    the pick over them equal np.argmax over the whole vector, NaN included."""
+    import torch
+    rng = np.random.default_rng(5)
+    st = torch.cuda.current_stream().cuda_stream
+    for trial in range(40):
+        n = int(rng.integers(8, 5000))
+        z = np.round(rng.standard_normal(n) * 3).astype(np.float32)
+        if trial % 4 == 1:
+            z[rng.integers(0, n, size=2)] = np.nan
+        elif trial % 4 == 2:
+            z[:] = -np.inf
+        world = int(rng.integers(1, 9))
+        pairs = torch.empty((world, 2), dtype=torch.int32, device="cuda")
+        d = torch.from_numpy(z).cuda()
+        for r in range(world):
+            lo, hi = n * r // world, n * (r + 1) // world
+            if hi == lo:
+                pairs[r, 0] = torch.tensor([np.float32(-np.inf)]).view(torch.int32)[0]
+                pairs[r, 1] = 2 ** 31 - 1
+                continue
+            assert lib.hq4_argmax_pair(d[lo:].data_ptr(), hi - lo, lo, pairs[r].data_ptr(), st) == 0
+        tok = torch.empty(1, dtype=torch.int32, device="cuda")
+        hist = torch.zeros(4, dtype=torch.int32, device="cuda")
+        assert lib.hq4_pick_token(pairs.data_ptr(), world, tok.data_ptr(), hist.data_ptr(), 2, st) == 0
+        torch.cuda.synchronize()
+        assert int(tok.item()) == int(z.argmax()) == int(hist[2].item()), (trial, world)
