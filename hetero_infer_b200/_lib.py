@@ -32,6 +32,7 @@ SIGNATURES = {
     "hq4_gemm_w4a16": (_I, [_P, _P, _P, _P, _I, _P, _I, _I, _I, _I, _P, _P, _P, _LL, _P]),
     "hq4_gemm_workspace_bytes": (_LL, [_I, _I, _I]),
     "hq4_gemm_plan": (_I, [_I, _I, _I, _I, _P]),
+    "hq4_gemm_w4a16_static": (_I, [_P, _P, _P, _P, _I, _P, _I, _I, _I, _I, _P, _P, _P]),
     "hq4_gemv_norm": (_I, [_P] * 5 + [_I] * 4 + [_P, _F, _I, _P, _P, _P]),
     "hq4_qkv_rope": (_I, [_P] * 4 + [_I] * 6 + [_P, _F, _P, _P, _P, _P, _I, _P, _P, _P, _P]),
     "hq4_attention": (_I, [_P] * 4 + [_I] * 4 + [_P, _I, _F, _P]),

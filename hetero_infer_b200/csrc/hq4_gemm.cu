@@ -1357,3 +1357,45 @@ extern "C" int hq4_gemm_plan(int n_out, int n_in, int m, int x_is_f32, int* info
     info[7] = 0;  // tcgen05 / TMEM
     return HQ4_OK;
 }
+
+// ---- allocation-free variant -------------------------------------------------
+// The same GEMM with its workspace taken from a fixed area of this module's
+// static device memory (one per device, allocated when the module loads), for
+// callers that cannot allocate device memory.  Every call on a device uses the
+// same area: calls queued on one stream are ordered and safe; calls that can
+// overlap (different streams, or host threads without a common stream) race
+// on it and must be serialised by the caller.
+static __device__ __align__(256) unsigned char g_hq4_gemm_scratch[HQ4_GEMM_STATIC_SCRATCH_BYTES];
+
+// Device address of g_hq4_gemm_scratch, resolved with cudaGetSymbolAddress
+// once per device (the first call may load the module, so it must not happen
+// while a stream is being captured); nullptr if the lookup fails.
+static void* static_scratch() {
+    static std::mutex mu;
+    static void* addr[64] = {nullptr};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+    std::lock_guard<std::mutex> lock(mu);
+    if (!addr[dev]) {
+        void* a = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&a, g_hq4_gemm_scratch);
+        if (e != cudaSuccess || !a) {
+            (void)cudaGetLastError();  // the failed lookup does not stick to later launches
+            return nullptr;
+        }
+        addr[dev] = a;
+    }
+    return addr[dev];
+}
+
+extern "C" int hq4_gemm_w4a16_static(const uint32_t* w, const uint16_t* scales, const uint16_t* biases,
+                                     const void* x, int x_is_f32, float* out, int n_out, int n_in, int gs,
+                                     int m, const float* row_add, const float* residual, void* stream) {
+    if (int rc = check_device_cap()) return rc;
+    const long long need = hq4_gemm_workspace_bytes(n_out, n_in, m);
+    if (need < 0 || need > (long long)HQ4_GEMM_STATIC_SCRATCH_BYTES) return HQ4_ERR_SHAPE;
+    void* ws = static_scratch();
+    if (!ws) return HQ4_ERR_LAUNCH;
+    return hq4_gemm_w4a16(w, scales, biases, x, x_is_f32, out, n_out, n_in, gs, m, row_add, residual, ws,
+                          (long long)HQ4_GEMM_STATIC_SCRATCH_BYTES, stream);
+}

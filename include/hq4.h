@@ -108,6 +108,21 @@ long long hq4_gemm_workspace_bytes(int n_out, int n_in, int m);
  * No reference counterpart. */
 int hq4_gemm_plan(int n_out, int n_in, int m, int x_is_f32, int* info);
 
+/* hq4_gemm_w4a16 without a caller workspace: the workspace is a fixed
+ * HQ4_GEMM_STATIC_SCRATCH_BYTES area of the library's static device memory,
+ * one per device, so the call allocates nothing and needs no buffer from the
+ * caller.  Shapes whose hq4_gemm_workspace_bytes(n_out, n_in, m) exceeds that
+ * size return -1.  All calls on a device share the area: calls ordered on one
+ * stream are safe; calls that can run at the same time (different streams,
+ * host threads without a common stream) race on it and must be serialised by
+ * the caller.  The first call on each device resolves the area's address
+ * (cudaGetSymbolAddress, which may load the module) and must be made outside
+ * stream capture.  No reference counterpart. */
+#define HQ4_GEMM_STATIC_SCRATCH_BYTES (16ll << 20)
+int hq4_gemm_w4a16_static(const uint32_t* w, const uint16_t* scales, const uint16_t* biases,
+                          const void* x, int x_is_f32, float* out, int n_out, int n_in, int gs,
+                          int m, const float* row_add, const float* residual, void* stream);
+
 /* ---- qwen2 stage forward (hetero/cpu_model.py:164-368) ---------------------
  * Hidden states, KV cache and attention are fp32 as in the reference's NumPy
  * stage.  `pos` is a device int: the position of the call's first token
