@@ -455,7 +455,8 @@ def pipeline_bench(rank: int, world: int, dev, n_micro: int, n_tokens: int = 256
     the `world` GPUs (NCCL send/recv of the fp16 hidden state between stages,
     lm_head row-sharded over all ranks), `n_micro` independent streams in
     flight, `n_tokens` per stream.  Aggregate decode tok/s over the pipelined
-    decode (device time, max over ranks)."""
+    decode: wall clock between two device synchronisations, max over ranks
+    (the work spans the compute stream and NCCL's streams)."""
     import torch
     import torch.distributed as dist
     from hetero_infer_b200 import pipeline, planner, synth
@@ -489,8 +490,8 @@ def pipeline_bench(rank: int, world: int, dev, n_micro: int, n_tokens: int = 256
                             "stream exceeds fp16 range at the cut, the fp16 wire carries inf, the next RMSNorm "
                             "NaN, and numpy argmax of NaN logits is 0 (tests/golden/golden_7b_pipe.json)")
             if zeros else "finite logits",
-            "timing": "host wall clock around the decode loop "
-            "(each tick synchronises on the sampled token), max over ranks"}
+            "timing": "host wall clock around the decode loop, device synchronised on both sides "
+            "(no host sync inside it: sampled tokens stay on the device), max over ranks"}
 
 
 def e2e_qlinear(args, dev, cuda_model, synth, np):
