@@ -1,6 +1,7 @@
 // Shared device helpers for the hq4 kernels (sm_100a only).
 #pragma once
 #include <cstdint>
+#include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
@@ -201,6 +202,14 @@ __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }
+// Initialise without the fence; the caller issues mbar_init_fence() once
+// after the last of several initialisations.
+__device__ __forceinline__ void mbar_init_nofence(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_init_fence() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
                  : "memory");
@@ -252,6 +261,19 @@ __device__ __forceinline__ bool mbar_wait_ns(uint32_t bar, uint32_t parity, uint
         if (globaltimer_ns() - t0 > limit_ns) return false;
     }
 }
+// Bounded wait without the timer (for hot loops): try_wait with a suspend-
+// time hint of hint_ns, at most `tries` times; false if none succeeded.
+__device__ __forceinline__ bool mbar_wait_tries(uint32_t bar, uint32_t parity, uint32_t hint_ns, int tries) {
+    for (int i = 0; i < tries; i++) {
+        uint32_t done;
+        asm volatile(
+            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
+            " selp.u32 %0, 1, 0, p;\n}\n"
+            : "=r"(done) : "r"(bar), "r"(parity), "r"(hint_ns) : "memory");
+        if (done) return true;
+    }
+    return false;
+}
 // Tight poll for the thread on the critical path (the MMA issuer): plain
 // try_wait, the timer read once every 1024 polls.
 __device__ __forceinline__ bool mbar_wait_spin(uint32_t bar, uint32_t parity, uint64_t limit_ns) {
@@ -273,6 +295,33 @@ __device__ __forceinline__ bool mbar_wait_nap(uint32_t bar, uint32_t parity, uin
         if (mbar_try(bar, parity)) return true;
         if (globaltimer_ns() - t0 > limit_ns) return false;
     }
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+// 2D tensor copy global -> this CTA's shared memory (no multicast), completing
+// on the mbarrier `bar`; (x, y) is the box origin in elements.  x times the
+// element size must be a multiple of 16 bytes.
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* tm, int x, int y, uint32_t bar,
+                                            uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(tm)), "r"(x), "r"(y), "r"(bar), "l"(policy)
+        : "memory");
+}
+// 3D tensor copy, as tma_load_2d with box origin (x, y, z).
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* tm, int x, int y, int z, uint32_t bar,
+                                            uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(tm)), "r"(x), "r"(y), "r"(z), "r"(bar), "l"(policy)
+        : "memory");
+}
+// Fetch a tensor map's descriptor ahead of its first use.
+__device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* tm) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tm)) : "memory");
 }
 __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");

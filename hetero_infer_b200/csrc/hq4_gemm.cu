@@ -55,6 +55,7 @@
 #include <mutex>
 
 #include "hq4_common.cuh"
+#include "hq4_tmap.cuh"
 #include "hq4.h"
 
 namespace hq4 {
@@ -157,23 +158,10 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16
 __device__ __forceinline__ void tmem_wait_st() {
     asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
-__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
-}
 __device__ __forceinline__ float ld_cluster_f32(uint32_t addr) {
     float v;
     asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
     return v;
-}
-// 2D tensor copy global -> this CTA's shared memory (no multicast), completing
-// on the mbarrier `bar`; (x, y) is the box origin in elements.
-__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* tm, int x, int y, uint32_t bar,
-                                            uint64_t policy) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
-        " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(dst),
-        "l"(reinterpret_cast<uint64_t>(tm)), "r"(x), "r"(y), "r"(bar), "l"(policy)
-        : "memory");
 }
 
 // Shared-memory matrix descriptor: K-major, 128-byte swizzle, rows of 128 B
@@ -648,38 +636,11 @@ static cudaLaunchAttribute pdl_attribute() {
     return a;
 }
 
-// ---- tensor maps (cuTensorMapEncodeTiled through the runtime's driver entry point)
-typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-static EncodeTiledFn encode_fn() {
-    static EncodeTiledFn fn = nullptr;
-    static bool tried = false;
-    if (!tried) {
-        tried = true;
-        void* f = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &f, 12000, cudaEnableDefault, &q) ==
-                cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<EncodeTiledFn>(f);
-    }
-    return fn;
-}
-
+// ---- tensor maps (hq4_tmap.cuh)
 // rows x cols 2D map of `elem`-byte elements, box (box_cols x 128 rows)
 static bool make_map(CUtensorMap* tm, const void* ptr, CUtensorMapDataType dt, int elem, long long rows,
                      long long cols, int box_cols, bool swizzle128) {
-    EncodeTiledFn fn = encode_fn();
-    if (!fn) return false;
-    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-    cuuint64_t strides[1] = {(cuuint64_t)(cols * elem)};
-    cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)kGemmRows};
-    cuuint32_t estr[2] = {1, 1};
-    return fn(tm, dt, 2, const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-              swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
-              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+    return make_map_2d(tm, ptr, dt, elem, rows, cols, box_cols, kGemmRows, swizzle128);
 }
 
 struct WeightMaps {

@@ -39,8 +39,12 @@
 //   producer of x is still draining.
 #include <algorithm>
 #include <cstdio>
+#include <functional>
+#include <mutex>
+#include <unordered_map>
 
 #include "hq4_common.cuh"
+#include "hq4_tmap.cuh"
 #include "hq4.h"
 
 namespace hq4 {
@@ -462,6 +466,357 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_m1_kernel(const GemvM1Pa
     }
 }
 
+// ---- streaming GEMV: the weights through a TMA ring ------------------------
+// The register-prefetch kernel above can hold only a few tiles of weights in
+// flight per warp, and it cannot request more until x has arrived and its
+// image has been built.  At each kernel boundary the DRAM therefore idles
+// while x is fetched and converted.  This kernel decouples the two:
+// * one producer thread streams the CTA's strips through a ring of shared-
+//   memory stages with TMA (cp.async.bulk.tensor, 128-byte swizzle; the
+//   packed words as a 3D view so one copy brings a whole stage).  It
+//   issues the first stages before griddepcontrol.wait, and since a CTA takes
+//   under half an SM, the next kernel's CTA fills its ring while this one
+//   drains;
+// * a stage is one 16-row strip x 8 k-chunks of 256 values (16 KB of packed
+//   weights plus its scales and biases).  Consumer warp w takes k-chunk w of
+//   every stage.  It therefore needs the x image only of its own k-chunks: it
+//   builds them itself, one chunk at a time, just before use (no CTA-wide
+//   image phase).  Stages run k-block-major, strip-minor, so one chunk image
+//   serves every strip of the CTA;
+// * per stage a warp adds its tile's per-row sums into its own shared-memory
+//   slot; at the end the 8 warps' slots are summed in warp order
+//   (deterministic, no atomics, no global scratch) and stored through the
+//   same epilogue as the kernel above.
+// Arithmetic per group is the kernel above's: exact digit dots on the
+// integer tensor cores, fp32 scale, bias and sums.
+constexpr int kStrConsumers = 16;
+constexpr int kStrThreads = (kStrConsumers + 1) * kWarp;  // + one producer warp
+constexpr int kStrKc = kStrConsumers;                      // k-chunks per stage (one per consumer warp)
+constexpr int kStrTileBytes = 16 * 128;                    // 16 rows x 32 packed words
+constexpr int kStrWBytes = kStrKc * kStrTileBytes;         // 32 KB
+constexpr int kStrSBCols = kStrKc * 4;                     // scale groups per stage at gs 64
+constexpr int kStrSBBytes = 16 * kStrSBCols * 2;           // 16 rows x up to 64 scale groups
+constexpr int kStrStageBytes = kStrWBytes + 2 * kStrSBBytes;  // 36 KB (a multiple of 1024)
+constexpr int kStrNormThreads = 256;                       // sum of squares as the kernel above
+constexpr int kStrImgBytes = 4 * M1<64>::kImgStride;       // one k-chunk: 4 lane-groups
+constexpr uint64_t kStrWaitNs = 1000000000ull;             // bounded waits: 1 s
+constexpr uint32_t kStrTryHintNs = 10000;                  // consumer waits: 10 us per try_wait,
+constexpr int kStrTries = 100000;                          // at most 1 s in all
+
+struct StreamLayout {
+    int ring, ns_max;
+    __host__ __device__ size_t img_off() const { return (size_t)ring * kStrStageBytes; }
+    __host__ __device__ size_t zero_off() const { return img_off() + (size_t)kStrConsumers * kStrImgBytes; }
+    __host__ __device__ size_t part_off() const { return zero_off() + 64; }
+    __host__ __device__ size_t red_off() const {
+        return part_off() + (size_t)kStrConsumers * ns_max * 16 * sizeof(float);
+    }
+    __host__ __device__ size_t bar_off() const { return red_off() + 8 * sizeof(float); }
+    __host__ __device__ size_t bytes() const { return bar_off() + (size_t)2 * ring * 8 + 1024; }  // + alignment
+};
+
+__device__ __forceinline__ uint4 lds128(const unsigned char* p) {
+    return *reinterpret_cast<const uint4*>(p);
+}
+
+__global__ void __launch_bounds__(kStrThreads, 1)
+gemv_stream_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_s,
+                   const __grid_constant__ CUtensorMap tm_b, const GemvM1Params p, const StreamLayout L) {
+    using C = M1<64>;
+    extern __shared__ unsigned char smem_raw[];
+    // stages need 1024-byte alignment (the 128-byte swizzle repeats every 8 rows)
+    const uint32_t raw_u = smem_u32(smem_raw);
+    unsigned char* base = smem_raw + (((raw_u + 1023u) & ~1023u) - raw_u);
+    const uint32_t base_u = smem_u32(base);
+    const int R = L.ring;
+    float* partials = reinterpret_cast<float*>(base + L.part_off());
+    float* red = reinterpret_cast<float*>(base + L.red_off());
+    const uint32_t bars = base_u + (uint32_t)L.bar_off();
+    auto full_bar = [&](int s) { return bars + 8u * s; };
+    auto empty_bar = [&](int s) { return bars + 8u * (R + s); };
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int s0 = (int)(blockIdx.x * (uint32_t)p.n_strips / gridDim.x);
+    const int s1 = (int)((blockIdx.x + 1) * (uint32_t)p.n_strips / gridDim.x);
+    const int ns = s1 - s0;
+    const int nk = (p.ng + 3) >> 2;              // k-chunks of 4 lane-groups
+    const int nkb = (nk + kStrKc - 1) / kStrKc;  // stages per strip
+    const int n_stages = nkb * ns;
+    const int sb_cols = kStrSBCols >> p.sg_shift;  // scale groups per stage
+    const uint32_t sb_bytes = 16u * sb_cols * 2u;
+
+    if (warp == kStrConsumers && lane == 0) {  // descriptors on their way before the first copy
+        prefetch_tensormap(&tm_w);
+        prefetch_tensormap(&tm_s);
+        prefetch_tensormap(&tm_b);
+    }
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < R; s++) {
+            mbar_init_nofence(full_bar(s), 1);
+            mbar_init_nofence(empty_bar(s), kStrConsumers);
+        }
+        mbar_init_fence();
+    }
+    if (threadIdx.x < 4) reinterpret_cast<uint4*>(base + L.zero_off())[threadIdx.x] = make_uint4(0, 0, 0, 0);
+    for (int i = threadIdx.x; i < kStrConsumers * L.ns_max * 16; i += kStrThreads) partials[i] = 0.0f;
+    __syncthreads();
+    pdl_launch_dependents();
+
+    if (warp == kStrConsumers) {
+        // ---- producer: one thread issues every copy, stages in order
+        if (lane == 0) {
+            const uint64_t pol = l2_policy_evict_first();  // weights are read once
+            bool ok = true;
+            int issued = 0;
+            int slot = 0, use = 0, kb = 0, jj = 0;
+            for (int i = 0; i < n_stages; i++) {
+                if (i == R) pdl_wait();  // past the prefetch, the waits below depend on the consumers
+                if (use > 0 && !mbar_wait_nap(empty_bar(slot), (use - 1) & 1, kStrWaitNs, 64)) {
+                    ok = false;
+                    break;
+                }
+                const int strip = s0 + jj;
+                const int kc0 = kb * kStrKc;
+                const uint32_t dst = base_u + (uint32_t)slot * kStrStageBytes;
+                // one copy of 8 k-chunks x 16 rows (chunks past the row end read as zeros)
+                mbar_arrive_expect_tx(full_bar(slot), (uint32_t)kStrWBytes + 2u * sb_bytes);
+                tma_load_3d(dst, &tm_w, 0, strip * 16, kc0, full_bar(slot), pol);
+                const int gx = (kc0 * 4) >> p.sg_shift;
+                tma_load_2d(dst + kStrWBytes, &tm_s, gx, strip * 16, full_bar(slot), pol);
+                tma_load_2d(dst + kStrWBytes + kStrSBBytes, &tm_b, gx, strip * 16, full_bar(slot), pol);
+                issued++;
+                if (++slot == R) {
+                    slot = 0;
+                    use++;
+                }
+                if (++jj == ns) {
+                    jj = 0;
+                    kb++;
+                }
+            }
+            if (!ok && p.status) atomicOr(p.status, 1);
+            // every issued copy lands before the CTA may exit; the last use of
+            // each slot is its final phase, so its parity cannot alias
+            for (int k = max(0, issued - R); k < issued; k++)
+                if (!mbar_wait_nap(full_bar(k % R), (k / R) & 1, kStrWaitNs, 64) && p.status) atomicOr(p.status, 1);
+        }
+        return;
+    }
+
+    // ---- consumers (warps 0-15; threadIdx.x in [0, 512))
+    pdl_wait();  // x, norm_w, residual and the outputs follow the previous kernel
+    float norm_r = 1.0f;
+    if (p.norm_w) {
+        // the kernel above's order: thread i < 256 sums x[i], x[i+256], ...;
+        // then the warp's xor tree; then the 8 warp sums in order
+        float ss = 0.0f;
+        if (threadIdx.x < kStrNormThreads)
+            for (int i = threadIdx.x; i < p.n_in; i += kStrNormThreads) ss = fmaf(p.x[i], p.x[i], ss);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        if (lane == 0 && threadIdx.x < kStrNormThreads) red[warp] = ss;
+        asm volatile("bar.sync 1, 512;" ::: "memory");
+        float tot = 0.0f;
+#pragma unroll
+        for (int i = 0; i < kStrNormThreads / kWarp; i++) tot += red[i];
+        const float mean = __fdiv_rn(tot, (float)p.n_in);
+        norm_r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, p.eps)));
+    }
+
+    const int g = lane >> 2, t = lane & 3;
+    unsigned char* img = base + L.img_off() + (size_t)warp * kStrImgBytes;
+    const unsigned char* zero_blk = base + L.zero_off();
+    const int role = (g >> 1) == t ? (g & 1) + 1 : 0;  // 1: d2+d0, 2: d1, 0: none
+    const int off0 = role == 1 ? 0 : 64;
+    // image build: lane holds values [8*(lane&7), +8) of lane-group lane>>3
+    const int bq = lane >> 3, bp = lane & 7;
+    float xv[8];
+    auto load_x = [&](int kc) {
+        const int G = kc * 4 + bq;
+        if (kc < nk && G < p.ng) {
+            const float4* src = reinterpret_cast<const float4*>(p.x + (size_t)kc * 256 + lane * 8);
+            const float4 a = src[0], b = src[1];
+            xv[0] = a.x; xv[1] = a.y; xv[2] = a.z; xv[3] = a.w;
+            xv[4] = b.x; xv[5] = b.y; xv[6] = b.z; xv[7] = b.w;
+            if (p.norm_w) {
+                const float4* nw = reinterpret_cast<const float4*>(p.norm_w + (size_t)kc * 256 + lane * 8);
+                const float4 c = nw[0], d = nw[1];
+                const float n8[8] = {c.x, c.y, c.z, c.w, d.x, d.y, d.z, d.w};
+#pragma unroll
+                for (int i = 0; i < 8; i++) xv[i] = __fmul_rn(__fmul_rn(xv[i], norm_r), n8[i]);
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < 8; i++) xv[i] = 0.0f;
+        }
+    };
+
+    bool ok = true;
+    int slot = 0;
+    uint32_t phase = 0;
+    // CTAs with one or two strips keep each strip's lane sums in registers
+    // across k-blocks; more strips go through the shared-memory slots per stage
+    const bool regacc = ns <= 2;
+    float r00 = 0.0f, r01 = 0.0f, r10 = 0.0f, r11 = 0.0f;
+    // scale/bias tiles carry the swizzle of their row width (128, 64 or 32 B)
+    const int sb_row = sb_cols * 2;
+    const int sb_mask = (sb_row >> 4) - 1;  // 16-byte units per row - 1: 128 B: 7, 64 B: 3, 32 B: 1
+    const int lg = (warp * 4 + t) >> p.sg_shift;                     // scale group inside the stage
+    auto sb_off = [&](int row) {
+        const int o = row * sb_row + lg * 2;
+        return o ^ (((o >> 7) & sb_mask) << 4);
+    };
+    const int sbo0 = sb_off(g), sbo1 = sb_off(g + 8);
+    load_x(warp);
+    for (int kb = 0; kb < nkb; kb++) {
+        const int kc = kb * kStrKc + warp;
+        const bool active = kc < nk;
+        if (active) {
+            // digits of this warp's chunk (the kernel above's image format)
+            float amax = 0.0f, s = 0.0f;
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                amax = fmaxf(amax, fabsf(xv[i]));
+                s += xv[i];
+            }
+#pragma unroll
+            for (int o = 1; o < 8; o <<= 1) {
+                amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+                s += __shfl_xor_sync(0xffffffffu, s, o);
+            }
+            const int E = group_exponent(amax);
+            const float up = exp2i(kXBits - E);
+            uint32_t r[8];
+#pragma unroll
+            for (int k = 0; k < 8; k++) r[k] = digits3(xv[k], up);
+            const uint32_t e01 = prmt(prmt(r[0], r[2], 0x5140), prmt(r[4], r[6], 0x5140), 0x5410);
+            const uint32_t e11 = prmt(prmt(r[0], r[2], 0x5140), prmt(r[4], r[6], 0x5140), 0x7632);
+            const uint32_t e21 = prmt(prmt(r[0], r[2], 0x0062), prmt(r[4], r[6], 0x0062), 0x5410);
+            const uint32_t o01 = prmt(prmt(r[1], r[3], 0x5140), prmt(r[5], r[7], 0x5140), 0x5410);
+            const uint32_t o11 = prmt(prmt(r[1], r[3], 0x5140), prmt(r[5], r[7], 0x5140), 0x7632);
+            const uint32_t o21 = prmt(prmt(r[1], r[3], 0x0062), prmt(r[5], r[7], 0x0062), 0x5410);
+            unsigned char* gb = img + bq * C::kImgStride;
+            *reinterpret_cast<uint2*>(gb + 0 * 64 + bp * 8) = make_uint2(e21, o21);
+            *reinterpret_cast<uint2*>(gb + 1 * 64 + bp * 8) = make_uint2(e11, o11);
+            *reinterpret_cast<uint2*>(gb + 2 * 64 + bp * 8) = make_uint2(e01, o01);
+            if (bp == 0) *reinterpret_cast<float2*>(gb + C::kMetaOff) = make_float2(exp2i(E - kXBits), s);
+        }
+        __syncwarp();
+        if (kb + 1 < nkb) load_x(kc + kStrKc);  // next chunk's x, in flight during this one's tiles
+
+        const bool gok = kc * 4 + t < p.ng;
+        const unsigned char* gb = img + t * C::kImgStride;
+        const uint4* src0 = reinterpret_cast<const uint4*>(role ? gb + off0 : zero_blk);
+        const uint4* src1 = reinterpret_cast<const uint4*>(role == 1 ? gb + 128 : zero_blk);
+        const float2 meta = *reinterpret_cast<const float2*>(gb + C::kMetaOff);
+        for (int j = 0; j < ns; j++) {
+            if (ok && !mbar_wait_tries(full_bar(slot), phase, kStrTryHintNs, kStrTries)) ok = false;
+            if (ok && active) {
+                const unsigned char* st = base + (size_t)slot * kStrStageBytes;
+                const unsigned char* wt = st + warp * kStrTileBytes;
+                // rows g and g+8; 16-byte chunks 2t and 2t+1 of the row, swizzled
+                const int c0 = ((2 * t) ^ g) << 4, c1 = ((2 * t + 1) ^ g) << 4;
+                const uint4 ra = lds128(wt + g * 128 + c0), rb = lds128(wt + g * 128 + c1);
+                const uint4 rc = lds128(wt + (g + 8) * 128 + c0), rd = lds128(wt + (g + 8) * 128 + c1);
+                const uint32_t w0[8] = {ra.x, ra.y, ra.z, ra.w, rb.x, rb.y, rb.z, rb.w};
+                const uint32_t w1[8] = {rc.x, rc.y, rc.z, rc.w, rd.x, rd.y, rd.z, rd.w};
+                int c0e[4] = {0, 0, 0, 0}, c0o[4] = {0, 0, 0, 0}, c1e[4] = {0, 0, 0, 0}, c1o[4] = {0, 0, 0, 0};
+#pragma unroll
+                for (int ks = 0; ks < C::kKSteps; ks += 2) {
+                    const uint4 q0 = src0[ks >> 1], q1 = src1[ks >> 1];
+                    uint32_t a0, a1, a2, a3;
+                    unpack_u8(w0[ks], a0, a2);
+                    unpack_u8(w1[ks], a1, a3);
+                    mma_u8s8_16832(c0e, a0, a1, a2, a3, q0.x, q0.y);
+                    mma_u8s8_16832(c1e, a0, a1, a2, a3, q1.x, q1.y);
+                    unpack_u8(w0[ks + 1], a0, a2);
+                    unpack_u8(w1[ks + 1], a1, a3);
+                    mma_u8s8_16832(c0o, a0, a1, a2, a3, q0.z, q0.w);
+                    mma_u8s8_16832(c1o, a0, a1, a2, a3, q1.z, q1.w);
+                }
+                const unsigned char* ss = st + kStrWBytes;
+                const unsigned char* sbi = st + kStrWBytes + kStrSBBytes;
+                float a0f = 0.0f, a1f = 0.0f;
+                if (gok) {
+                    const float dot0 = fmaf((float)(c0e[0] + c0o[0]), 65536.0f,
+                                            fmaf((float)(c0e[1] + c0o[1]), 256.0f, (float)(c1e[0] + c1o[0])));
+                    const float dot1 = fmaf((float)(c0e[2] + c0o[2]), 65536.0f,
+                                            fmaf((float)(c0e[3] + c0o[3]), 256.0f, (float)(c1e[2] + c1o[2])));
+                    const float s0 = h2f(*reinterpret_cast<const uint16_t*>(ss + sbo0));
+                    const float b0 = h2f(*reinterpret_cast<const uint16_t*>(sbi + sbo0));
+                    const float s1 = h2f(*reinterpret_cast<const uint16_t*>(ss + sbo1));
+                    const float b1 = h2f(*reinterpret_cast<const uint16_t*>(sbi + sbo1));
+                    a0f = fmaf(s0 * meta.x, dot0, 0.0f);
+                    a0f = fmaf(b0, meta.y, a0f);
+                    a1f = fmaf(s1 * meta.x, dot1, 0.0f);
+                    a1f = fmaf(b1, meta.y, a1f);
+                }
+                if (regacc) {
+                    if (j == 0) {
+                        r00 += a0f;
+                        r01 += a1f;
+                    } else {
+                        r10 += a0f;
+                        r11 += a1f;
+                    }
+                } else {
+                    a0f += __shfl_xor_sync(0xffffffffu, a0f, 1);
+                    a0f += __shfl_xor_sync(0xffffffffu, a0f, 2);
+                    a1f += __shfl_xor_sync(0xffffffffu, a1f, 1);
+                    a1f += __shfl_xor_sync(0xffffffffu, a1f, 2);
+                    if (t == 0) {
+                        float* slotp = partials + ((size_t)warp * L.ns_max + j) * 16;
+                        slotp[g] += a0f;
+                        slotp[g + 8] += a1f;
+                    }
+                }
+            }
+            __syncwarp();
+            // a slot whose copy never arrived is not handed back: the producer
+            // then stops instead of reusing it under a copy still in flight
+            if (ok && lane == 0) mbar_arrive(empty_bar(slot));
+            if (++slot == R) {
+                slot = 0;
+                phase ^= 1u;
+            }
+        }
+        __syncwarp();  // the chunk image is rebuilt next
+    }
+    if (!ok && lane == 0 && p.status) atomicOr(p.status, 1);
+    if (regacc) {
+#pragma unroll
+        for (int j = 0; j < 2; j++) {
+            float a0f = j == 0 ? r00 : r10, a1f = j == 0 ? r01 : r11;
+            a0f += __shfl_xor_sync(0xffffffffu, a0f, 1);
+            a0f += __shfl_xor_sync(0xffffffffu, a0f, 2);
+            a1f += __shfl_xor_sync(0xffffffffu, a1f, 1);
+            a1f += __shfl_xor_sync(0xffffffffu, a1f, 2);
+            if (j < ns && t == 0) {
+                float* slotp = partials + ((size_t)warp * L.ns_max + j) * 16;
+                slotp[g] = a0f;
+                slotp[g + 8] = a1f;
+            }
+        }
+    }
+
+    // ---- per-strip totals: warps' slots summed in warp order
+    asm volatile("bar.sync 1, 512;" ::: "memory");
+    if (!__any_sync(0xffffffffu, !ok)) {
+        for (int j = warp; j < ns; j += kStrConsumers) {
+            if (t == 0) {
+                float y0 = 0.0f, y1 = 0.0f;
+#pragma unroll
+                for (int k = 0; k < kStrConsumers; k++) {
+                    const float* sl = partials + ((size_t)k * L.ns_max + j) * 16;
+                    y0 += sl[g];
+                    y1 += sl[g + 8];
+                }
+                store_pair(p, s0 + j, g, y0, y1);
+            }
+        }
+    }
+}
+
 // ---- block dequantisation ------------------------------------------------
 // One thread per packed word; out rows are relative to row0.
 __global__ void dequant_kernel(const uint32_t* __restrict__ w, const uint16_t* __restrict__ sc,
@@ -590,6 +945,106 @@ static int launch_m1(const GemvPlan& pl, const GemvM1Params& prm, cudaStream_t s
     return e == cudaSuccess ? HQ4_OK : HQ4_ERR_LAUNCH;
 }
 
+// ---- streaming kernel: tensor maps, plan, launch
+// One CTA per SM: the ring takes what the SM's shared memory leaves.
+constexpr size_t kStrSmemTarget = 220 * 1024;
+constexpr int kStrMaxRing = 5;
+
+struct StreamKey {
+    const void* w;
+    const void* s;
+    const void* b;
+    int n_out, n_in, sg_cols, dev;
+    bool operator==(const StreamKey& o) const {
+        return w == o.w && s == o.s && b == o.b && n_out == o.n_out && n_in == o.n_in && sg_cols == o.sg_cols &&
+               dev == o.dev;
+    }
+};
+struct StreamKeyHash {
+    size_t operator()(const StreamKey& k) const {
+        size_t h = std::hash<const void*>()(k.w);
+        h = h * 1000003u ^ std::hash<const void*>()(k.s);
+        h = h * 1000003u ^ std::hash<const void*>()(k.b);
+        h = h * 1000003u ^ (size_t)k.n_out * 31u ^ (size_t)k.n_in * 131u ^ (size_t)k.sg_cols ^ ((size_t)k.dev << 40);
+        return h;
+    }
+};
+struct StreamMaps {
+    CUtensorMap tw, ts, tb;
+};
+
+// Swizzle of a scale/bias tile whose rows are sg_cols fp16 values (128, 64 or
+// 32 bytes): the 16 rows' reads of one column then fall in different banks.
+static CUtensorMapSwizzle sb_swizzle(int sg_cols) {
+    return sg_cols * 2 >= 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                              : sg_cols * 2 == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B;
+}
+
+// The three maps of a weight matrix (packed words: 16 rows x 8 k-chunks of
+// 32 words, 128-byte swizzle; scales and biases: sg_cols x 16-row boxes), cached by
+// (pointers, shape, device).  False if the driver cannot encode them.
+static bool stream_maps(const GemvM1Params& p, int n_sg, int sg_cols, StreamMaps* out) {
+    static std::mutex mu;
+    static std::unordered_map<StreamKey, StreamMaps, StreamKeyHash> cache;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return false;
+    const StreamKey key{p.w, p.sc, p.bi, p.n_out, p.n_in, sg_cols, dev};
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) {
+        *out = it->second;
+        return true;
+    }
+    StreamMaps m;
+    if (!make_map_chunks(&m.tw, p.w, p.n_out, p.n_in / 8, 16, kStrKc) ||
+        !make_map_2d_sw(&m.ts, p.sc, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, p.n_out, n_sg, sg_cols, 16, sb_swizzle(sg_cols)) ||
+        !make_map_2d_sw(&m.tb, p.bi, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, p.n_out, n_sg, sg_cols, 16, sb_swizzle(sg_cols)))
+        return false;
+    if (cache.size() >= 4096) cache.clear();
+    cache.emplace(key, m);
+    *out = m;
+    return true;
+}
+
+// Launch the streaming kernel when the shape suits it (lane-groups of 64,
+// scale groups of 64..256 whose rows are whole 16-byte units, 16-byte aligned
+// scales and biases); *used says whether it was launched.
+static int launch_stream(const GemvPlan& pl, const GemvM1Params& prm, cudaStream_t st, bool* used) {
+    *used = false;
+    if (pl.kg != 64 || pl.sg_shift > 2 || pl.n_sg % 8 || (((uintptr_t)prm.sc | (uintptr_t)prm.bi) & 15))
+        return HQ4_OK;
+    const int grid = std::min(pl.n_strips, sm_count());
+    StreamLayout L;
+    L.ns_max = (pl.n_strips + grid - 1) / grid;
+    L.ring = kStrMaxRing;
+    while (L.ring > 2 && L.bytes() > kStrSmemTarget) L.ring--;
+    if (L.bytes() > kStrSmemTarget) return HQ4_OK;
+    StreamMaps m;
+    if (!stream_maps(prm, pl.n_sg, kStrSBCols >> pl.sg_shift, &m)) return HQ4_OK;
+    static bool attr_done[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !attr_done[dev]) {
+        if (cudaFuncSetAttribute(gemv_stream_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024) !=
+            cudaSuccess)
+            return HQ4_ERR_LAUNCH;
+        attr_done[dev] = true;
+    }
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t lc = {};
+    lc.gridDim = dim3(grid);
+    lc.blockDim = dim3(kStrThreads);
+    lc.dynamicSmemBytes = L.bytes();
+    lc.stream = st;
+    lc.attrs = attr;
+    lc.numAttrs = 1;
+    *used = true;
+    const cudaError_t e = cudaLaunchKernelEx(&lc, gemv_stream_kernel, m.tw, m.ts, m.tb, prm, L);
+    return e == cudaSuccess ? HQ4_OK : HQ4_ERR_LAUNCH;
+}
+
 // Fill the shape/plan part of the parameters and launch.  `prm` carries the
 // pointers and the epilogue/prologue options.
 int gemv_launch(GemvM1Params prm, int gs, cudaStream_t st) {
@@ -605,6 +1060,9 @@ int gemv_launch(GemvM1Params prm, int gs, cudaStream_t st) {
     prm.n_strips = pl.n_strips;
     prm.nq = pl.nq;
     prm.status = status_word();
+    bool streamed = false;
+    rc = launch_stream(pl, prm, st, &streamed);
+    if (streamed || rc) return rc;
     return pl.kg == 64 ? launch_m1<64>(pl, prm, st) : launch_m1<32>(pl, prm, st);
 }
 

@@ -35,6 +35,9 @@ SHAPES = [
     (100, 64, 32),         # fewer units than warps per CTA
     (4608, 3584, 64),      # fused q|k|v rows
     (2, 4096, 64),
+    (256, 2048, 256),      # scale groups of 256 (4 lane-groups per scale)
+    (40000, 512, 64),      # 17 strips per CTA on 148 SMs
+    (1000, 18944, 128),    # long rows, gs 128, ragged last strip
 ]
 
 
