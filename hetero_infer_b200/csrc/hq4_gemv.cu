@@ -545,59 +545,65 @@ gemv_stream_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_consta
     const int sb_cols = kStrSBCols >> p.sg_shift;  // scale groups per stage
     const uint32_t sb_bytes = 16u * sb_cols * 2u;
 
-    if (warp == kStrConsumers && lane == 0) {  // descriptors on their way before the first copy
+    // ---- producer (warp 16, one thread): it sets up the barriers and issues
+    // the first stages before the CTA-wide barrier, so the first copies leave
+    // as early as possible; it issues every copy, stages in order
+    const bool producer = warp == kStrConsumers && lane == 0;
+    int p_issued = 0, p_slot = 0, p_use = 0, p_kb = 0, p_jj = 0;
+    uint64_t pol = 0;
+    auto issue_stage = [&]() {
+        const int strip = s0 + p_jj;
+        const int kc0 = p_kb * kStrKc;
+        const uint32_t dst = base_u + (uint32_t)p_slot * kStrStageBytes;
+        // one copy of the stage's k-chunks x 16 rows (chunks past the row end read as zeros)
+        mbar_arrive_expect_tx(full_bar(p_slot), (uint32_t)kStrWBytes + 2u * sb_bytes);
+        tma_load_3d(dst, &tm_w, 0, strip * 16, kc0, full_bar(p_slot), pol);
+        const int gx = (kc0 * 4) >> p.sg_shift;
+        tma_load_2d(dst + kStrWBytes, &tm_s, gx, strip * 16, full_bar(p_slot), pol);
+        tma_load_2d(dst + kStrWBytes + kStrSBBytes, &tm_b, gx, strip * 16, full_bar(p_slot), pol);
+        p_issued++;
+        if (++p_slot == R) {
+            p_slot = 0;
+            p_use++;
+        }
+        if (++p_jj == ns) {
+            p_jj = 0;
+            p_kb++;
+        }
+    };
+    if (producer) {
         prefetch_tensormap(&tm_w);
         prefetch_tensormap(&tm_s);
         prefetch_tensormap(&tm_b);
-    }
-    if (threadIdx.x == 0) {
         for (int s = 0; s < R; s++) {
             mbar_init_nofence(full_bar(s), 1);
             mbar_init_nofence(empty_bar(s), kStrConsumers);
         }
         mbar_init_fence();
+        pol = l2_policy_evict_first();  // weights are read once
+        const int first = min(R, n_stages);
+        for (int i = 0; i < first; i++) issue_stage();
     }
     if (threadIdx.x < 4) reinterpret_cast<uint4*>(base + L.zero_off())[threadIdx.x] = make_uint4(0, 0, 0, 0);
     for (int i = threadIdx.x; i < kStrConsumers * L.ns_max * 16; i += kStrThreads) partials[i] = 0.0f;
-    __syncthreads();
+    __syncthreads();  // barriers initialised, zero block and partial slots cleared
     pdl_launch_dependents();
 
     if (warp == kStrConsumers) {
-        // ---- producer: one thread issues every copy, stages in order
-        if (lane == 0) {
-            const uint64_t pol = l2_policy_evict_first();  // weights are read once
+        if (producer) {
             bool ok = true;
-            int issued = 0;
-            int slot = 0, use = 0, kb = 0, jj = 0;
-            for (int i = 0; i < n_stages; i++) {
-                if (i == R) pdl_wait();  // past the prefetch, the waits below depend on the consumers
-                if (use > 0 && !mbar_wait_nap(empty_bar(slot), (use - 1) & 1, kStrWaitNs, 64)) {
+            if (n_stages > R) pdl_wait();  // the waits below depend on the consumers
+            while (p_issued < n_stages) {
+                if (!mbar_wait_nap(empty_bar(p_slot), (p_use - 1) & 1, kStrWaitNs, 64)) {
                     ok = false;
                     break;
                 }
-                const int strip = s0 + jj;
-                const int kc0 = kb * kStrKc;
-                const uint32_t dst = base_u + (uint32_t)slot * kStrStageBytes;
-                // one copy of 8 k-chunks x 16 rows (chunks past the row end read as zeros)
-                mbar_arrive_expect_tx(full_bar(slot), (uint32_t)kStrWBytes + 2u * sb_bytes);
-                tma_load_3d(dst, &tm_w, 0, strip * 16, kc0, full_bar(slot), pol);
-                const int gx = (kc0 * 4) >> p.sg_shift;
-                tma_load_2d(dst + kStrWBytes, &tm_s, gx, strip * 16, full_bar(slot), pol);
-                tma_load_2d(dst + kStrWBytes + kStrSBBytes, &tm_b, gx, strip * 16, full_bar(slot), pol);
-                issued++;
-                if (++slot == R) {
-                    slot = 0;
-                    use++;
-                }
-                if (++jj == ns) {
-                    jj = 0;
-                    kb++;
-                }
+                issue_stage();
             }
             if (!ok && p.status) atomicOr(p.status, 1);
             // every issued copy lands before the CTA may exit; the last use of
             // each slot is its final phase, so its parity cannot alias
-            for (int k = max(0, issued - R); k < issued; k++)
+            for (int k = max(0, p_issued - R); k < p_issued; k++)
                 if (!mbar_wait_nap(full_bar(k % R), (k / R) & 1, kStrWaitNs, 64) && p.status) atomicOr(p.status, 1);
         }
         return;
@@ -803,16 +809,20 @@ gemv_stream_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_consta
     asm volatile("bar.sync 1, 512;" ::: "memory");
     if (!__any_sync(0xffffffffu, !ok)) {
         for (int j = warp; j < ns; j += kStrConsumers) {
-            if (t == 0) {
-                float y0 = 0.0f, y1 = 0.0f;
+            // lane t sums warps 4t..4t+3 in order; the four sums are then
+            // combined by a fixed xor tree (the same on every lane)
+            float y0 = 0.0f, y1 = 0.0f;
 #pragma unroll
-                for (int k = 0; k < kStrConsumers; k++) {
-                    const float* sl = partials + ((size_t)k * L.ns_max + j) * 16;
-                    y0 += sl[g];
-                    y1 += sl[g + 8];
-                }
-                store_pair(p, s0 + j, g, y0, y1);
+            for (int k = 0; k < kStrConsumers / 4; k++) {
+                const float* sl = partials + ((size_t)(t * (kStrConsumers / 4) + k) * L.ns_max + j) * 16;
+                y0 += sl[g];
+                y1 += sl[g + 8];
             }
+            y0 += __shfl_xor_sync(0xffffffffu, y0, 1);
+            y0 += __shfl_xor_sync(0xffffffffu, y0, 2);
+            y1 += __shfl_xor_sync(0xffffffffu, y1, 1);
+            y1 += __shfl_xor_sync(0xffffffffu, y1, 2);
+            if (t == 0) store_pair(p, s0 + j, g, y0, y1);
         }
     }
 }
