@@ -504,9 +504,11 @@ constexpr uint32_t kStrTryHintNs = 10000;                  // consumer waits: 10
 constexpr int kStrTries = 100000;                          // at most 1 s in all
 
 struct StreamLayout {
-    int ring, ns_max;
+    int ring, ns_max, nkb;  // nkb: k-blocks per strip = chunk images per warp
     __host__ __device__ size_t img_off() const { return (size_t)ring * kStrStageBytes; }
-    __host__ __device__ size_t zero_off() const { return img_off() + (size_t)kStrConsumers * kStrImgBytes; }
+    __host__ __device__ size_t zero_off() const {
+        return img_off() + (size_t)kStrConsumers * nkb * kStrImgBytes;
+    }
     __host__ __device__ size_t part_off() const { return zero_off() + 64; }
     __host__ __device__ size_t red_off() const {
         return part_off() + (size_t)kStrConsumers * ns_max * 16 * sizeof(float);
@@ -630,30 +632,26 @@ gemv_stream_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_consta
     }
 
     const int g = lane >> 2, t = lane & 3;
-    unsigned char* img = base + L.img_off() + (size_t)warp * kStrImgBytes;
+    // this warp's chunk images, one per k-block, built up front
+    unsigned char* img_w = base + L.img_off() + (size_t)warp * L.nkb * kStrImgBytes;
     const unsigned char* zero_blk = base + L.zero_off();
     const int role = (g >> 1) == t ? (g & 1) + 1 : 0;  // 1: d2+d0, 2: d1, 0: none
     const int off0 = role == 1 ? 0 : 64;
     // image build: lane holds values [8*(lane&7), +8) of lane-group lane>>3
     const int bq = lane >> 3, bp = lane & 7;
-    float xv[8];
-    auto load_x = [&](int kc) {
+    // x of this warp's chunks (raw; the norm is applied in the image build),
+    // the next chunk's in flight while one is built
+    float xr0[8], xr1[8];
+    auto load_x = [&](int kc, float (&dst)[8]) {
         const int G = kc * 4 + bq;
         if (kc < nk && G < p.ng) {
             const float4* src = reinterpret_cast<const float4*>(p.x + (size_t)kc * 256 + lane * 8);
             const float4 a = src[0], b = src[1];
-            xv[0] = a.x; xv[1] = a.y; xv[2] = a.z; xv[3] = a.w;
-            xv[4] = b.x; xv[5] = b.y; xv[6] = b.z; xv[7] = b.w;
-            if (p.norm_w) {
-                const float4* nw = reinterpret_cast<const float4*>(p.norm_w + (size_t)kc * 256 + lane * 8);
-                const float4 c = nw[0], d = nw[1];
-                const float n8[8] = {c.x, c.y, c.z, c.w, d.x, d.y, d.z, d.w};
-#pragma unroll
-                for (int i = 0; i < 8; i++) xv[i] = __fmul_rn(__fmul_rn(xv[i], norm_r), n8[i]);
-            }
+            dst[0] = a.x; dst[1] = a.y; dst[2] = a.z; dst[3] = a.w;
+            dst[4] = b.x; dst[5] = b.y; dst[6] = b.z; dst[7] = b.w;
         } else {
 #pragma unroll
-            for (int i = 0; i < 8; i++) xv[i] = 0.0f;
+            for (int i = 0; i < 8; i++) dst[i] = 0.0f;
         }
     };
 
@@ -673,12 +671,24 @@ gemv_stream_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_consta
         return o ^ (((o >> 7) & sb_mask) << 4);
     };
     const int sbo0 = sb_off(g), sbo1 = sb_off(g + 8);
-    load_x(warp);
+    // every chunk image of this warp before the first stage: the builds
+    // overlap the ring filling, and the stage loop below is tiles only
+    load_x(warp, xr0);
     for (int kb = 0; kb < nkb; kb++) {
         const int kc = kb * kStrKc + warp;
-        const bool active = kc < nk;
-        if (active) {
+        if (kb + 1 < nkb) load_x(kc + kStrKc, xr1);  // in flight during this build
+        if (kc < nk) {
             // digits of this warp's chunk (the kernel above's image format)
+            float xv[8];
+#pragma unroll
+            for (int i = 0; i < 8; i++) xv[i] = xr0[i];
+            if (p.norm_w && kc * 4 + bq < p.ng) {
+                const float4* nw = reinterpret_cast<const float4*>(p.norm_w + (size_t)kc * 256 + lane * 8);
+                const float4 c = nw[0], d = nw[1];
+                const float n8[8] = {c.x, c.y, c.z, c.w, d.x, d.y, d.z, d.w};
+#pragma unroll
+                for (int i = 0; i < 8; i++) xv[i] = __fmul_rn(__fmul_rn(xv[i], norm_r), n8[i]);
+            }
             float amax = 0.0f, s = 0.0f;
 #pragma unroll
             for (int i = 0; i < 8; i++) {
@@ -701,15 +711,21 @@ gemv_stream_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_consta
             const uint32_t o01 = prmt(prmt(r[1], r[3], 0x5140), prmt(r[5], r[7], 0x5140), 0x5410);
             const uint32_t o11 = prmt(prmt(r[1], r[3], 0x5140), prmt(r[5], r[7], 0x5140), 0x7632);
             const uint32_t o21 = prmt(prmt(r[1], r[3], 0x0062), prmt(r[5], r[7], 0x0062), 0x5410);
-            unsigned char* gb = img + bq * C::kImgStride;
+            unsigned char* gb = img_w + (size_t)kb * kStrImgBytes + bq * C::kImgStride;
             *reinterpret_cast<uint2*>(gb + 0 * 64 + bp * 8) = make_uint2(e21, o21);
             *reinterpret_cast<uint2*>(gb + 1 * 64 + bp * 8) = make_uint2(e11, o11);
             *reinterpret_cast<uint2*>(gb + 2 * 64 + bp * 8) = make_uint2(e01, o01);
             if (bp == 0) *reinterpret_cast<float2*>(gb + C::kMetaOff) = make_float2(exp2i(E - kXBits), s);
         }
-        __syncwarp();
-        if (kb + 1 < nkb) load_x(kc + kStrKc);  // next chunk's x, in flight during this one's tiles
+#pragma unroll
+        for (int i = 0; i < 8; i++) xr0[i] = xr1[i];
+    }
+    __syncwarp();
 
+    for (int kb = 0; kb < nkb; kb++) {
+        const int kc = kb * kStrKc + warp;
+        const bool active = kc < nk;
+        const unsigned char* img = img_w + (size_t)kb * kStrImgBytes;
         const bool gok = kc * 4 + t < p.ng;
         const unsigned char* gb = img + t * C::kImgStride;
         const uint4* src0 = reinterpret_cast<const uint4*>(role ? gb + off0 : zero_blk);
@@ -786,7 +802,6 @@ gemv_stream_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_consta
                 phase ^= 1u;
             }
         }
-        __syncwarp();  // the chunk image is rebuilt next
     }
     if (!ok && lane == 0 && p.status) atomicOr(p.status, 1);
     if (regacc) {
@@ -1026,9 +1041,10 @@ static int launch_stream(const GemvPlan& pl, const GemvM1Params& prm, cudaStream
     const int grid = std::min(pl.n_strips, sm_count());
     StreamLayout L;
     L.ns_max = (pl.n_strips + grid - 1) / grid;
+    L.nkb = (pl.ng / 4 + kStrKc - 1) / kStrKc;
     L.ring = kStrMaxRing;
-    while (L.ring > 2 && L.bytes() > kStrSmemTarget) L.ring--;
-    if (L.bytes() > kStrSmemTarget) return HQ4_OK;
+    while (L.ring > 3 && L.bytes() > kStrSmemTarget) L.ring--;
+    if (L.bytes() > kStrSmemTarget) return HQ4_OK;  // rows too long for the chunk images: register kernel
     StreamMaps m;
     if (!stream_maps(prm, pl.n_sg, kStrSBCols >> pl.sg_shift, &m)) return HQ4_OK;
     static bool attr_done[64] = {false};
