@@ -87,8 +87,8 @@ def measured_tensor_peak() -> float:
 
 def profiled_traffic():
     """DRAM bytes per GEMV launch of the layer step, from the committed ncu
-    summary (profiles/gemv_m1_layer_step.md), or None."""
-    path = os.path.join(ROOT, "profiles", "gemv_m1_layer_step.md")
+    summary (profiles/gemv_stream_layer_step.md), or None."""
+    path = os.path.join(ROOT, "profiles", "gemv_stream_layer_step.md")
     try:
         for line in open(path):
             if line.startswith("traffic_bytes_per_launch:"):
@@ -266,7 +266,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
                          "frac": round(value / world / peak, 4),
                          "frac_of_8000": round(value / world / 8000.0, 4),
                          "traffic": traffic, "algorithmic_bytes_per_launch": STEP_BYTES / len(LAUNCHES),
-                         "kernel": "gemv_m1_kernel (avg over the step's 4 launches)"},
+                         "kernel": "gemv_stream_kernel (avg over the step's 4 launches)"},
             "clocks": sampler.summary(t_wall0, t_wall1),
             "gpu_launches": len(LAUNCHES) * args.steps,
         }
@@ -358,7 +358,7 @@ def gemm_bench(lib, dev, gen, stream, q4_on_device, launches=60):
             work = ops.gemm_workspace(n, k, m, dev)
             torch.cuda.synchronize(dev)
             plan = ops.gemm_plan(n, k, m)
-            variants = [("gemm", plan["kernel"])] + ([("gemv", "gemv_m1")] if m == 1 else [])
+            variants = [("gemm", plan["kernel"])] + ([("gemv", "gemv_stream")] if m == 1 else [])
             row = {}
             for label, kern in variants:
                 def one(i):
