@@ -66,17 +66,25 @@ __global__ void embed_kernel(const __half* __restrict__ table, const int* __rest
 }
 
 // ---- attention ---------------------------------------------------------------
-// CTA (head h, query token i): position p = *pos + i attends to keys [0, p].
-// scores: one key per warp iteration, lanes split head_dim; softmax in fp32
-// as the reference writes it (s - max, exp, / sum); out[d] = sum_s p_s v_s[d].
-constexpr int kAttnThreads = 128;
+// CTA (head h, query token i): position p = *pos + i attends to keys [0, p],
+// in the reference's order of operations (hetero/cpu_model.py:233-252):
+// s = (q . k) * scale, s -= max, e = exp(s), e /= sum(e), out = sum_s e_s v_s.
+// Decode is latency-bound (a few hundred keys, 28 heads), so every key's score
+// is its own thread: a 4-chain fp32 dot over float4 rows of the K cache, with
+// q broadcast from shared memory.  The value pass gives each thread a float4
+// column of V and one of 8 key residues; the 8 partial sums are added in a
+// fixed order (deterministic).
+constexpr int kAttnThreads = 256;
+constexpr int kAttnParts = 8;  // key residues in the value pass
 
 __global__ void __launch_bounds__(kAttnThreads) attention_kernel(
     const float* __restrict__ q, const float* __restrict__ k_cache, const float* __restrict__ v_cache,
     float* __restrict__ out, int n_heads, int n_kv, int head_dim, int max_ctx, const int* __restrict__ pos,
     float scale) {
     extern __shared__ float sc[];  // [max positions]
+    __shared__ float4 qs[64];      // head_dim <= 256
     __shared__ float red[kAttnThreads / 32];
+    __shared__ float4 part[kAttnParts][64];
     pdl_launch_dependents();
     pdl_wait();
     const int h = blockIdx.x, i = blockIdx.y;
@@ -85,27 +93,36 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(
     if (p < 0 || p >= max_ctx) return;  // outside the cache: write nothing
     const int n = p + 1;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = kAttnThreads / 32;
-    const float* qh = q + ((size_t)i * n_heads + h) * head_dim;
-    const float* kbase = k_cache + (size_t)kh * max_ctx * head_dim;
-    const float* vbase = v_cache + (size_t)kh * max_ctx * head_dim;
-    // query slice in registers: lane owns elements lane, lane+32, ...
-    float qr[8];
-    const int per = head_dim / 32;  // head_dim <= 256
-#pragma unroll
-    for (int j = 0; j < 8; j++) qr[j] = j < per ? qh[lane + 32 * j] : 0.0f;
+    const int d4n = head_dim >> 2;  // float4 columns
+    const float4* qh = reinterpret_cast<const float4*>(q + ((size_t)i * n_heads + h) * head_dim);
+    const float4* kbase = reinterpret_cast<const float4*>(k_cache + (size_t)kh * max_ctx * head_dim);
+    const float4* vbase = reinterpret_cast<const float4*>(v_cache + (size_t)kh * max_ctx * head_dim);
+    for (int j = threadIdx.x; j < d4n; j += kAttnThreads) qs[j] = qh[j];
+    __syncthreads();
+
     float mx = -FLT_MAX;
-    for (int s = warp; s < n; s += nw) {
-        const float* kr = kbase + (size_t)s * head_dim;
-        float d = 0.0f;
+    for (int s = threadIdx.x; s < n; s += kAttnThreads) {
+        const float4* kr = kbase + (size_t)s * d4n;
+        float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+        for (int j0 = 0; j0 < d4n; j0 += 8) {  // d4n is a multiple of 8: 8 loads in flight
+            float4 kv[8];
 #pragma unroll
-        for (int j = 0; j < 8; j++)
-            if (j < per) d = fmaf(qr[j], kr[lane + 32 * j], d);
+            for (int u = 0; u < 8; u++) kv[u] = __ldg(kr + j0 + u);
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
-        d = __fmul_rn(d, scale);
-        if (lane == 0) sc[s] = d;
+            for (int u = 0; u < 8; u++) {
+                const float4 qv = qs[j0 + u];
+                a0 = fmaf(qv.x, kv[u].x, a0);
+                a1 = fmaf(qv.y, kv[u].y, a1);
+                a2 = fmaf(qv.z, kv[u].z, a2);
+                a3 = fmaf(qv.w, kv[u].w, a3);
+            }
+        }
+        const float d = __fmul_rn(__fadd_rn(__fadd_rn(a0, a1), __fadd_rn(a2, a3)), scale);
+        sc[s] = d;
         mx = fmaxf(mx, d);
     }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
     if (lane == 0) red[warp] = mx;
     __syncthreads();
     mx = red[0];
@@ -125,10 +142,51 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(
     for (int j = 0; j < nw; j++) tot += red[j];
     for (int s = threadIdx.x; s < n; s += kAttnThreads) sc[s] = __fdiv_rn(sc[s], tot);
     __syncthreads();
-    for (int d = threadIdx.x; d < head_dim; d += kAttnThreads) {
-        float acc = 0.0f;
-        for (int s = 0; s < n; s++) acc = fmaf(sc[s], vbase[(size_t)s * head_dim + d], acc);
-        out[((size_t)i * n_heads + h) * head_dim + d] = acc;
+
+    // out[d] = sum_s e_s v_s[d]: thread (column c, residue r) sums keys r, r+8, ...
+    for (int c0 = 0; c0 < d4n; c0 += kAttnThreads / kAttnParts) {
+        const int c = c0 + threadIdx.x % (kAttnThreads / kAttnParts);
+        const int r = threadIdx.x / (kAttnThreads / kAttnParts);
+        float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (c < d4n) {
+            int s = r;
+            for (; s + 3 * kAttnParts < n; s += 4 * kAttnParts) {  // four keys' loads in flight
+                float4 v[4];
+#pragma unroll
+                for (int u = 0; u < 4; u++) v[u] = __ldg(vbase + (size_t)(s + u * kAttnParts) * d4n + c);
+#pragma unroll
+                for (int u = 0; u < 4; u++) {
+                    const float e = sc[s + u * kAttnParts];
+                    acc.x = fmaf(e, v[u].x, acc.x);
+                    acc.y = fmaf(e, v[u].y, acc.y);
+                    acc.z = fmaf(e, v[u].z, acc.z);
+                    acc.w = fmaf(e, v[u].w, acc.w);
+                }
+            }
+            for (; s < n; s += kAttnParts) {
+                const float e = sc[s];
+                const float4 v = __ldg(vbase + (size_t)s * d4n + c);
+                acc.x = fmaf(e, v.x, acc.x);
+                acc.y = fmaf(e, v.y, acc.y);
+                acc.z = fmaf(e, v.z, acc.z);
+                acc.w = fmaf(e, v.w, acc.w);
+            }
+            part[r][c - c0] = acc;
+        }
+        __syncthreads();
+        if (r == 0 && c < d4n) {
+            float4 o4 = part[0][c - c0];
+#pragma unroll
+            for (int k = 1; k < kAttnParts; k++) {
+                const float4 t4 = part[k][c - c0];
+                o4.x += t4.x;
+                o4.y += t4.y;
+                o4.z += t4.z;
+                o4.w += t4.w;
+            }
+            reinterpret_cast<float4*>(out + ((size_t)i * n_heads + h) * head_dim)[c] = o4;
+        }
+        __syncthreads();
     }
 }
 
@@ -294,6 +352,7 @@ extern "C" int hq4_attention(const float* q, const float* k_cache, const float* 
     if (n_heads <= 0 || n_kv <= 0 || n_heads % n_kv || head_dim % 32 || head_dim > 256 ||
         n_tokens <= 0 || max_ctx <= 0)
         return HQ4_ERR_SHAPE;
+    if (((uintptr_t)q | (uintptr_t)k_cache | (uintptr_t)v_cache | (uintptr_t)out) & 15) return HQ4_ERR_ALIGN;
     const size_t smem = (size_t)max_ctx * sizeof(float);
     if (smem > 200 * 1024) return HQ4_ERR_SHAPE;
     static bool attr = false;
