@@ -197,6 +197,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(
 // [0, n)).  Writes the index to idx_out and, when given, to history[*pos]
 // (the generated-token record).
 constexpr int kArgmaxThreads = 1024;
+constexpr int kArgmaxCluster = 8;  // CTAs (SMs) that split the vector
 
 __device__ __forceinline__ bool argmax_before(float v, int i, float bv, int bi) {
     const bool vn = v != v, bn = bv != bv;
@@ -204,20 +205,15 @@ __device__ __forceinline__ bool argmax_before(float v, int i, float bv, int bi) 
     return v > bv || (v == bv && i < bi);
 }
 
-__global__ void __launch_bounds__(kArgmaxThreads) argmax_kernel(const float* __restrict__ x, int n,
-                                                                int* __restrict__ idx_out,
-                                                                int* __restrict__ history, int hist_len,
-                                                                const int* __restrict__ pos,
-                                                                float* __restrict__ val_out) {
+// Numpy-order best of x[lo..hi) over the CTA; the result is valid in thread 0.
+// (-inf, INT_MAX) loses to every element, so a thread that saw one element
+// holds an index in [lo, hi).
+__device__ __forceinline__ void cta_argmax(const float* __restrict__ x, int lo, int hi, float& best, int& bidx) {
     __shared__ float bv[kArgmaxThreads / 32];
     __shared__ int bi[kArgmaxThreads / 32];
-    pdl_launch_dependents();
-    pdl_wait();
-    // (-inf, INT_MAX) loses to every element, so any thread that saw one
-    // element holds an index in [0, n)
-    float best = -INFINITY;
-    int bidx = 0x7fffffff;
-    for (int i = threadIdx.x; i < n; i += kArgmaxThreads) {
+    best = -INFINITY;
+    bidx = 0x7fffffff;
+    for (int i = lo + threadIdx.x; i < hi; i += kArgmaxThreads) {
         const float v = x[i];
         if (argmax_before(v, i, best, bidx)) {
             best = v;
@@ -247,58 +243,57 @@ __global__ void __launch_bounds__(kArgmaxThreads) argmax_kernel(const float* __r
                 best = bv[j];
                 bidx = bi[j];
             }
-        *idx_out = bidx;
-        if (val_out) *val_out = best;
-        if (history) {
-            const int at = *pos;
-            if (at >= 0 && at < hist_len) history[at] = bidx;
-        }
     }
 }
 
-// One shard's greedy pick as a pair for an all-gather across ranks: the
-// numpy-order best of x[0..n) as (float bits, offset + index).
-__global__ void __launch_bounds__(kArgmaxThreads) argmax_pair_kernel(const float* __restrict__ x, int n,
-                                                                     int offset, int* __restrict__ pair) {
-    __shared__ float bv[kArgmaxThreads / 32];
-    __shared__ int bi[kArgmaxThreads / 32];
+// Argmax over a thread-block cluster: CTA r of the cluster takes the r-th
+// slice of x, then rank 0 combines the slices' pairs read over DSMEM (the
+// pair order is total -- value, then lowest index, NaN first -- so the
+// combination order does not change the result).  Outputs: either
+// (idx_out [, val_out] [, history[*pos]]) or, with `pair`, the shard pair
+// (value bits, offset + index) for a cross-rank all-gather.
+__global__ void __launch_bounds__(kArgmaxThreads) argmax_cluster_kernel(
+    const float* __restrict__ x, int n, int* __restrict__ idx_out, int* __restrict__ history, int hist_len,
+    const int* __restrict__ pos, float* __restrict__ val_out, int* __restrict__ pair, int offset) {
+    __shared__ float cbest;
+    __shared__ int cidx;
     pdl_launch_dependents();
     pdl_wait();
-    float best = -INFINITY;
-    int bidx = 0x7fffffff;
-    for (int i = threadIdx.x; i < n; i += kArgmaxThreads) {
-        const float v = x[i];
-        if (argmax_before(v, i, best, bidx)) {
-            best = v;
-            bidx = i;
-        }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, best, o);
-        const int oi = __shfl_xor_sync(0xffffffffu, bidx, o);
-        if (argmax_before(ov, oi, best, bidx)) {
-            best = ov;
-            bidx = oi;
-        }
-    }
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    if (lane == 0) {
-        bv[warp] = best;
-        bi[warp] = bidx;
-    }
-    __syncthreads();
+    const int rank = (int)cluster_ctarank(), nr = (int)cluster_nctarank();
+    const int chunk = (n + nr - 1) / nr;
+    const int lo = min(n, rank * chunk), hi = min(n, lo + chunk);
+    float best;
+    int bidx;
+    cta_argmax(x, lo, hi, best, bidx);
     if (threadIdx.x == 0) {
-        best = bv[0];
-        bidx = bi[0];
-        for (int j = 1; j < kArgmaxThreads / 32; j++)
-            if (argmax_before(bv[j], bi[j], best, bidx)) {
-                best = bv[j];
-                bidx = bi[j];
-            }
-        pair[0] = __float_as_int(best);
-        pair[1] = offset + bidx;
+        cbest = best;
+        cidx = bidx;
     }
+    cluster_sync();  // every slice's pair written and visible across the cluster
+    if (rank == 0 && threadIdx.x == 0) {
+        for (int r = 1; r < nr; r++) {
+            float v;
+            int i;
+            asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(map_to_rank(smem_u32(&cbest), r)) : "memory");
+            asm volatile("ld.shared::cluster.b32 %0, [%1];" : "=r"(i) : "r"(map_to_rank(smem_u32(&cidx), r)) : "memory");
+            if (argmax_before(v, i, best, bidx)) {
+                best = v;
+                bidx = i;
+            }
+        }
+        if (pair) {
+            pair[0] = __float_as_int(best);
+            pair[1] = offset + bidx;
+        } else {
+            *idx_out = bidx;
+            if (val_out) *val_out = best;
+            if (history) {
+                const int at = *pos;
+                if (at >= 0 && at < hist_len) history[at] = bidx;
+            }
+        }
+    }
+    cluster_sync();  // the other CTAs' shared memory stays alive until rank 0 has read it
 }
 
 // The global greedy token from `world` shard pairs (value bits, global
@@ -365,20 +360,40 @@ extern "C" int hq4_attention(const float* q, const float* k_cache, const float* 
                       head_dim, max_ctx, pos, scale);
 }
 
+static int launch_argmax_cluster(cudaStream_t st, const float* x, int n, int* idx_out, int* history, int hist_len,
+                                 const int* pos, float* val_out, int* pair, int offset) {
+    cudaLaunchAttribute attr[2];
+    attr[0] = pdl_attr();
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = kArgmaxCluster;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cudaLaunchConfig_t lc = {};
+    lc.gridDim = dim3(kArgmaxCluster);
+    lc.blockDim = dim3(kArgmaxThreads);
+    lc.stream = st;
+    lc.attrs = attr;
+    lc.numAttrs = 2;
+    return cudaLaunchKernelEx(&lc, argmax_cluster_kernel, x, n, idx_out, history, hist_len, pos, val_out, pair,
+                              offset) == cudaSuccess
+               ? HQ4_OK
+               : HQ4_ERR_LAUNCH;
+}
+
 extern "C" int hq4_argmax(const float* x, int n, int* idx_out, int* history, int hist_len,
                           const int* pos, float* val_out, void* stream) {
     if (int rc = check_device_cap()) return rc;
     if (n <= 0) return HQ4_ERR_SHAPE;
     if (history && (!pos || hist_len <= 0)) return HQ4_ERR_SHAPE;
-    return launch_pdl(argmax_kernel, dim3(1), dim3(kArgmaxThreads), 0, static_cast<cudaStream_t>(stream),
-                      x, n, idx_out, history, hist_len, pos, val_out);
+    return launch_argmax_cluster(static_cast<cudaStream_t>(stream), x, n, idx_out, history, hist_len, pos, val_out,
+                                 nullptr, 0);
 }
 
 extern "C" int hq4_argmax_pair(const float* x, int n, int offset, int* pair, void* stream) {
     if (int rc = check_device_cap()) return rc;
     if (n <= 0 || !pair) return HQ4_ERR_SHAPE;
-    return launch_pdl(argmax_pair_kernel, dim3(1), dim3(kArgmaxThreads), 0, static_cast<cudaStream_t>(stream), x,
-                      n, offset, pair);
+    return launch_argmax_cluster(static_cast<cudaStream_t>(stream), x, n, nullptr, nullptr, 0, nullptr, nullptr, pair,
+                                 offset);
 }
 
 extern "C" int hq4_pick_token(const int* pairs, int world, int* tok, int* history, int slot, void* stream) {
