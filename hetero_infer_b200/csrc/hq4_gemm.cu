@@ -62,6 +62,10 @@ namespace hq4 {
 
 int check_device_cap();
 int* status_word();
+int gemv_stream_m1(const uint32_t* w, const uint16_t* sc, const uint16_t* bi, const void* x, bool x_bf16,
+                   float* out, int n_out, int n_in, int gs, const float* row_add, const float* residual,
+                   cudaStream_t st, bool* used);
+bool gemv_stream_fits_gs64(int n_out, int n_in);
 
 constexpr int kGemmRows = 128;                          // MMA M
 constexpr int kAWarps = 8;                              // dequant + epilogue
@@ -1234,6 +1238,12 @@ extern "C" int hq4_gemm_w4a16(const uint32_t* w, const uint16_t* scales, const u
     const GemmPlan pl = plan_gemm(n_out, n_in, m);
     const SmallPlan sp = plan_small(n_out, n_in, m, xf32);
     if (!workspace || workspace_bytes < (long long)(small ? sp.ws_bytes : pl.ws_bytes)) return HQ4_ERR_SHAPE;
+    if (m == 1) {  // one token: the streaming GEMV (the weights exact, x widened to fp32)
+        bool used = false;
+        const int rc = gemv_stream_m1(w, scales, biases, x, !xf32, out, n_out, n_in, gs, row_add, residual,
+                                      static_cast<cudaStream_t>(stream), &used);
+        if (rc || used) return rc;
+    }
     int* status = status_word();
     if (!status) return HQ4_ERR_LAUNCH;
     WeightMaps wm;
@@ -1295,6 +1305,11 @@ extern "C" int hq4_gemm_w4a16(const uint32_t* w, const uint16_t* scales, const u
 
 extern "C" int hq4_gemm_plan(int n_out, int n_in, int m, int x_is_f32, int* info) {
     if (n_out <= 0 || n_in <= 0 || m <= 0 || n_in % 64 || !info) return HQ4_ERR_SHAPE;
+    if (m == 1 && gemv_stream_fits_gs64(n_out, n_in)) {
+        for (int i = 0; i < 7; i++) info[i] = 0;
+        info[7] = 2;  // streaming GEMV
+        return HQ4_OK;
+    }
     if (use_small(m, x_is_f32 != 0)) {
         const SmallPlan sp = plan_small(n_out, n_in, m, x_is_f32 != 0);
         info[0] = sp.row_tiles;

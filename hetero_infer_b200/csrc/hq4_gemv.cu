@@ -82,6 +82,7 @@ struct GemvM1Params {
     float eps;
     // epilogue mode
     int mode;               // kEpiPlain, kEpiSiluMul or kEpiQkvRope
+    int x_bf16;             // streaming kernel only: x is bf16 (no RMSNorm then)
     // kEpiQkvRope: q|k|v rows of one decoder layer, q and k rows permuted so
     // strip rows g and g+8 are the rotation pair (d, d + head_dim/2)
     int q_strips, k_strips, head_dim, max_ctx;
@@ -644,7 +645,16 @@ gemv_stream_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_consta
     float xr0[8], xr1[8];
     auto load_x = [&](int kc, float (&dst)[8]) {
         const int G = kc * 4 + bq;
-        if (kc < nk && G < p.ng) {
+        if (kc < nk && G < p.ng && p.x_bf16) {  // bf16 widens to fp32 exactly
+            const uint4 r = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(p.x) +
+                                                            (size_t)kc * 256 + lane * 8);
+            const uint32_t w4[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                dst[2 * i] = __uint_as_float(w4[i] << 16);
+                dst[2 * i + 1] = __uint_as_float(w4[i] & 0xFFFF0000u);
+            }
+        } else if (kc < nk && G < p.ng) {
             const float4* src = reinterpret_cast<const float4*>(p.x + (size_t)kc * 256 + lane * 8);
             const float4 a = src[0], b = src[1];
             dst[0] = a.x; dst[1] = a.y; dst[2] = a.z; dst[3] = a.w;
@@ -1073,6 +1083,47 @@ static int launch_stream(const GemvPlan& pl, const GemvM1Params& prm, cudaStream
 
 // Fill the shape/plan part of the parameters and launch.  `prm` carries the
 // pointers and the epilogue/prologue options.
+static void fill_shape(GemvM1Params& prm, const GemvPlan& pl) {
+    prm.ng = pl.ng;
+    prm.sg_shift = pl.sg_shift;
+    prm.n_sg = pl.n_sg;
+    prm.n_strips = pl.n_strips;
+    prm.nq = pl.nq;
+    prm.status = status_word();
+}
+
+GemvM1Params gemv_params(const uint32_t* w, const uint16_t* scales, const uint16_t* biases,
+                         const float* x, float* out, int n_out, int n_in);
+
+// The W4A16 GEMM entry point's batch-1 case (x fp32 or bf16): the streaming
+// kernel when the shape and pointers suit it; *used says whether it ran.
+int gemv_stream_m1(const uint32_t* w, const uint16_t* sc, const uint16_t* bi, const void* x, bool x_bf16,
+                   float* out, int n_out, int n_in, int gs, const float* row_add, const float* residual,
+                   cudaStream_t st, bool* used) {
+    *used = false;
+    GemvPlan pl;
+    if (plan_gemv(n_out, n_in, gs, pl)) return HQ4_OK;
+    GemvM1Params prm = gemv_params(w, sc, bi, static_cast<const float*>(x), out, n_out, n_in);
+    prm.row_add = row_add;
+    prm.residual = residual;
+    prm.x_bf16 = x_bf16 ? 1 : 0;
+    fill_shape(prm, pl);
+    return launch_stream(pl, prm, st, used);
+}
+
+// Whether gemv_stream_m1 takes a shape at group size 64 with 16-byte aligned
+// scales and biases (host only; for the launch plan).
+bool gemv_stream_fits_gs64(int n_out, int n_in) {
+    GemvPlan pl;
+    if (n_out <= 0 || n_in <= 0 || plan_gemv(n_out, n_in, 64, pl) || pl.kg != 64 || pl.n_sg % 8) return false;
+    const int grid = std::min(pl.n_strips, sm_count());
+    StreamLayout L;
+    L.ns_max = (pl.n_strips + grid - 1) / grid;
+    L.nkb = (pl.ng / 4 + kStrKc - 1) / kStrKc;
+    L.ring = 3;
+    return L.bytes() <= kStrSmemTarget;
+}
+
 int gemv_launch(GemvM1Params prm, int gs, cudaStream_t st) {
     GemvPlan pl;
     int rc = plan_gemv(prm.n_out, prm.n_in, gs, pl);
@@ -1080,12 +1131,7 @@ int gemv_launch(GemvM1Params prm, int gs, cudaStream_t st) {
     if (((uintptr_t)prm.w & 31) || ((uintptr_t)prm.x & 15) || ((uintptr_t)prm.out & 3))
         return HQ4_ERR_ALIGN;
     if (prm.norm_w && ((uintptr_t)prm.norm_w & 15)) return HQ4_ERR_ALIGN;
-    prm.ng = pl.ng;
-    prm.sg_shift = pl.sg_shift;
-    prm.n_sg = pl.n_sg;
-    prm.n_strips = pl.n_strips;
-    prm.nq = pl.nq;
-    prm.status = status_word();
+    fill_shape(prm, pl);
     bool streamed = false;
     rc = launch_stream(pl, prm, st, &streamed);
     if (streamed || rc) return rc;

@@ -78,7 +78,9 @@ int hq4_dequant(const uint32_t* w, const uint16_t* scales, const uint16_t* biase
  * Replaces QLinear._gemm (hetero/cpu_model.py:118-136: q4_dequant of 512-row
  * blocks, kernel/q4gemv.c:311-379, then a BLAS matmul).  Weight layout as
  * hq4_gemv; x is [m][n_in] bf16 (x_is_f32 = 0) or fp32 (x_is_f32 = 1), 16-byte
- * aligned; out fp32 [m][n_out].  Up to 16 bf16 (8 fp32) tokens the weights
+ * aligned; out fp32 [m][n_out].  One token goes through hq4_gemv's
+ * streaming kernel when the shape suits it (x widened to fp32, exact
+ * digits).  Up to 16 bf16 (8 fp32) tokens the weights
  * stay exact (128+q in bf16 MMAs, the scale and bias folded per group in
  * fp32) and fp32 x is carried as bf16 hi + lo (16 significant bits); above,
  * the tcgen05 kernel rounds the weights once to fp16 and converts x to fp16
@@ -104,8 +106,10 @@ long long hq4_gemm_workspace_bytes(int n_out, int n_in, int m);
  * K-split cluster size, token tiles, tokens per tile, activation stages,
  * shared memory bytes, packed-weight ring slots, kernel (0: tcgen05 with the
  * A operand in TMEM, for larger token counts; 1: warp-level MMAs with the
- * weights exact as 128+q in bf16, for up to 16 bf16 / 8 fp32 tokens).
- * No reference counterpart. */
+ * weights exact as 128+q in bf16, for up to 16 bf16 / 8 fp32 tokens; 2: one
+ * token through the streaming GEMV of hq4_gemv, info[0..6] then 0 -- reported
+ * for group size 64 with 16-byte aligned scales and biases, which that kernel
+ * needs; other one-token calls take kernel 1).  No reference counterpart. */
 int hq4_gemm_plan(int n_out, int n_in, int m, int x_is_f32, int* info);
 
 /* hq4_gemm_w4a16 without a caller workspace: the workspace is a fixed

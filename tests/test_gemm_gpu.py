@@ -5,6 +5,8 @@ Two kernels sit behind the entry point (hq4_gemm_plan says which):
   bf16 hi + lo -- checked against the full-precision product (the
   reference's float path, out = x . (q*s+b)^T, hetero/cpu_model.py QLinear,
   kernel/q4gemv.c:113-139 per token) to 2e-5 (bf16 x) / 5e-5 (fp32 x);
+* one token: hq4_gemv's streaming kernel (weights exact, x widened to fp32)
+  -- the register path's bars;
 * tcgen05 path: weights rounded once to fp16, x to fp16 -- checked against
   that exact fp16-operand product in float64 (<= 1e-5: only fp32
   accumulation order differs) and against the full-precision product at the
@@ -74,6 +76,9 @@ SHAPES = [
     (1024, 2048, 6, 64, "f32"),           # register path, hi/lo tokens
     (2048, 4096, 32, 64, "bf16"),         # tcgen05 path, 32 tokens
     (3584, 18944, 7, 128, "f32"),         # register path, K split, gs 128
+    (18944, 3584, 1, 64, "bf16"),         # one token: the streaming GEMV
+    (3584, 18944, 1, 64, "f32"),          # one token, fp32 x
+    (512, 1024, 1, 128, "bf16"),          # one token, gs 128
 ]
 
 
@@ -90,7 +95,7 @@ def test_gemm_matches_exact_and_reference(cuda, ci):
     exact, spec = _refs(dw, ds, db, x, gs)
     plan = ops.gemm_plan(n_out, n_in, m, xd == "f32")
     e1, e2 = rel_l2(y, exact), rel_l2(y, spec)
-    if plan["kernel"] == "mma.sync":
+    if plan["kernel"] in ("mma.sync", "gemv"):
         assert e2 <= (5e-5 if xd == "f32" else 2e-5), f"{SHAPES[ci]}: vs full precision {e2:.2e} ({plan})"
     else:
         assert e1 <= EXACT_TOL, f"{SHAPES[ci]}: vs fp16-operand product {e1:.2e} ({plan})"

@@ -121,3 +121,51 @@ def test_argmax_pair_and_pick_token_match_numpy_over_shards(lib):
         assert lib.hq4_pick_token(pairs.data_ptr(), world, tok.data_ptr(), hist.data_ptr(), 2, st) == 0
         torch.cuda.synchronize()
         assert int(tok.item()) == int(z.argmax()) == int(hist[2].item()), (trial, world)
+
+
+def _attention_ref(q, kc, vc, p0, n_heads, n_kv, scale):
+    """float64 restatement of the reference's sdpa (hetero/cpu_model.py:233-252)
+    for the decode layout: query token i sits at position p0 + i and attends
+    to cache rows [0, p0 + i]."""
+    L, H, D = q.shape
+    G = n_heads // n_kv
+    out = np.zeros((L, H, D))
+    for i in range(L):
+        n = p0 + i + 1
+        for h in range(H):
+            k = kc[h // G, :n].astype(np.float64)
+            v = vc[h // G, :n].astype(np.float64)
+            s = k @ q[i, h].astype(np.float64) * scale
+            e = np.exp(s - s.max())
+            out[i, h] = (e / e.sum()) @ v
+    return out
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("n_heads,n_kv,head_dim,p0,n_tokens", [
+    (28, 4, 128, 0, 1),       # first token: one key
+    (28, 4, 128, 37, 1),
+    (28, 4, 128, 480, 1),     # long context: two key rounds per thread
+    (28, 4, 128, 10, 5),      # prefill rows, causal
+    (8, 8, 64, 100, 3),       # no grouping, head_dim 64
+    (4, 1, 256, 300, 2),      # head_dim 256: two value-pass column rounds
+])
+def test_attention_matches_float64_sdpa(lib, n_heads, n_kv, head_dim, p0, n_tokens):
+    import torch
+    max_ctx = 512
+    rng = np.random.default_rng(p0 + head_dim)
+    q = rng.standard_normal((n_tokens, n_heads, head_dim)).astype(np.float32)
+    kc = rng.standard_normal((n_kv, max_ctx, head_dim)).astype(np.float32)
+    vc = rng.standard_normal((n_kv, max_ctx, head_dim)).astype(np.float32)
+    scale = float(1.0 / np.sqrt(head_dim))
+    dq, dk, dv = (torch.from_numpy(a).cuda() for a in (q, kc, vc))
+    out = torch.full((n_tokens, n_heads, head_dim), float("nan"), device="cuda")
+    pos = torch.tensor([p0], dtype=torch.int32, device="cuda")
+    rc = lib.hq4_attention(dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), out.data_ptr(), n_heads, n_kv, head_dim,
+                           max_ctx, pos.data_ptr(), n_tokens, scale, torch.cuda.current_stream().cuda_stream)
+    assert rc == 0
+    torch.cuda.synchronize()
+    ref = _attention_ref(q, kc, vc, p0, n_heads, n_kv, scale)
+    got = out.cpu().numpy().astype(np.float64)
+    err = np.linalg.norm(got - ref) / np.linalg.norm(ref)
+    assert err < 2e-6, err
