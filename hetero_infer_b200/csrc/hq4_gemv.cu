@@ -1234,6 +1234,21 @@ extern "C" int hq4_gemv_fused(const uint32_t* w, const uint16_t* scales, const u
     return HQ4_OK;
 }
 
+extern "C" int hq4_gemv_host(const uint32_t* w, const uint16_t* scales, const uint16_t* biases,
+                             const float* row_add, const float* x_host, float* out_host, int n_out, int n_in,
+                             int gs, int m, float* x_dev, float* out_dev, void* stream) {
+    if (int rc = check_device()) return rc;
+    if (m <= 0 || n_out <= 0 || n_in <= 0 || !x_host || !out_host || !x_dev || !out_dev) return HQ4_ERR_SHAPE;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const size_t in_bytes = (size_t)m * n_in * sizeof(float), out_bytes = (size_t)m * n_out * sizeof(float);
+    if (cudaMemcpyAsync(x_dev, x_host, in_bytes, cudaMemcpyHostToDevice, st) != cudaSuccess) return HQ4_ERR_LAUNCH;
+    if (int rc = hq4_gemv_fused(w, scales, biases, x_dev, out_dev, n_out, n_in, gs, m, row_add, nullptr, stream))
+        return rc;
+    if (cudaMemcpyAsync(out_host, out_dev, out_bytes, cudaMemcpyDeviceToHost, st) != cudaSuccess)
+        return HQ4_ERR_LAUNCH;
+    return cudaStreamSynchronize(st) == cudaSuccess ? HQ4_OK : HQ4_ERR_LAUNCH;
+}
+
 extern "C" int hq4_dequant(const uint32_t* w, const uint16_t* scales, const uint16_t* biases,
                            float* out, int row0, int row1, int n_in, int gs, void* stream) {
     if (int rc = check_device()) return rc;

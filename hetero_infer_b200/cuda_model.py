@@ -17,7 +17,7 @@ from typing import Optional
 import numpy as np
 import torch
 
-from . import ops
+from . import _lib, ops
 
 
 def _dev_array(a, dtype=None, device="cuda"):
@@ -32,6 +32,13 @@ def _dev_array(a, dtype=None, device="cuda"):
     if dtype is not None:
         t = t.to(dtype)
     return t.to(device).contiguous()
+
+
+def _raw_stream(idx: int) -> int:
+    """Handle of the current CUDA stream of device idx (without building a
+    Stream object on every call)."""
+    get = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+    return get(idx) if get is not None else torch.cuda.current_stream(idx).cuda_stream
 
 
 class _Pinned:
@@ -67,6 +74,9 @@ class QLinear:
         self.biases = _dev_array(biases, torch.float16, self.device)
         self.bias = None if bias is None else _dev_array(bias, torch.float32, self.device)
         self._pinned = _Pinned()
+        self._ptrs = (self.w.data_ptr(), self.scales.data_ptr(), self.biases.data_ptr(),
+                      None if self.bias is None else self.bias.data_ptr())
+        self._stage = None  # (rows, pinned x, pinned y, device x, device y, x view, y view)
 
     def forward_device(self, x: torch.Tensor, out: Optional[torch.Tensor] = None,
                        residual: Optional[torch.Tensor] = None) -> torch.Tensor:
@@ -74,21 +84,40 @@ class QLinear:
         return ops.q4_gemv_fused(self.w, self.scales, self.biases, x.contiguous(),
                                  self.group_size, self.bias, residual, out)
 
+    def _staging(self, m: int):
+        """Pinned host and device staging for m rows (grow-only)."""
+        st = self._stage
+        if st is None or st[0] < m:
+            hx = torch.empty((m, self.n_in), dtype=torch.float32, pin_memory=True)
+            hy = torch.empty((m, self.n_out), dtype=torch.float32, pin_memory=True)
+            dx = torch.empty((m, self.n_in), dtype=torch.float32, device=self.device)
+            dy = torch.empty((m, self.n_out), dtype=torch.float32, device=self.device)
+            st = self._stage = (m, hx, hy, dx, dy, hx.numpy(), hy.numpy(),
+                                (hx.data_ptr(), hy.data_ptr(), dx.data_ptr(), dy.data_ptr()))
+        return st
+
     def __call__(self, x):
         if isinstance(x, torch.Tensor) and x.is_cuda:
             return self.forward_device(x)
-        # host path: NumPy in, NumPy out (the reference's calling convention)
+        # host path: NumPy in, NumPy out (the reference's calling convention);
+        # one C call copies x in, runs the GEMV, copies the result back and
+        # waits -- q4_gemv's own synchronous host-buffer contract
         xa = np.asarray(x, dtype=np.float32)
         lead = xa.shape[:-1]
         flat = xa.reshape(-1, self.n_in)
-        h_in = self._pinned.get("x", flat.shape, torch.float32)
-        h_in.numpy()[...] = flat
-        d_in = h_in.to(self.device, non_blocking=True)
-        d_out = self.forward_device(d_in)
-        h_out = self._pinned.get("y", (flat.shape[0], self.n_out), torch.float32)
-        h_out.copy_(d_out, non_blocking=True)
-        torch.cuda.current_stream(self.device).synchronize()
-        return h_out.numpy().copy().reshape(*lead, self.n_out)
+        m = flat.shape[0]
+        *_, hxn, hyn, (hxp, hyp, dxp, dyp) = self._staging(m)
+        np.copyto(hxn[:m], flat)
+        w, s, b, bias = self._ptrs
+        idx = self.device.index if self.device.index is not None else torch.cuda.current_device()
+        if torch.cuda.current_device() != idx:
+            with torch.cuda.device(idx):
+                return self.__call__(x)
+        rc = _lib.load().hq4_gemv_host(w, s, b, bias, hxp, hyp, self.n_out, self.n_in, self.group_size, m,
+                                       dxp, dyp, _raw_stream(idx))
+        if rc:
+            _lib.check(rc, "hq4_gemv_host")
+        return hyn[:m].copy().reshape(*lead, self.n_out)
 
 
 # ---------------------------------------------------------------------------

@@ -65,6 +65,17 @@ int hq4_gemv_fused(const uint32_t* w, const uint16_t* scales, const uint16_t* bi
                    const float* x, float* out, int n_out, int n_in, int gs, int m,
                    const float* row_add, const float* residual, void* stream);
 
+/* hq4_gemv_fused with the activations and outputs in host memory, the
+ * calling convention of q4_gemv itself (kernel/q4gemv.c:232: host x and out,
+ * the call returns when out is written).  The weights stay on the device;
+ * x_host [m][n_in] is copied to x_dev, the product (+ row_add) is written to
+ * out_dev and copied to out_host, and the call waits for `stream`.  x_dev and
+ * out_dev are caller-owned device buffers of at least m*n_in and m*n_out
+ * floats; pinned host buffers keep the copies at full speed. */
+int hq4_gemv_host(const uint32_t* w, const uint16_t* scales, const uint16_t* biases,
+                  const float* row_add, const float* x_host, float* out_host, int n_out, int n_in,
+                  int gs, int m, float* x_dev, float* out_dev, void* stream);
+
 /* Rows [row0,row1) of W expanded to fp32 into out [row1-row0][n_in].
  * Replaces  int q4_dequant(w, scales, biases, out, row0, row1, n_in, gs,
  * nthreads)  (kernel/q4gemv.c:359-360).  Bit-exact with the reference. */

@@ -153,3 +153,39 @@ def test_gemv_rejects_bad_shapes(cuda):
         ops.q4_gemv(to_dev(w), to_dev(s), to_dev(b), to_dev(x), 96)   # gs=96 unsupported
     with pytest.raises(RuntimeError):
         ops.q4_gemv(to_dev(w), to_dev(s), to_dev(b), torch.from_numpy(x), 64)  # host x
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("m,with_bias", [(1, False), (1, True), (3, True)])
+def test_qlinear_host_path_matches_oracle(oracle, cuda, m, with_bias):
+    """The reference's calling convention (hetero/cpu_model.py QLinear: NumPy
+    in, NumPy out) through hq4_gemv_host: copy in, GEMV (+ bias), copy out,
+    synchronous.  Same numbers as the device path and the float path."""
+    from hetero_infer_b200 import cuda_model, ops
+    n_out, n_in, gs = 4608, 3584, 64
+    w, s, b, x = make_case(n_out, n_in, gs, seed=41 + m, m=m)
+    bias = np.random.default_rng(m).standard_normal(n_out).astype(np.float32) if with_bias else None
+    q = cuda_model.QLinear(w, s, b, bias, gs, 4, device="cuda")
+    y = q(x)
+    assert isinstance(y, np.ndarray) and y.shape == (m, n_out)
+    ref = oracle.gemv_f32(w, s, b, x, gs) + (0 if bias is None else bias)
+    assert rel_l2(y, ref) <= OUR_TOL
+    yd = q(to_dev(x)).cpu().numpy()
+    assert np.array_equal(y, yd)
+    y2 = q(x[0]) if m == 1 else None          # a 1-D activation keeps its shape
+    if y2 is not None:
+        assert y2.shape == (n_out,) and np.array_equal(y2, y[0])
+
+
+@pytest.mark.gpu
+def test_gemv_host_rejects_missing_buffers(cuda):
+    import torch
+    from hetero_infer_b200 import _lib
+    lib = _lib.load()
+    d = torch.zeros(16, device="cuda")
+    h = torch.zeros(16).pin_memory()
+    st = torch.cuda.current_stream().cuda_stream
+    assert lib.hq4_gemv_host(d.data_ptr(), d.data_ptr(), d.data_ptr(), None, h.data_ptr(), None, 16, 64, 64, 1,
+                             d.data_ptr(), d.data_ptr(), st) == -1
+    assert lib.hq4_gemv_host(d.data_ptr(), d.data_ptr(), d.data_ptr(), None, h.data_ptr(), h.data_ptr(), 16, 64, 64,
+                             0, d.data_ptr(), d.data_ptr(), st) == -1
