@@ -190,6 +190,62 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(
     }
 }
 
+// ---- int8 activation codec (hetero/transport.py:198-225) ----------------------
+// The pipeline hand-off at half the bytes of fp16: per row an fp32 scale
+// amax/127 (1 for an all-zero row) and int8 q = clip(rint(x / scale), +-127);
+// decoded as fp16(q * scale).  Every step is one IEEE fp32 operation in the
+// reference's order (max of |x|, division, round-half-even, clip; multiply,
+// round to fp16), so both directions are bit-identical to the NumPy codec.
+// Payload layout as the reference's bytes: [rows] fp32 scales, then
+// [rows][cols] int8.  (Non-finite inputs are outside the codec's contract.)
+constexpr int kCodecThreads = 256;
+
+__global__ void __launch_bounds__(kCodecThreads) act_encode_i8_kernel(const float* __restrict__ x, int rows, int cols,
+                                                                     unsigned char* __restrict__ payload) {
+    __shared__ float red[kCodecThreads / 32];
+    __shared__ float s_scale;
+    pdl_launch_dependents();
+    pdl_wait();
+    const int r = blockIdx.x;
+    const float* xr = x + (size_t)r * cols;
+    float amax = 0.0f;
+    for (int i = threadIdx.x; i < cols; i += kCodecThreads) amax = fmaxf(amax, fabsf(xr[i]));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float m = red[0];
+        for (int j = 1; j < kCodecThreads / 32; j++) m = fmaxf(m, red[j]);
+        float sc = __fdiv_rn(m, 127.0f);
+        if (sc == 0.0f) sc = 1.0f;
+        s_scale = sc;
+        reinterpret_cast<float*>(payload)[r] = sc;
+    }
+    __syncthreads();
+    const float sc = s_scale;
+    signed char* q = reinterpret_cast<signed char*>(payload + (size_t)rows * 4 + (size_t)r * cols);
+    for (int i = threadIdx.x; i < cols; i += kCodecThreads) {
+        const float v = fminf(fmaxf(rintf(__fdiv_rn(xr[i], sc)), -127.0f), 127.0f);
+        q[i] = (signed char)(int)v;
+    }
+}
+
+__global__ void __launch_bounds__(kCodecThreads) act_decode_i8_kernel(const unsigned char* __restrict__ payload,
+                                                                     int rows, int cols, __half* __restrict__ out16,
+                                                                     float* __restrict__ out32) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const float* scales = reinterpret_cast<const float*>(payload);
+    const signed char* q = reinterpret_cast<const signed char*>(payload + (size_t)rows * 4);
+    const size_t n = (size_t)rows * cols;
+    for (size_t i = (size_t)blockIdx.x * kCodecThreads + threadIdx.x; i < n; i += (size_t)gridDim.x * kCodecThreads) {
+        const __half h = __float2half_rn(__fmul_rn((float)q[i], scales[i / cols]));
+        if (out16) out16[i] = h;
+        if (out32) out32[i] = __half2float(h);
+    }
+}
+
 // ---- argmax --------------------------------------------------------------------
 // numpy argmax order (hetero/backends.py:106-109 calls z.argmax()): a NaN is
 // above every number and the first NaN wins; otherwise the largest value,
@@ -378,6 +434,26 @@ static int launch_argmax_cluster(cudaStream_t st, const float* x, int n, int* id
                               offset) == cudaSuccess
                ? HQ4_OK
                : HQ4_ERR_LAUNCH;
+}
+
+extern "C" int hq4_act_encode_i8(const float* x, int rows, int cols, void* payload, void* stream) {
+    if (int rc = check_device_cap()) return rc;
+    if (rows <= 0 || cols <= 0 || !x || !payload) return HQ4_ERR_SHAPE;
+    if (((uintptr_t)x & 3) || ((uintptr_t)payload & 3)) return HQ4_ERR_ALIGN;
+    return launch_pdl(act_encode_i8_kernel, dim3(rows), dim3(kCodecThreads), 0, static_cast<cudaStream_t>(stream), x,
+                      rows, cols, static_cast<unsigned char*>(payload));
+}
+
+extern "C" int hq4_act_decode_i8(const void* payload, int rows, int cols, uint16_t* out_f16, float* out_f32,
+                                 void* stream) {
+    if (int rc = check_device_cap()) return rc;
+    if (rows <= 0 || cols <= 0 || !payload || (!out_f16 && !out_f32)) return HQ4_ERR_SHAPE;
+    if (((uintptr_t)payload & 3) || ((uintptr_t)out_f16 & 1) || ((uintptr_t)out_f32 & 3)) return HQ4_ERR_ALIGN;
+    const long long n = (long long)rows * cols;
+    const int grid = (int)std::min<long long>((n + kCodecThreads - 1) / kCodecThreads, 1184);
+    return launch_pdl(act_decode_i8_kernel, dim3(grid), dim3(kCodecThreads), 0, static_cast<cudaStream_t>(stream),
+                      static_cast<const unsigned char*>(payload), rows, cols, reinterpret_cast<__half*>(out_f16),
+                      out_f32);
 }
 
 extern "C" int hq4_argmax(const float* x, int n, int* idx_out, int* history, int hist_len,

@@ -174,3 +174,31 @@ def gemm_plan(n_out: int, n_in: int, m: int, x_is_f32: bool = False) -> dict:
     d = dict(zip(keys, list(info)))
     d["kernel"] = {0: "tcgen05", 1: "mma.sync", 2: "gemv"}[d["kernel"]]
     return d
+
+
+def act_encode_i8(x: torch.Tensor, payload: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """int8 wire payload of fp32 activations [..., cols] (hetero/transport.py:198-211):
+    the rows' fp32 scales then the int8 rows, as a uint8 tensor."""
+    xs = x.contiguous()
+    cols = int(xs.shape[-1])
+    rows = xs.numel() // cols
+    if payload is None:
+        payload = torch.empty(rows * (4 + cols), dtype=torch.uint8, device=xs.device)
+    lib = _lib.load()
+    _lib.check(lib.hq4_act_encode_i8(xs.data_ptr(), rows, cols, payload.data_ptr(),
+                                     torch.cuda.current_stream(xs.device).cuda_stream), "hq4_act_encode_i8")
+    return payload
+
+
+def act_decode_i8(payload: torch.Tensor, rows: int, cols: int, dtype=torch.float16,
+                  out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Activations [rows, cols] from an int8 wire payload (hetero/transport.py:214-225):
+    fp16(q * scale), or that value widened to fp32 when dtype is float32."""
+    if out is None:
+        out = torch.empty((rows, cols), dtype=dtype, device=payload.device)
+    lib = _lib.load()
+    f16 = out.data_ptr() if out.dtype == torch.float16 else None
+    f32 = out.data_ptr() if out.dtype == torch.float32 else None
+    _lib.check(lib.hq4_act_decode_i8(payload.data_ptr(), rows, cols, f16, f32,
+                                     torch.cuda.current_stream(payload.device).cuda_stream), "hq4_act_decode_i8")
+    return out

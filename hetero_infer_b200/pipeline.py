@@ -108,9 +108,11 @@ class PipelineRank:
     """One rank's side of the pipelined decode.
 
     compute: object with
-      hidden_dim, wire_dtype (torch.float16: the reference's format),
+      hidden_dim, wire_empty(rows) -> receive buffer of the wire format on the
+      comm device (fp16 is the reference's format; fp32 and the reference's
+      int8 codec are the others),
       new_cache(), embed_forward(ids, cache) -> h, forward(h, cache) -> h,
-      to_wire(h) -> wire_dtype tensor on the comm device, from_wire(t) -> h,
+      to_wire(h) -> wire tensor on the comm device, from_wire(t) -> h,
       to_comm32(h_last) -> fp32 [H] tensor on the comm device,
       head(h32) -> (max value, global index) of this rank's vocabulary shard.
     """
@@ -187,8 +189,7 @@ class PipelineRank:
                     if not self.last:
                         self.comm.exchange(self.c.to_wire(h), None)
                 elif r == s + 1:
-                    wire_in = torch.empty((1, P, self.c.hidden_dim), dtype=self.c.wire_dtype,
-                                          device=self.comm.device)
+                    wire_in = self.c.wire_empty(P)
                     self.comm.exchange(None, wire_in)
             self._record(m, self._head(h if self.last else None, m))
 
@@ -205,7 +206,7 @@ class PipelineRank:
             mine = adm[t - r] if 0 <= t - r < len(adm) else -1
             recv = None
             if r > 0 and mine >= 0:
-                recv = torch.empty((1, 1, H), dtype=self.c.wire_dtype, device=self.comm.device)
+                recv = self.c.wire_empty(1)
             self.comm.exchange(out_prev if (not self.last and out_prev is not None) else None, recv)
             out_prev = None
             h = None
@@ -231,16 +232,20 @@ class DeviceCompute:
     argmax with value).
 
     wire: "float16" is the reference's hand-off (backends.py:100-104; values
-    beyond fp16 range become inf there and here alike); "float32" sends the
-    fp32 hidden state unchanged, so the pipelined model computes exactly what
-    one unsplit stage computes (not a reference format)."""
+    beyond fp16 range become inf there and here alike); "int8" is the
+    reference's int8 codec (transport.py:198-225: per-row fp32 scale + int8,
+    half the bytes; encoded and decoded on the device, bit-identical to the
+    NumPy codec); "float32" sends the fp32 hidden state unchanged, so the
+    pipelined model computes exactly what one unsplit stage computes (not a
+    reference format)."""
 
     def __init__(self, cfg: dict, spec, weights: Dict[str, np.ndarray], head_rows: tuple,
                  device: torch.device, max_ctx: int = 1024, wire: str = "float16"):
         from . import _lib, cuda_model
-        if wire not in ("float16", "float32"):
-            raise ValueError(f"wire must be float16 or float32, not {wire!r}")
-        self.wire_dtype = getattr(torch, wire)
+        if wire not in ("float16", "float32", "int8"):
+            raise ValueError(f"wire must be float16, float32 or int8, not {wire!r}")
+        self.wire = wire
+        self.wire_dtype = torch.uint8 if wire == "int8" else getattr(torch, wire)
         self.cfg, self.device = cfg, device
         self.hidden_dim = cfg["hidden_size"]
         self.stage = cuda_model.Stage(cfg, spec, weights, device=device, max_ctx=max_ctx)
@@ -295,14 +300,14 @@ class DeviceCompute:
         st = self.stage
         H = self.hidden_dim
         static_in = (torch.zeros((1, 1), dtype=torch.int32, device=self.device) if first
-                     else torch.zeros((1, 1, H), dtype=self.wire_dtype, device=self.device))
-        static_wire = None if last else torch.empty((1, 1, H), dtype=self.wire_dtype, device=self.device)
+                     else self.wire_empty(1).zero_())
+        static_wire = None if last else self.wire_empty(1)
         static_h = torch.empty((1, 1, H), dtype=torch.float32, device=self.device)
         side = torch.cuda.Stream(self.device)
         side.wait_stream(torch.cuda.current_stream(self.device))
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph, stream=side, capture_error_mode="thread_local"):
-            h = st.embed(static_in) if first else static_in.to(torch.float32)
+            h = st.embed(static_in) if first else self.from_wire(static_in)
             h = h.reshape(1, H).contiguous()
             for i in range(len(st.layers)):
                 st.layer_forward(i, h, cache, 1)
@@ -310,15 +315,36 @@ class DeviceCompute:
                 st._check(st.lib.hq4_advance_position(cache.pos.data_ptr(), 1, st._stream()),
                           "hq4_advance_position")
             if static_wire is not None:
-                static_wire.copy_(h.view(1, 1, H).to(self.wire_dtype))
+                self._encode_into(h, static_wire)
             static_h.copy_(h.view(1, 1, H))
         torch.cuda.current_stream(self.device).wait_stream(side)
         return static_in, static_wire, static_h, graph
 
+    def wire_empty(self, rows: int) -> torch.Tensor:
+        H = self.hidden_dim
+        if self.wire == "int8":
+            return torch.empty(rows * (4 + H), dtype=torch.uint8, device=self.device)
+        return torch.empty((1, rows, H), dtype=self.wire_dtype, device=self.device)
+
+    def _encode_into(self, h, dst):
+        if self.wire == "int8":
+            from . import ops
+            ops.act_encode_i8(h.reshape(-1, self.hidden_dim), payload=dst)
+        else:
+            dst.copy_(h.view(dst.shape).to(self.wire_dtype))
+
     def to_wire(self, h):
-        return h.to(self.wire_dtype).contiguous()
+        rows = h.numel() // self.hidden_dim
+        t = self.wire_empty(rows)
+        self._encode_into(h.contiguous(), t)
+        return t
 
     def from_wire(self, t):
+        H = self.hidden_dim
+        if self.wire == "int8":
+            from . import ops
+            rows = t.numel() // (4 + H)
+            return ops.act_decode_i8(t, rows, H, dtype=torch.float32).view(1, rows, H)
         return t.to(torch.float32)
 
     def to_comm32(self, h):
@@ -363,10 +389,12 @@ class OracleCompute:
     """The same on the CPU with the NumPy stage oracle (test infrastructure:
     lets the schedule and communication run under gloo without a GPU)."""
 
-    wire_dtype = torch.float16
-
     def __init__(self, cfg: dict, start: int, end: int, weights: Dict[str, np.ndarray], head_rows: tuple,
-                 embed_rows=None):
+                 embed_rows=None, wire: str = "float16"):
+        if wire not in ("float16", "int8"):
+            raise ValueError(f"wire must be float16 or int8, not {wire!r}")
+        self.wire = wire
+        self.wire_dtype = torch.uint8 if wire == "int8" else torch.float16
         from oracle import stage as ost
         self.cfg, self.hidden_dim = cfg, cfg["hidden_size"]
         self.stage = ost.OracleStage(cfg, weights, start, end, start == 0, False, embed_rows=embed_rows)
@@ -390,10 +418,22 @@ class OracleCompute:
         h = self.embed_forward(src, cache) if first else self.forward(self.from_wire(src), cache)
         return (None if last else self.to_wire(h)), h
 
+    def wire_empty(self, rows: int) -> torch.Tensor:
+        if self.wire == "int8":
+            return torch.empty(rows * (4 + self.hidden_dim), dtype=torch.uint8)
+        return torch.empty((1, rows, self.hidden_dim), dtype=torch.float16)
+
     def to_wire(self, h):
+        if self.wire == "int8":
+            from oracle import codec
+            return torch.frombuffer(bytearray(codec.encode_i8(np.asarray(h, np.float32))), dtype=torch.uint8)
         return torch.from_numpy(np.ascontiguousarray(np.asarray(h, dtype=np.float16)))
 
     def from_wire(self, t):
+        if self.wire == "int8":
+            from oracle import codec
+            rows = t.numel() // (4 + self.hidden_dim)
+            return codec.decode_i8(t.numpy().tobytes(), (1, rows, self.hidden_dim)).astype(np.float32)
         return t.numpy().astype(np.float32)
 
     def to_comm32(self, h):

@@ -186,6 +186,17 @@ int hq4_attention(const float* q, const float* k_cache, const float* v_cache, fl
                   int n_heads, int n_kv, int head_dim, int max_ctx, const int* pos,
                   int n_tokens, float scale, void* stream);
 
+/* int8 activation codec, the reference's pipeline hand-off at half the bytes
+ * of fp16 (hetero/transport.py:198-225).  payload = [rows] fp32 scales then
+ * [rows][cols] int8 -- byte for byte what transport.encode(x, "int8")
+ * returns as its payload.  encode: scale = max|x_row| / 127 (1 for an
+ * all-zero row), q = clip(rint(x / scale), -127, 127).  decode: fp16(q *
+ * scale) into out_f16 and/or, widened exactly, into out_f32 (either may be
+ * NULL, not both).  Bit-identical to the NumPy codec for finite inputs. */
+int hq4_act_encode_i8(const float* x, int rows, int cols, void* payload, void* stream);
+int hq4_act_decode_i8(const void* payload, int rows, int cols, uint16_t* out_f16, float* out_f32,
+                      void* stream);
+
 /* Greedy sampling (hetero/backends.py:106-109): numpy argmax of x[0..n) --
  * the first NaN if there is one, else the largest value, lowest index among
  * equals (the result is always in [0, n)) -- written to *idx_out; also to history[*pos] when

@@ -1,8 +1,9 @@
 """The pipelined decode (hetero_infer_b200/pipeline.py) on CPU ranks over gloo,
 with the NumPy stage oracle as the compute: the schedule, the grouped
-send/recv of the fp16 wire, the broadcast + row-sharded head + all-gather must
+send/recv of the wire, the broadcast + row-sharded head + all-gather must
 give every microbatch the tokens of a single-process run of the same stages
-joined by the reference's fp16 wire (hetero/backends.py:100-104)."""
+joined by the reference's fp16 wire (hetero/backends.py:100-104) or its int8
+codec (hetero/transport.py:198-225)."""
 import os
 import socket
 
@@ -24,8 +25,10 @@ def _free_port():
     return p
 
 
-def reference_tokens(cuts):
-    """Single process: stage slices joined by the fp16 wire, full head."""
+def reference_tokens(cuts, wire="float16"):
+    """Single process: stage slices joined by the wire (the reference's fp16
+    conversion, or its int8 codec), full head."""
+    from oracle import codec
     from oracle import stage as ost
     cfg = synth.small_config(**CFG)
     w = synth.model_weights(cfg, SEED)
@@ -41,7 +44,10 @@ def reference_tokens(cuts):
             h = x
             for i, s in enumerate(stages):
                 h = s(h, caches[i], apply_head=True, last_only=True)
-                if i < len(stages) - 1:
+                if i < len(stages) - 1 and wire == "int8":
+                    h = np.asarray(h, np.float32)
+                    h = codec.decode_i8(codec.encode_i8(h), h.shape).astype(np.float32)
+                elif i < len(stages) - 1:
                     h = np.asarray(h, np.float16).astype(np.float32)
             toks.append(int(np.asarray(h)[0, -1].argmax()))
             x = np.array([[toks[-1]]])
@@ -49,7 +55,7 @@ def reference_tokens(cuts):
     return out
 
 
-def _rank_main(rank, world, port, cuts, q):
+def _rank_main(rank, world, port, cuts, q, wire="float16"):
     import torch
     import torch.distributed as dist
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
@@ -59,7 +65,8 @@ def _rank_main(rank, world, port, cuts, q):
         a, b = cuts[rank], cuts[rank + 1]
         w = synth.model_weights(cfg, SEED, layers=range(a, b), embed=(rank == 0), head=True)
         comp = pipeline.OracleCompute(cfg, a, b, w, pipeline.head_rows(cfg["vocab_size"], world, rank),
-                                      embed_rows=lambda ids: synth.embed_rows(SEED, ids, cfg["hidden_size"]))
+                                      embed_rows=lambda ids: synth.embed_rows(SEED, ids, cfg["hidden_size"]),
+                                      wire=wire)
         pr = pipeline.PipelineRank(pipeline.Comm(rank, world, torch.device("cpu")), comp, N_MICRO)
         pr.prefill([synth.prompt_ids(100 + m, PROMPT, cfg["vocab_size"]) for m in range(N_MICRO)])
         pr.decode(STEPS)
@@ -68,20 +75,20 @@ def _rank_main(rank, world, port, cuts, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("cuts", [[0, 2, 3], [0, 1, 2, 3]])
-def test_gloo_pipeline_matches_single_process(cuts):
+@pytest.mark.parametrize("cuts,wire", [([0, 2, 3], "float16"), ([0, 1, 2, 3], "float16"), ([0, 1, 2, 3], "int8")])
+def test_gloo_pipeline_matches_single_process(cuts, wire):
     world = len(cuts) - 1
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank_main, args=(r, world, port, cuts, q)) for r in range(world)]
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, cuts, q, wire)) for r in range(world)]
     for p in procs:
         p.start()
     got = dict(q.get(timeout=240) for _ in procs)
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
-    ref = reference_tokens(cuts)
+    ref = reference_tokens(cuts, wire)
     for r in range(world):
         assert got[r] == ref, f"rank {r}"
 

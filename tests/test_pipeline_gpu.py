@@ -81,11 +81,15 @@ def _run(world, case):
 
 
 @pytest.mark.gpu
-def test_nccl_pipeline_two_gpus_matches_single_process():
+@pytest.mark.parametrize("wire", ["float16", "int8"])
+def test_nccl_pipeline_two_gpus_matches_single_process(wire):
+    """The device codec (hq4_act_encode_i8 / decode, bit-identical to the
+    reference's NumPy codec) on the NCCL wire gives the tokens of the oracle
+    stages joined by the reference's codec."""
     cuts = [0, 2, 3]
-    got = _run(2, dict(model="small", cuts=cuts, seed=SEED, wire="float16", prompt_len=PROMPT,
+    got = _run(2, dict(model="small", cuts=cuts, seed=SEED, wire=wire, prompt_len=PROMPT,
                        prompt_seeds=[100 + m for m in range(N_MICRO)], steps=STEPS))
-    assert got == reference_tokens(cuts)
+    assert got == reference_tokens(cuts, wire)
 
 
 @pytest.mark.gpu
