@@ -250,6 +250,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     pipe = None
     if world > 1 and not args.no_extras:
         pipe = {f"micro{m}": pipeline_bench(rank, world, dev, m) for m in (4, 8)}
+        pipe["micro8_int8_wire"] = pipeline_bench(rank, world, dev, 8, wire="int8")
     result = None
     if rank == 0:
         peak, peak_kind = measured_peak()
@@ -450,7 +451,8 @@ def decode_bench(dev, n_tokens: int = 128, prompt_len: int = 32):
             "setup_s": round(t_load, 1)}
 
 
-def pipeline_bench(rank: int, world: int, dev, n_micro: int, n_tokens: int = 256, prompt_len: int = 32):
+def pipeline_bench(rank: int, world: int, dev, n_micro: int, n_tokens: int = 256, prompt_len: int = 32,
+                   wire: str = "float16"):
     """Benchmark config 5: the 7B-shape random model split by the planner over
     the `world` GPUs (NCCL send/recv of the fp16 hidden state between stages,
     lm_head row-sharded over all ranks), `n_micro` independent streams in
@@ -465,7 +467,7 @@ def pipeline_bench(rank: int, world: int, dev, n_micro: int, n_tokens: int = 256
     spec = plan.specs[rank]
     w = synth.model_weights(cfg, 0, layers=range(spec.start, spec.end), embed=spec.embed, head=True)
     comp = pipeline.DeviceCompute(cfg, spec, w, pipeline.head_rows(cfg["vocab_size"], world, rank), dev,
-                                  max_ctx=512)
+                                  max_ctx=512, wire=wire)
     del w
     pr = pipeline.PipelineRank(pipeline.Comm(rank, world, dev), comp, n_micro)
     prompts = [synth.prompt_ids(1000 + m, prompt_len, cfg["vocab_size"]) for m in range(n_micro)]
@@ -484,7 +486,9 @@ def pipeline_bench(rank: int, world: int, dev, n_micro: int, n_tokens: int = 256
     return {"streams": n_micro, "tokens_per_stream": n_tokens, "decode_tokens": gen,
             "tok_s": round(gen / dt, 1), "seconds": round(dt, 3), "ticks": pr.ticks,
             "ms_per_tick": round(dt * 1e3 / pr.ticks, 4), "cuts": plan.cuts,
-            "head": "row-sharded over all ranks", "wire": "fp16 NCCL send/recv (reference format)",
+            "head": "row-sharded over all ranks",
+            "wire": ("fp16 NCCL send/recv (reference format)" if wire == "float16" else
+                     "int8 codec NCCL send/recv (reference transport codec, encoded/decoded on device)"),
             "first_tokens": pr.tokens[0][:6],
             "tokens_note": ("every token 0, as the reference's own stages produce on this model: its residual "
                             "stream exceeds fp16 range at the cut, the fp16 wire carries inf, the next RMSNorm "
@@ -642,6 +646,8 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
         out = {f"micro{m}": pipeline_bench(rank, world, dev, m, n_tokens=max(3, args.pipeline_only))
                for m in (4, 8)}
+        out["micro8_int8_wire"] = pipeline_bench(rank, world, dev, 8, n_tokens=max(3, args.pipeline_only),
+                                                 wire="int8")
         if rank == 0:
             print(json.dumps({"pipeline": out, "n_gpus": world}), flush=True)
         dist.destroy_process_group()
