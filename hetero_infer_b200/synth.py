@@ -179,3 +179,37 @@ def model_weights(cfg: dict, seed: int, layers: Optional[Iterable[int]] = None,
 def prompt_ids(seed: int, n: int, vocab: int) -> np.ndarray:
     """Uniform-random prompt token ids, shape [1, n]."""
     return rng_for(seed, "prompt").integers(0, vocab, size=(1, n)).astype(np.int64)
+
+
+def snapshot_weights(cfg: dict, seed: int, tied: bool = False) -> Dict[str, np.ndarray]:
+    """Every tensor of the model as an MLX-format checkpoint holds it: the
+    quantized layers and head of ``model_weights`` plus a quantized embedding
+    table (model.embed_tokens.{weight,scales,biases}); a tied model has no
+    lm_head tensors (its head is the embedding)."""
+    gs = cfg["quantization"]["group_size"]
+    out = model_weights(cfg, seed, embed=False, head=True)
+    w, s, b = q4_linear(seed, "model.embed_tokens", cfg["vocab_size"], cfg["hidden_size"], gs)
+    out["model.embed_tokens.weight"], out["model.embed_tokens.scales"], out["model.embed_tokens.biases"] = w, s, b
+    if tied:
+        for k in ("lm_head.weight", "lm_head.scales", "lm_head.biases"):
+            out.pop(k)
+    return out
+
+
+def write_snapshot(model_dir: str, cfg: dict, seed: int, files: int = 2, tied: bool = False) -> Dict[str, np.ndarray]:
+    """An MLX-format safetensors snapshot of the synthetic model: config.json
+    and `files` .safetensors files (tensors spread over them by sorted name).
+    Returns the tensors written."""
+    import json
+    import os
+    from safetensors.numpy import save_file
+    os.makedirs(model_dir, exist_ok=True)
+    w = snapshot_weights(cfg, seed, tied)
+    names = sorted(w)
+    for f in range(files):
+        part = {n: np.ascontiguousarray(w[n]) for i, n in enumerate(names) if i % files == f}
+        save_file(part, os.path.join(model_dir, f"model-{f + 1:05d}-of-{files:05d}.safetensors"))
+    conf = dict(cfg, tie_word_embeddings=bool(tied))
+    with open(os.path.join(model_dir, "config.json"), "w") as fh:
+        json.dump(conf, fh, indent=1, sort_keys=True)
+    return w
