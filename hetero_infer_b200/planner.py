@@ -209,8 +209,14 @@ def _plan(index, nodes, link, head_at, objective, max_ctx, batch, codec, kv_dtyp
     def mem(i, spec):
         return _resident(index, spec, nodes[i].weight_expansion) + spec.n_layers * kv + head_share_bytes
 
+    # a row-sharded head costs every stage, every token, its share of the
+    # head GEMV plus the two collectives that join the shards: the broadcast
+    # of the last stage's fp32 hidden state and the all-gather of the N
+    # (value, index) pairs
+    head_coll = (link.seconds_for(int(cfg["hidden_size"]) * 4) + link.seconds_for(8 * N)) if sharded_head else 0.0
+
     def share(i):
-        return nodes[i].head_s / N if sharded_head else 0.0
+        return nodes[i].head_s / N + head_coll if sharded_head else 0.0
 
     for i in range(N - 1, -1, -1):
         node = nodes[i]
@@ -255,13 +261,17 @@ def _plan(index, nodes, link, head_at, objective, max_ctx, batch, codec, kv_dtyp
 def plan_gpu_pipeline(cfg: dict, n_gpus: int, layer_s: float, head_s: float = 0.0,
                       embed_s: float = 0.0, mem_bytes: int = 160 * 2**30,
                       objective: str = "throughput", max_ctx: int = 2048,
-                      sharded_head: bool = True, link: Optional[LinkSpec] = None) -> Plan:
+                      sharded_head: bool = True, link: Optional[LinkSpec] = None,
+                      index=None, codec: str = "fp16") -> Plan:
     """Cut `cfg` over `n_gpus` identical GPUs of one box.  With sharded_head the
     vocabulary projection is row-sharded across every stage (each computes
-    V/N logits and a local argmax, reduced by an all-gather)."""
+    V/N logits and a local argmax, reduced by an all-gather; every stage pays
+    its share and the two collectives per token).  `index` gives the weight
+    bytes (a checkpoint.WeightIndex of a snapshot; by default they follow
+    from the config); `codec` is the wire format ("fp16" or "int8")."""
     nodes = [NodeProfile(f"gpu{i}", mem_bytes=mem_bytes, decode_s_per_layer=layer_s, embed_s=embed_s,
                          head_s=head_s) for i in range(n_gpus)]
-    index = ModelIndex(cfg)
+    index = index if index is not None else ModelIndex(cfg)
     link = link or LinkSpec()
     if n_gpus == 1:
         spec = ShardSpec(0, int(cfg["num_hidden_layers"]), True, True)
@@ -269,5 +279,5 @@ def plan_gpu_pipeline(cfg: dict, n_gpus: int, layer_s: float, head_s: float = 0.
                     predicted_decode_s=_stage_time(nodes[0], spec), stage_compute_s=[_stage_time(nodes[0], spec)],
                     stage_comm_s=[0.0], stage_mem_bytes=[index.total_bytes()])
     if sharded_head:
-        return _plan(index, nodes, link, -1, objective, max_ctx, 1, "fp16", 4, sharded_head=True)
-    return plan_pipeline(index, nodes, link, objective, max_ctx, 1, "fp16", 4)
+        return _plan(index, nodes, link, -1, objective, max_ctx, 1, codec, 4, sharded_head=True)
+    return plan_pipeline(index, nodes, link, objective, max_ctx, 1, codec, 4)
