@@ -423,32 +423,48 @@ def decode_bench(dev, n_tokens: int = 128, prompt_len: int = 32):
     del w
     t_load = time.perf_counter() - t0
     prompt = synth.prompt_ids(0, prompt_len, cfg["vocab_size"])
-    dec = cuda_model.GreedyDecoder(stage)
-    torch.cuda.synchronize(dev)
-    e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
-    e0.record(dec.stream)
-    dec.prefill(prompt)
-    e1.record(dec.stream)
-    dec.capture()
-    torch.cuda.synchronize(dev)
-    n_steps = n_tokens - 2
-    e1b = torch.cuda.Event(enable_timing=True)
-    e1b.record(dec.stream)
-    dec.steps(n_steps)
-    e2.record(dec.stream)
-    torch.cuda.synchronize(dev)
-    toks = dec.tokens()
-    ms = e1b.elapsed_time(e2)
     per_token_bytes = 28 * sum(alg_bytes(n, k) for _, n, k in PROJECTIONS) + alg_bytes(cfg["vocab_size"], HIDDEN)
-    tok_s = n_steps / (ms * 1e-3)
-    return {"tok_s": round(tok_s, 1), "ms_per_token": round(ms / n_steps, 4),
-            "ttft_ms": round(e0.elapsed_time(e1), 2), "generated": len(toks),
-            "prompt_tokens": prompt_len, "timed_steps": n_steps,
-            "weight_GB_per_s": round(per_token_bytes * tok_s / 1e9, 1),
-            "hbm_ceiling_tok_s": round(measured_peak()[0] * 1e9 / per_token_bytes, 1),
-            "launches_per_token": 28 * 5 + 4, "first_tokens": toks[:8],
-            "model": "qwen2-7b-shape random int4 (28 layers, h3584, 28q/4kv, i18944, v152064)",
-            "setup_s": round(t_load, 1)}
+
+    def run(persistent):
+        dec = cuda_model.GreedyDecoder(stage, persistent=persistent)
+        torch.cuda.synchronize(dev)
+        e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+        e0.record(dec.stream)
+        dec.prefill(prompt)
+        e1.record(dec.stream)
+        dec.capture()
+        torch.cuda.synchronize(dev)
+        n_steps = n_tokens - 2
+        e1b = torch.cuda.Event(enable_timing=True)
+        e1b.record(dec.stream)
+        dec.steps(n_steps)
+        e2.record(dec.stream)
+        torch.cuda.synchronize(dev)
+        toks = dec.tokens()
+        ms = e1b.elapsed_time(e2)
+        tok_s = n_steps / (ms * 1e-3)
+        out = {"tok_s": round(tok_s, 1), "ms_per_token": round(ms / n_steps, 4),
+               "ttft_ms": round(e0.elapsed_time(e1), 2), "generated": len(toks),
+               "prompt_tokens": prompt_len, "timed_steps": n_steps,
+               "weight_GB_per_s": round(per_token_bytes * tok_s / 1e9, 1),
+               "launches_per_token": 5 if dec.plan is not None else 28 * 5 + 4,
+               "persistent_layers": dec.plan is not None, "first_tokens": toks[:8]}
+        if dec.plan is not None:
+            out["plan"] = dec.plan.info()
+        dec.graph = None  # the graph holds the plan's launch: release it first
+        torch.cuda.synchronize(dev)
+        if dec.plan is not None:
+            dec.plan.close()
+        del dec
+        return out, toks
+
+    res, toks = run("auto")
+    res_layers, toks_layers = run(False)
+    res.update({"hbm_ceiling_tok_s": round(measured_peak()[0] * 1e9 / per_token_bytes, 1),
+                "per_layer_launches": res_layers, "tokens_equal_per_layer_path": toks == toks_layers,
+                "model": "qwen2-7b-shape random int4 (28 layers, h3584, 28q/4kv, i18944, v152064)",
+                "setup_s": round(t_load, 1)})
+    return res
 
 
 def pipeline_bench(rank: int, world: int, dev, n_micro: int, n_tokens: int = 256, prompt_len: int = 32,

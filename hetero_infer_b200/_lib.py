@@ -44,6 +44,10 @@ SIGNATURES = {
     "hq4_argmax_pair": (_I, [_P, _I, _I, _P, _P]),
     "hq4_pick_token": (_I, [_P, _I, _P, _P, _I, _P]),
     "hq4_advance_position": (_I, [_P, _I, _P]),
+    "hq4_decode_plan_create": (_I, [_P] + [_I] * 7 + [_F, _F, _P, _P, _I] + [_P] * 6),
+    "hq4_decode_plan_run": (_I, [_P, _P]),
+    "hq4_decode_plan_info": (_I, [_P, _P]),
+    "hq4_decode_plan_destroy": (None, [_P]),
 }
 
 ERRORS = {

@@ -1,0 +1,387 @@
+// Device-side pieces of the one-token GEMV shared by the streaming kernel
+// (hq4_gemv.cu) and the persistent decode kernel (hq4_decode.cu): the launch
+// parameters, the epilogues, and the streaming kernel's consumer steps (x
+// image build, stage loop, strip totals).  Both kernels therefore compute
+// every output with the same instructions in the same order.
+#pragma once
+#include "hq4_common.cuh"
+
+namespace hq4 {
+
+template <int KG>
+struct M1 {
+    static constexpr int kWords = KG / 8;        // packed words per group-row
+    static constexpr int kKSteps = KG / 8;       // one word per row per k32 step
+    static constexpr int kDigitBytes = KG;       // one s8 digit per value
+    static constexpr int kBRegs = KG / 4;        // B registers per (group, digit)
+    static constexpr int kImgStride = 3 * KG + 16;  // bytes per group: d2|d1|d0|(2^(E-22), xsum)|pad
+    static constexpr int kMetaOff = 3 * KG;
+};
+
+struct GemvM1Params {
+    const uint32_t* w;
+    const uint16_t* sc;
+    const uint16_t* bi;
+    const float* x;
+    float* out;
+    int n_out, n_in;
+    int ng;        // lane-groups per row (n_in / KG)
+    int sg_shift;  // scale index = lane-group >> sg_shift
+    int n_sg;      // scale groups per row (n_in / gs)
+    int n_strips, nq;
+    const float* row_add;   // optional: out[r] += row_add[r]
+    const float* residual;  // optional: out[r] += residual[r]
+    int* status;            // device status word; bit 0 set when a bounded wait ran out
+    // optional RMSNorm of x before the product: x <- x * rsqrt(mean(x^2)+eps) * norm_w
+    const float* norm_w;
+    float eps;
+    // epilogue mode
+    int mode;               // kEpiPlain, kEpiSiluMul or kEpiQkvRope
+    int x_bf16;             // streaming kernel only: x is bf16 (no RMSNorm then)
+    // kEpiQkvRope: q|k|v rows of one decoder layer, q and k rows permuted so
+    // strip rows g and g+8 are the rotation pair (d, d + head_dim/2)
+    int q_strips, k_strips, head_dim, max_ctx;
+    int tok;                // token index inside this call (position = *pos + tok)
+    const int* pos;         // device position of token 0
+    const float* rope_cos;  // [max_ctx][head_dim/2]
+    const float* rope_sin;
+    float* q_out;           // [n_heads][head_dim], rotated
+    float* k_cache;         // [n_kv][max_ctx][head_dim]
+    float* v_cache;
+};
+
+enum : int { kEpiPlain = 0, kEpiSiluMul = 1, kEpiQkvRope = 2 };
+
+__device__ __forceinline__ void store_row(const GemvM1Params& p, int r, float y) {
+    if (r >= p.n_out) return;
+    if (p.row_add) y += p.row_add[r];
+    if (p.residual) y += p.residual[r];
+    p.out[r] = y;
+}
+
+// silu as the reference's NumPy stage writes it: x / (1 + exp(-x))
+// (hetero/cpu_model.py:169-170), every operation rounded separately.
+__device__ __forceinline__ float silu_ref(float x) {
+    return __fdiv_rn(x, __fadd_rn(1.0f, expf(-x)));
+}
+
+// Store the finished pair of rows (g, g+8) of strip s according to the mode.
+__device__ __forceinline__ void store_pair(const GemvM1Params& p, int s, int g, float y0, float y1) {
+    if (p.mode == kEpiPlain) {
+        store_row(p, s * 16 + g, y0);
+        store_row(p, s * 16 + g + 8, y1);
+        return;
+    }
+    if (p.mode == kEpiSiluMul) {
+        // strip s holds gate rows 8s..8s+7 (g) and the matching up rows (g+8)
+        const int r = s * 8 + g;
+        if (r < p.n_out / 2) p.out[r] = __fmul_rn(silu_ref(y0), y1);
+        return;
+    }
+    // kEpiQkvRope
+    if (p.row_add) {
+        y0 = __fadd_rn(y0, p.row_add[s * 16 + g]);
+        y1 = __fadd_rn(y1, p.row_add[s * 16 + g + 8]);
+    }
+    const int half = p.head_dim >> 1;
+    const int spp = half >> 3;  // strips per head (8 rotation pairs per strip)
+    const int pos = *p.pos + p.tok;
+    if (pos < 0 || pos >= p.max_ctx) return;  // outside the cache: write nothing
+    if (s < p.q_strips + p.k_strips) {
+        const bool is_q = s < p.q_strips;
+        const int sl = is_q ? s : s - p.q_strips;
+        const int head = sl / spp, j = (sl % spp) * 8 + g;
+        const float c = p.rope_cos[(size_t)pos * half + j], sn = p.rope_sin[(size_t)pos * half + j];
+        // hetero/cpu_model.py:200-203: (x1*cos - x2*sin, x1*sin + x2*cos)
+        const float o1 = __fsub_rn(__fmul_rn(y0, c), __fmul_rn(y1, sn));
+        const float o2 = __fadd_rn(__fmul_rn(y0, sn), __fmul_rn(y1, c));
+        float* dst = is_q ? p.q_out + (size_t)head * p.head_dim
+                          : p.k_cache + ((size_t)head * p.max_ctx + pos) * p.head_dim;
+        dst[j] = o1;
+        dst[j + half] = o2;
+    } else {
+        const int r0 = (s - p.q_strips - p.k_strips) * 16 + g;  // natural v row order
+        const int r1 = r0 + 8;
+        const int head0 = r0 / p.head_dim, head1 = r1 / p.head_dim;
+        p.v_cache[((size_t)head0 * p.max_ctx + pos) * p.head_dim + (r0 % p.head_dim)] = y0;
+        p.v_cache[((size_t)head1 * p.max_ctx + pos) * p.head_dim + (r1 % p.head_dim)] = y1;
+    }
+}
+
+
+constexpr int kStrConsumers = 16;
+constexpr int kStrThreads = (kStrConsumers + 1) * kWarp;  // + one producer warp
+constexpr int kStrKc = kStrConsumers;                      // k-chunks per stage (one per consumer warp)
+constexpr int kStrTileBytes = 16 * 128;                    // 16 rows x 32 packed words
+constexpr int kStrWBytes = kStrKc * kStrTileBytes;         // 32 KB
+constexpr int kStrSBCols = kStrKc * 4;                     // scale groups per stage at gs 64
+constexpr int kStrSBBytes = 16 * kStrSBCols * 2;           // 16 rows x up to 64 scale groups
+constexpr int kStrStageBytes = kStrWBytes + 2 * kStrSBBytes;  // 36 KB (a multiple of 1024)
+constexpr int kStrNormThreads = 256;                       // sum of squares as the kernel above
+constexpr int kStrImgBytes = 4 * M1<64>::kImgStride;       // one k-chunk: 4 lane-groups
+constexpr uint64_t kStrWaitNs = 1000000000ull;             // bounded waits: 1 s
+constexpr uint32_t kStrTryHintNs = 10000;                  // consumer waits: 10 us per try_wait,
+constexpr int kStrTries = 100000;                          // at most 1 s in all
+
+__device__ __forceinline__ uint4 lds128(const unsigned char* p) {
+    return *reinterpret_cast<const uint4*>(p);
+}
+
+// ---- streaming consumer steps (512 consumer threads, warps 0-15) ----------
+
+// RMSNorm factor 1/sqrt(mean(x^2)+eps): thread i < 256 sums x[i], x[i+256],
+// ...; then the warp's xor tree; then the 8 warp sums in order.  Uses named
+// barrier 1 over the 512 consumer threads.
+__device__ __forceinline__ float str_norm_factor(const GemvM1Params& p, float* red, int warp, int lane) {
+    float ss = 0.0f;
+    if (threadIdx.x < kStrNormThreads)
+        for (int i = threadIdx.x; i < p.n_in; i += kStrNormThreads) ss = fmaf(p.x[i], p.x[i], ss);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if (lane == 0 && threadIdx.x < kStrNormThreads) red[warp] = ss;
+    asm volatile("bar.sync 1, 512;" ::: "memory");
+    float tot = 0.0f;
+#pragma unroll
+    for (int i = 0; i < kStrNormThreads / kWarp; i++) tot += red[i];
+    const float mean = __fdiv_rn(tot, (float)p.n_in);
+    return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, p.eps)));
+}
+
+// This warp's chunk images (k-chunk kb*16 + warp for kb < nkb), built from x
+// (optionally normalised), one x load in flight while the previous chunk is
+// converted.  Image format: per lane-group the digit blocks d2, d1, d0 of 64
+// bytes in k-step order, then (2^(E-22), xsum).
+__device__ __forceinline__ void str_build_images(const GemvM1Params& p, unsigned char* img_w, int nkb, int nk,
+                                                 int warp, int lane, float norm_r) {
+    using C = M1<64>;
+    // lane holds values [8*(lane&7), +8) of lane-group lane>>3
+    const int bq = lane >> 3, bp = lane & 7;
+    float xr0[8], xr1[8];
+    auto load_x = [&](int kc, float (&dst)[8]) {
+        const int G = kc * 4 + bq;
+        if (kc < nk && G < p.ng && p.x_bf16) {  // bf16 widens to fp32 exactly
+            const uint4 r = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(p.x) +
+                                                            (size_t)kc * 256 + lane * 8);
+            const uint32_t w4[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                dst[2 * i] = __uint_as_float(w4[i] << 16);
+                dst[2 * i + 1] = __uint_as_float(w4[i] & 0xFFFF0000u);
+            }
+        } else if (kc < nk && G < p.ng) {
+            const float4* src = reinterpret_cast<const float4*>(p.x + (size_t)kc * 256 + lane * 8);
+            const float4 a = src[0], b = src[1];
+            dst[0] = a.x; dst[1] = a.y; dst[2] = a.z; dst[3] = a.w;
+            dst[4] = b.x; dst[5] = b.y; dst[6] = b.z; dst[7] = b.w;
+        } else {
+#pragma unroll
+            for (int i = 0; i < 8; i++) dst[i] = 0.0f;
+        }
+    };
+    load_x(warp, xr0);
+    for (int kb = 0; kb < nkb; kb++) {
+        const int kc = kb * kStrKc + warp;
+        if (kb + 1 < nkb) load_x(kc + kStrKc, xr1);  // in flight during this build
+        if (kc < nk) {
+            float xv[8];
+#pragma unroll
+            for (int i = 0; i < 8; i++) xv[i] = xr0[i];
+            if (p.norm_w && kc * 4 + bq < p.ng) {
+                const float4* nw = reinterpret_cast<const float4*>(p.norm_w + (size_t)kc * 256 + lane * 8);
+                const float4 c = nw[0], d = nw[1];
+                const float n8[8] = {c.x, c.y, c.z, c.w, d.x, d.y, d.z, d.w};
+#pragma unroll
+                for (int i = 0; i < 8; i++) xv[i] = __fmul_rn(__fmul_rn(xv[i], norm_r), n8[i]);
+            }
+            float amax = 0.0f, s = 0.0f;
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                amax = fmaxf(amax, fabsf(xv[i]));
+                s += xv[i];
+            }
+#pragma unroll
+            for (int o = 1; o < 8; o <<= 1) {
+                amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+                s += __shfl_xor_sync(0xffffffffu, s, o);
+            }
+            const int E = group_exponent(amax);
+            const float up = exp2i(kXBits - E);
+            uint32_t r[8];
+#pragma unroll
+            for (int k = 0; k < 8; k++) r[k] = digits3(xv[k], up);
+            const uint32_t e01 = prmt(prmt(r[0], r[2], 0x5140), prmt(r[4], r[6], 0x5140), 0x5410);
+            const uint32_t e11 = prmt(prmt(r[0], r[2], 0x5140), prmt(r[4], r[6], 0x5140), 0x7632);
+            const uint32_t e21 = prmt(prmt(r[0], r[2], 0x0062), prmt(r[4], r[6], 0x0062), 0x5410);
+            const uint32_t o01 = prmt(prmt(r[1], r[3], 0x5140), prmt(r[5], r[7], 0x5140), 0x5410);
+            const uint32_t o11 = prmt(prmt(r[1], r[3], 0x5140), prmt(r[5], r[7], 0x5140), 0x7632);
+            const uint32_t o21 = prmt(prmt(r[1], r[3], 0x0062), prmt(r[5], r[7], 0x0062), 0x5410);
+            unsigned char* gb = img_w + (size_t)kb * kStrImgBytes + bq * C::kImgStride;
+            *reinterpret_cast<uint2*>(gb + 0 * 64 + bp * 8) = make_uint2(e21, o21);
+            *reinterpret_cast<uint2*>(gb + 1 * 64 + bp * 8) = make_uint2(e11, o11);
+            *reinterpret_cast<uint2*>(gb + 2 * 64 + bp * 8) = make_uint2(e01, o01);
+            if (bp == 0) *reinterpret_cast<float2*>(gb + C::kMetaOff) = make_float2(exp2i(E - kXBits), s);
+        }
+#pragma unroll
+        for (int i = 0; i < 8; i++) xr0[i] = xr1[i];
+    }
+    __syncwarp();
+}
+
+// Lane sums of the (at most two) strips a CTA keeps in registers.
+struct StrAcc {
+    float r00, r01, r10, r11;
+};
+
+// The stage loop of one GEMV: ns strips x nkb k-blocks through the ring
+// (stages k-block-major, strip-minor), starting at ring position (slot,
+// phase), which it advances.  `stages` is the ring's first stage, `full` /
+// `empty` the barrier addresses of slot 0 (8 bytes apart).  A wait that
+// runs out clears ok; a slot whose copy never arrived is not handed back.
+__device__ __forceinline__ void str_consume(const GemvM1Params& p, const unsigned char* stages, uint32_t full,
+                                            uint32_t empty, int R, int& slot, uint32_t& phase, bool& ok, int ns,
+                                            int nkb, int nk, const unsigned char* img_w,
+                                            const unsigned char* zero_blk, float* partials, int ns_max, int warp,
+                                            int lane, StrAcc& acc) {
+    using C = M1<64>;
+    const int g = lane >> 2, t = lane & 3;
+    const int role = (g >> 1) == t ? (g & 1) + 1 : 0;  // 1: d2+d0, 2: d1, 0: none
+    const int off0 = role == 1 ? 0 : 64;
+    // CTAs with one or two strips keep each strip's lane sums in registers
+    // across k-blocks; more strips go through the shared-memory slots per stage
+    const bool regacc = ns <= 2;
+    // scale/bias tiles carry the swizzle of their row width (128, 64 or 32 B)
+    const int sb_cols = kStrSBCols >> p.sg_shift;
+    const int sb_row = sb_cols * 2;
+    const int sb_mask = (sb_row >> 4) - 1;  // 16-byte units per row - 1: 128 B: 7, 64 B: 3, 32 B: 1
+    const int lg = (warp * 4 + t) >> p.sg_shift;  // scale group inside the stage
+    auto sb_off = [&](int row) {
+        const int o = row * sb_row + lg * 2;
+        return o ^ (((o >> 7) & sb_mask) << 4);
+    };
+    const int sbo0 = sb_off(g), sbo1 = sb_off(g + 8);
+    for (int kb = 0; kb < nkb; kb++) {
+        const int kc = kb * kStrKc + warp;
+        const bool active = kc < nk;
+        const unsigned char* img = img_w + (size_t)kb * kStrImgBytes;
+        const bool gok = kc * 4 + t < p.ng;
+        const unsigned char* gb = img + t * C::kImgStride;
+        const uint4* src0 = reinterpret_cast<const uint4*>(role ? gb + off0 : zero_blk);
+        const uint4* src1 = reinterpret_cast<const uint4*>(role == 1 ? gb + 128 : zero_blk);
+        const float2 meta = *reinterpret_cast<const float2*>(gb + C::kMetaOff);
+        for (int j = 0; j < ns; j++) {
+            if (ok && !mbar_wait_tries(full + 8u * slot, phase, kStrTryHintNs, kStrTries)) ok = false;
+            if (ok && active) {
+                const unsigned char* st = stages + (size_t)slot * kStrStageBytes;
+                const unsigned char* wt = st + warp * kStrTileBytes;
+                // rows g and g+8; 16-byte chunks 2t and 2t+1 of the row, swizzled
+                const int c0 = ((2 * t) ^ g) << 4, c1 = ((2 * t + 1) ^ g) << 4;
+                const uint4 ra = lds128(wt + g * 128 + c0), rb = lds128(wt + g * 128 + c1);
+                const uint4 rc = lds128(wt + (g + 8) * 128 + c0), rd = lds128(wt + (g + 8) * 128 + c1);
+                const uint32_t w0[8] = {ra.x, ra.y, ra.z, ra.w, rb.x, rb.y, rb.z, rb.w};
+                const uint32_t w1[8] = {rc.x, rc.y, rc.z, rc.w, rd.x, rd.y, rd.z, rd.w};
+                int c0e[4] = {0, 0, 0, 0}, c0o[4] = {0, 0, 0, 0}, c1e[4] = {0, 0, 0, 0}, c1o[4] = {0, 0, 0, 0};
+#pragma unroll
+                for (int ks = 0; ks < C::kKSteps; ks += 2) {
+                    const uint4 q0 = src0[ks >> 1], q1 = src1[ks >> 1];
+                    uint32_t a0, a1, a2, a3;
+                    unpack_u8(w0[ks], a0, a2);
+                    unpack_u8(w1[ks], a1, a3);
+                    mma_u8s8_16832(c0e, a0, a1, a2, a3, q0.x, q0.y);
+                    mma_u8s8_16832(c1e, a0, a1, a2, a3, q1.x, q1.y);
+                    unpack_u8(w0[ks + 1], a0, a2);
+                    unpack_u8(w1[ks + 1], a1, a3);
+                    mma_u8s8_16832(c0o, a0, a1, a2, a3, q0.z, q0.w);
+                    mma_u8s8_16832(c1o, a0, a1, a2, a3, q1.z, q1.w);
+                }
+                const unsigned char* ss = st + kStrWBytes;
+                const unsigned char* sbi = st + kStrWBytes + kStrSBBytes;
+                float a0f = 0.0f, a1f = 0.0f;
+                if (gok) {
+                    const float dot0 = fmaf((float)(c0e[0] + c0o[0]), 65536.0f,
+                                            fmaf((float)(c0e[1] + c0o[1]), 256.0f, (float)(c1e[0] + c1o[0])));
+                    const float dot1 = fmaf((float)(c0e[2] + c0o[2]), 65536.0f,
+                                            fmaf((float)(c0e[3] + c0o[3]), 256.0f, (float)(c1e[2] + c1o[2])));
+                    const float s0 = h2f(*reinterpret_cast<const uint16_t*>(ss + sbo0));
+                    const float b0 = h2f(*reinterpret_cast<const uint16_t*>(sbi + sbo0));
+                    const float s1 = h2f(*reinterpret_cast<const uint16_t*>(ss + sbo1));
+                    const float b1 = h2f(*reinterpret_cast<const uint16_t*>(sbi + sbo1));
+                    a0f = fmaf(s0 * meta.x, dot0, 0.0f);
+                    a0f = fmaf(b0, meta.y, a0f);
+                    a1f = fmaf(s1 * meta.x, dot1, 0.0f);
+                    a1f = fmaf(b1, meta.y, a1f);
+                }
+                if (regacc) {
+                    if (j == 0) {
+                        acc.r00 += a0f;
+                        acc.r01 += a1f;
+                    } else {
+                        acc.r10 += a0f;
+                        acc.r11 += a1f;
+                    }
+                } else {
+                    a0f += __shfl_xor_sync(0xffffffffu, a0f, 1);
+                    a0f += __shfl_xor_sync(0xffffffffu, a0f, 2);
+                    a1f += __shfl_xor_sync(0xffffffffu, a1f, 1);
+                    a1f += __shfl_xor_sync(0xffffffffu, a1f, 2);
+                    if (t == 0) {
+                        float* slotp = partials + ((size_t)warp * ns_max + j) * 16;
+                        slotp[g] += a0f;
+                        slotp[g + 8] += a1f;
+                    }
+                }
+            }
+            __syncwarp();
+            // a slot whose copy never arrived is not handed back: the producer
+            // then stops instead of reusing it under a copy still in flight
+            if (ok && lane == 0) mbar_arrive(empty + 8u * slot);
+            if (++slot == R) {
+                slot = 0;
+                phase ^= 1u;
+            }
+        }
+    }
+}
+
+// Strip totals: register sums parked in the warp's slots, then per strip the
+// 16 warps' slots summed in a fixed order (lane t adds warps 4t..4t+3, then a
+// fixed xor tree) and stored through the epilogue.  Deterministic, no
+// atomics.  Named barrier 1 over the 512 consumer threads; nothing is stored
+// when any warp of the CTA saw a wait run out.
+__device__ __forceinline__ void str_finish(const GemvM1Params& p, float* partials, int ns, int ns_max, int s0,
+                                           bool ok, const StrAcc& acc, int warp, int lane) {
+    const int g = lane >> 2, t = lane & 3;
+    if (ns <= 2) {
+#pragma unroll
+        for (int j = 0; j < 2; j++) {
+            float a0f = j == 0 ? acc.r00 : acc.r10, a1f = j == 0 ? acc.r01 : acc.r11;
+            a0f += __shfl_xor_sync(0xffffffffu, a0f, 1);
+            a0f += __shfl_xor_sync(0xffffffffu, a0f, 2);
+            a1f += __shfl_xor_sync(0xffffffffu, a1f, 1);
+            a1f += __shfl_xor_sync(0xffffffffu, a1f, 2);
+            if (j < ns && t == 0) {
+                float* slotp = partials + ((size_t)warp * ns_max + j) * 16;
+                slotp[g] = a0f;
+                slotp[g + 8] = a1f;
+            }
+        }
+    }
+    asm volatile("bar.sync 1, 512;" ::: "memory");
+    if (!__any_sync(0xffffffffu, !ok)) {
+        for (int j = warp; j < ns; j += kStrConsumers) {
+            float y0 = 0.0f, y1 = 0.0f;
+#pragma unroll
+            for (int k = 0; k < kStrConsumers / 4; k++) {
+                const float* sl = partials + ((size_t)(t * (kStrConsumers / 4) + k) * ns_max + j) * 16;
+                y0 += sl[g];
+                y1 += sl[g + 8];
+            }
+            y0 += __shfl_xor_sync(0xffffffffu, y0, 1);
+            y0 += __shfl_xor_sync(0xffffffffu, y0, 2);
+            y1 += __shfl_xor_sync(0xffffffffu, y1, 1);
+            y1 += __shfl_xor_sync(0xffffffffu, y1, 2);
+            if (t == 0) store_pair(p, s0 + j, g, y0, y1);
+        }
+    }
+}
+
+}  // namespace hq4

@@ -12,6 +12,7 @@
 #include <algorithm>
 #include <cfloat>
 
+#include "hq4_attn.cuh"
 #include "hq4_common.cuh"
 #include "hq4.h"
 
@@ -73,10 +74,8 @@ __global__ void embed_kernel(const __half* __restrict__ table, const int* __rest
 // is its own thread: a 4-chain fp32 dot over float4 rows of the K cache, with
 // q broadcast from shared memory.  The value pass gives each thread a float4
 // column of V and one of 8 key residues; the 8 partial sums are added in a
-// fixed order (deterministic).
-constexpr int kAttnThreads = 256;
-constexpr int kAttnParts = 8;  // key residues in the value pass
-
+// fixed order (deterministic).  attention_row (hq4_attn.cuh) is the same
+// arithmetic for the persistent decode kernel.
 __global__ void __launch_bounds__(kAttnThreads) attention_kernel(
     const float* __restrict__ q, const float* __restrict__ k_cache, const float* __restrict__ v_cache,
     float* __restrict__ out, int n_heads, int n_kv, int head_dim, int max_ctx, const int* __restrict__ pos,

@@ -65,4 +65,11 @@ static inline bool make_map_chunks(CUtensorMap* tm, const void* ptr, long long r
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// Swizzle of a scale/bias tile whose rows are sg_cols fp16 values (128, 64 or
+// 32 bytes): the 16 rows' reads of one column then fall in different banks.
+static inline CUtensorMapSwizzle sb_swizzle(int sg_cols) {
+    return sg_cols * 2 >= 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                              : sg_cols * 2 == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B;
+}
+
 }  // namespace hq4

@@ -12,6 +12,7 @@ stage uses.
 """
 from __future__ import annotations
 
+import ctypes
 from typing import Optional
 
 import numpy as np
@@ -524,6 +525,79 @@ def get(name: str = "auto"):
     raise ValueError(f"unknown backend {name}")
 
 
+class _DecodeLayer(ctypes.Structure):
+    """include/hq4.h hq4_decode_layer: one layer's device pointers."""
+    _fields_ = [(n, ctypes.c_void_p) for n in (
+        "qkv_w", "qkv_s", "qkv_b", "qkv_bias", "input_norm", "o_w", "o_s", "o_b", "post_norm",
+        "gate_up_w", "gate_up_s", "gate_up_b", "down_w", "down_s", "down_b", "k_cache", "v_cache")]
+
+
+class DecodePlan:
+    """Every layer of a stage for one decode token as ONE persistent launch
+    (hq4_decode_plan_*): the same five steps per layer as
+    ``Stage.layer_forward`` with the same bits, without the kernel boundaries.
+    Bound to the hidden row h [1, H], the KV cache and the step buffers;
+    ``run`` is capturable in a CUDA graph.
+
+    ``DecodePlan.build`` returns None when a shape does not fit the kernel
+    (-1 from the library); any other failure raises."""
+
+    def __init__(self, handle, stage, keep):
+        self.handle, self.stage, self._keep = handle, stage, keep
+
+    @classmethod
+    def build(cls, stage: "Stage", h: torch.Tensor, cache: "DeviceKVCache", bufs: dict):
+        from ._lib import expect
+        lib = stage.lib
+        n = len(stage.layers)
+        if n == 0:
+            return None
+        arr = (_DecodeLayer * n)()
+        for i, lay in enumerate(stage.layers):
+            e = arr[i]
+            e.qkv_w, e.qkv_s, e.qkv_b = lay.qkv.w.data_ptr(), lay.qkv.s.data_ptr(), lay.qkv.b.data_ptr()
+            e.qkv_bias, e.input_norm = lay.qkv_bias.data_ptr(), lay.in_w.data_ptr()
+            e.o_w, e.o_s, e.o_b = lay.o.w.data_ptr(), lay.o.s.data_ptr(), lay.o.b.data_ptr()
+            e.post_norm = lay.post_w.data_ptr()
+            e.gate_up_w, e.gate_up_s, e.gate_up_b = (lay.gate_up.w.data_ptr(), lay.gate_up.s.data_ptr(),
+                                                     lay.gate_up.b.data_ptr())
+            e.down_w, e.down_s, e.down_b = lay.down.w.data_ptr(), lay.down.s.data_ptr(), lay.down.b.data_ptr()
+            e.k_cache, e.v_cache = cache.k[i].data_ptr(), cache.v[i].data_ptr()
+        expect(h, stage.H * 4, "h", 16)
+        if cache.max_ctx > stage.max_ctx:
+            raise RuntimeError("cache larger than the stage's rope table")
+        handle = ctypes.c_void_p()
+        rc = lib.hq4_decode_plan_create(arr, n, stage.H, stage.nh, stage.nkv, stage.hd, stage.I, stage.gs,
+                                        stage.eps, stage.scale, stage.rope_cos.data_ptr(),
+                                        stage.rope_sin.data_ptr(), cache.max_ctx, h.data_ptr(),
+                                        cache.pos.data_ptr(), bufs["q"].data_ptr(), bufs["a"].data_ptr(),
+                                        bufs["m"].data_ptr(), ctypes.byref(handle))
+        if rc == -1:
+            return None
+        _lib.check(rc, "hq4_decode_plan_create")
+        return cls(handle, stage, (h, cache, bufs))
+
+    def run(self) -> None:
+        self.stage._check(self.stage.lib.hq4_decode_plan_run(self.handle, self.stage._stream()),
+                          "hq4_decode_plan_run")
+
+    def info(self) -> dict:
+        out = (ctypes.c_int * 4)()
+        _lib.check(self.stage.lib.hq4_decode_plan_info(self.handle, out), "hq4_decode_plan_info")
+        return {"grid": out[0], "ring": out[1], "smem": out[2], "phases": out[3]}
+
+    def close(self) -> None:
+        if self.handle:
+            self.stage.lib.hq4_decode_plan_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
 class GreedyDecoder:
     """Batch-1 greedy generation on one device stage that owns the embedding
     and the head (the single-node decode loop of hetero/coordinator.py:266-292).
@@ -532,9 +606,13 @@ class GreedyDecoder:
     decode step -- embedding of the previous token, every layer, the head,
     argmax, position advance -- and is replayed once per token.  The token, the
     position and the history of generated tokens stay on the device, so there
-    is no host round trip between steps; `generate` reads the history once."""
+    is no host round trip between steps; `generate` reads the history once.
 
-    def __init__(self, stage: Stage, cache: Optional[DeviceKVCache] = None):
+    persistent: the layers of a decode step run as one persistent launch
+    (DecodePlan) -- True requires it, False keeps one launch per layer step,
+    "auto" takes the plan when the shapes fit it."""
+
+    def __init__(self, stage: Stage, cache: Optional[DeviceKVCache] = None, persistent="auto"):
         if not (stage.spec.embed and stage.spec.head):
             raise ValueError("GreedyDecoder needs a stage with both embedding and head")
         self.stage = stage
@@ -549,6 +627,11 @@ class GreedyDecoder:
                      "m": torch.empty((1, stage.I), dtype=torch.float32, device=dev)}
         self.graph = None
         self.stream = torch.cuda.Stream(dev)
+        self.plan = None
+        if persistent:
+            self.plan = DecodePlan.build(stage, self.h, self.cache, self.bufs)
+            if self.plan is None and persistent is True:
+                raise ValueError("the stage's shapes do not fit the persistent decode kernel")
 
     def _argmax(self):
         s = self.stage
@@ -559,8 +642,11 @@ class GreedyDecoder:
         s = self.stage
         s._check(s.lib.hq4_embed_f16(s.embed_table.data_ptr(), self.tok.data_ptr(), 1, s.H, s.embed_table.shape[0],
                                      self.h.data_ptr(), s._stream()), "hq4_embed_f16")
-        for i in range(len(s.layers)):
-            s.layer_forward(i, self.h, self.cache, 1, self.bufs)
+        if self.plan is not None:
+            self.plan.run()
+        else:
+            for i in range(len(s.layers)):
+                s.layer_forward(i, self.h, self.cache, 1, self.bufs)
         s._check(s.lib.hq4_advance_position(self.cache.pos.data_ptr(), 1, s._stream()), "advance")
         s.head_logits(self.h, self.logits)
         self._argmax()

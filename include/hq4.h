@@ -227,6 +227,60 @@ int hq4_pick_token(const int* pairs, int world, int* tok, int* history, int slot
 /* *pos += delta on the device (advances the decode position inside a graph). */
 int hq4_advance_position(int* pos, int delta, void* stream);
 
+/* ---- persistent decode ----------------------------------------------------
+ * One token through n_layers qwen2 decoder layers (hetero/cpu_model.py:280-310
+ * per layer) as ONE cooperative launch: per layer the q|k|v GEMV (RMSNorm,
+ * bias, RoPE, cache append at *pos), attention over the cache, o GEMV +
+ * residual, gate|up GEMV (RMSNorm, silu*up) and down GEMV + residual, in place
+ * on h.  Same results, bit for bit, as hq4_qkv_rope, hq4_attention,
+ * hq4_gemv_fused and hq4_gemv_norm called per layer.  No reference counterpart
+ * (the reference runs a layer as NumPy calls around q4_gemv); it replaces the
+ * per-layer launches of a decode step.
+ *
+ * Weights in the device layout of those entry points: q|k|v rows
+ * concatenated, q and k rows permuted for the RoPE pairs; gate and up rows
+ * interleaved in blocks of 8.  All buffers are device memory, 16-byte aligned
+ * (weights 32-byte); caches [n_kv][max_ctx][head_dim] fp32. */
+typedef struct hq4_decode_layer {
+    const uint32_t* qkv_w;
+    const uint16_t* qkv_s;
+    const uint16_t* qkv_b;
+    const float* qkv_bias;   /* [(n_heads + 2 n_kv) head_dim], may be NULL */
+    const float* input_norm; /* [hidden] */
+    const uint32_t* o_w;
+    const uint16_t* o_s;
+    const uint16_t* o_b;
+    const float* post_norm;  /* [hidden] */
+    const uint32_t* gate_up_w;
+    const uint16_t* gate_up_s;
+    const uint16_t* gate_up_b;
+    const uint32_t* down_w;
+    const uint16_t* down_s;
+    const uint16_t* down_b;
+    float* k_cache;
+    float* v_cache;
+} hq4_decode_layer;
+
+/* Build a plan: the phase program and tensor maps in device memory, bound to
+ * these buffers (h [hidden], q_buf [n_heads head_dim], attn_buf
+ * [n_heads head_dim], mlp_buf [intermediate] fp32; pos the device position).
+ * `layers` is a host array.  Shapes: group size 64, 128 or 256, every
+ * projection's n_in a multiple of 256 with n_in / gs a multiple of 8,
+ * head_dim a multiple of 32 up to 256; max_ctx must leave the scores in one
+ * CTA's shared memory.  -1 when a shape does not fit. */
+int hq4_decode_plan_create(const hq4_decode_layer* layers, int n_layers, int hidden, int n_heads, int n_kv,
+                           int head_dim, int intermediate, int gs, float eps, float attn_scale,
+                           const float* rope_cos, const float* rope_sin, int max_ctx, float* h,
+                           const int* pos, float* q_buf, float* attn_buf, float* mlp_buf, void** plan);
+
+/* One decode step of the plan on `stream` (capturable in a CUDA graph). */
+int hq4_decode_plan_run(void* plan, void* stream);
+
+/* info[0..3] = grid, ring stages, dynamic shared memory bytes, phases. */
+int hq4_decode_plan_info(void* plan, int* info);
+
+void hq4_decode_plan_destroy(void* plan);
+
 #ifdef __cplusplus
 }
 #endif
