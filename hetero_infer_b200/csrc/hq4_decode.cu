@@ -269,7 +269,6 @@ decode_kernel(const DecPhase* __restrict__ phases, const CUtensorMap* __restrict
         bool ok = true;
         int slot = 0;
         uint32_t phase = 0;
-        unsigned long long target = 0;
         for (int ph = 0; ph < n_phases; ph++) {
             const int b = ph & 1;
             if (ph > 0) {
@@ -279,8 +278,10 @@ decode_kernel(const DecPhase* __restrict__ phases, const CUtensorMap* __restrict
                     bool good = ok;
                     mbar_arrive(dempty_bar(b ^ 1));  // phase ph - 1's descriptor is no longer read
                     if (good) {
-                        target += G;
-                        __threadfence();
+                        // the CTA's writes (ordered before this thread by the
+                        // named barrier) are published by the release; the
+                        // acquire below orders the next phase's reads
+                        const unsigned long long target = (unsigned long long)ph * G;  // ph barriers
                         red_release_add_u64(&sy->arrive, 1ull);
                         uint64_t t0 = 0;
                         for (uint32_t n = 1;; n++) {
@@ -299,7 +300,6 @@ decode_kernel(const DecPhase* __restrict__ phases, const CUtensorMap* __restrict
                                 }
                             }
                         }
-                        __threadfence();
                     }
                     if (!good) {
                         atomicExch(&sy->abort, 1u);
@@ -340,10 +340,11 @@ decode_kernel(const DecPhase* __restrict__ phases, const CUtensorMap* __restrict
             const int nk = (p.ng + 3) >> 2, nkb = d.nkb;
             unsigned char* img_w = uni + (size_t)warp * nkb * kStrImgBytes;
             float* partials = reinterpret_cast<float*>(uni + (size_t)kStrConsumers * nkb * kStrImgBytes);
+            const int epi_pos = str_epi_prefetch(p, ns, s0, warp, lane);
             for (int i = threadIdx.x; i < kStrConsumers * ns_max * 16; i += kStrConsumers * kWarp) partials[i] = 0.0f;
+            str_prologue(p, red, img_w, nkb, nk, warp, lane);
+            str_epi_prefetch_late(p, ns, s0, warp, lane, epi_pos);
             asm volatile("bar.sync 1, 512;" ::: "memory");  // slots cleared before any warp adds into them
-            const float norm_r = p.norm_w ? str_norm_factor(p, red, warp, lane) : 1.0f;
-            str_build_images(p, img_w, nkb, nk, warp, lane, norm_r);
             StrAcc acc = {0.0f, 0.0f, 0.0f, 0.0f};
             str_consume(p, base, full_bar(0), empty_bar(0), R, slot, phase, ok, ns, nkb, nk, img_w, zero_blk,
                         partials, ns_max, warp, lane, acc);

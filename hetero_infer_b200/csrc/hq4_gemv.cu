@@ -499,11 +499,12 @@ gemv_stream_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_consta
 
     // ---- consumers (warps 0-15; threadIdx.x in [0, 512))
     pdl_wait();  // x, norm_w, residual and the outputs follow the previous kernel
-    const float norm_r = p.norm_w ? str_norm_factor(p, red, warp, lane) : 1.0f;
+    const int epi_pos = str_epi_prefetch(p, ns, s0, warp, lane);
     // this warp's chunk images, one per k-block, built up front: the builds
     // overlap the ring filling, and the stage loop is tiles only
     unsigned char* img_w = base + L.img_off() + (size_t)warp * L.nkb * kStrImgBytes;
-    str_build_images(p, img_w, nkb, nk, warp, lane, norm_r);
+    str_prologue(p, red, img_w, nkb, nk, warp, lane);
+    str_epi_prefetch_late(p, ns, s0, warp, lane, epi_pos);
     bool ok = true;
     int slot = 0;
     uint32_t phase = 0;

@@ -52,10 +52,51 @@ struct GemvM1Params {
 
 enum : int { kEpiPlain = 0, kEpiSiluMul = 1, kEpiQkvRope = 2 };
 
-__device__ __forceinline__ void store_row(const GemvM1Params& p, int r, float y) {
+// Inputs of a strip's store that do not depend on the product: the row add
+// and residual of rows g and g+8, and for q|k|v the position and the RoPE
+// rotation.  Loaded ahead (before the stage loop) so their latency hides
+// behind the weight stream; applied by store_pair_in.
+struct EpiIn {
+    float a0, a1;  // row_add[r0], row_add[r1] (kEpiPlain, kEpiQkvRope)
+    float r0, r1;  // residual[r0], residual[r1] (kEpiPlain)
+    float c, sn;   // cos, sin of the rotation pair (kEpiQkvRope, q and k strips)
+    int pos;       // *pos + tok (kEpiQkvRope)
+};
+
+__device__ __forceinline__ EpiIn epi_load(const GemvM1Params& p, int s, int g) {
+    EpiIn e = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0};
+    if (p.mode == kEpiPlain) {
+        const int r0 = s * 16 + g, r1 = r0 + 8;
+        if (p.row_add) {
+            if (r0 < p.n_out) e.a0 = p.row_add[r0];
+            if (r1 < p.n_out) e.a1 = p.row_add[r1];
+        }
+        if (p.residual) {
+            if (r0 < p.n_out) e.r0 = p.residual[r0];
+            if (r1 < p.n_out) e.r1 = p.residual[r1];
+        }
+    } else if (p.mode == kEpiQkvRope) {
+        if (p.row_add) {
+            e.a0 = p.row_add[s * 16 + g];
+            e.a1 = p.row_add[s * 16 + g + 8];
+        }
+        e.pos = *p.pos + p.tok;
+        if (e.pos >= 0 && e.pos < p.max_ctx && s < p.q_strips + p.k_strips) {
+            const int half = p.head_dim >> 1;
+            const int spp = half >> 3;  // strips per head (8 rotation pairs per strip)
+            const int sl = s < p.q_strips ? s : s - p.q_strips;
+            const int j = (sl % spp) * 8 + g;
+            e.c = p.rope_cos[(size_t)e.pos * half + j];
+            e.sn = p.rope_sin[(size_t)e.pos * half + j];
+        }
+    }
+    return e;
+}
+
+__device__ __forceinline__ void store_row_in(const GemvM1Params& p, int r, float y, float add, float res) {
     if (r >= p.n_out) return;
-    if (p.row_add) y += p.row_add[r];
-    if (p.residual) y += p.residual[r];
+    if (p.row_add) y += add;
+    if (p.residual) y += res;
     p.out[r] = y;
 }
 
@@ -65,11 +106,13 @@ __device__ __forceinline__ float silu_ref(float x) {
     return __fdiv_rn(x, __fadd_rn(1.0f, expf(-x)));
 }
 
-// Store the finished pair of rows (g, g+8) of strip s according to the mode.
-__device__ __forceinline__ void store_pair(const GemvM1Params& p, int s, int g, float y0, float y1) {
+// Store the finished pair of rows (g, g+8) of strip s according to the mode,
+// with the inputs e = epi_load(p, s, g).
+__device__ __forceinline__ void store_pair_in(const GemvM1Params& p, int s, int g, float y0, float y1,
+                                              const EpiIn& e) {
     if (p.mode == kEpiPlain) {
-        store_row(p, s * 16 + g, y0);
-        store_row(p, s * 16 + g + 8, y1);
+        store_row_in(p, s * 16 + g, y0, e.a0, e.r0);
+        store_row_in(p, s * 16 + g + 8, y1, e.a1, e.r1);
         return;
     }
     if (p.mode == kEpiSiluMul) {
@@ -80,18 +123,18 @@ __device__ __forceinline__ void store_pair(const GemvM1Params& p, int s, int g, 
     }
     // kEpiQkvRope
     if (p.row_add) {
-        y0 = __fadd_rn(y0, p.row_add[s * 16 + g]);
-        y1 = __fadd_rn(y1, p.row_add[s * 16 + g + 8]);
+        y0 = __fadd_rn(y0, e.a0);
+        y1 = __fadd_rn(y1, e.a1);
     }
     const int half = p.head_dim >> 1;
     const int spp = half >> 3;  // strips per head (8 rotation pairs per strip)
-    const int pos = *p.pos + p.tok;
+    const int pos = e.pos;
     if (pos < 0 || pos >= p.max_ctx) return;  // outside the cache: write nothing
     if (s < p.q_strips + p.k_strips) {
         const bool is_q = s < p.q_strips;
         const int sl = is_q ? s : s - p.q_strips;
         const int head = sl / spp, j = (sl % spp) * 8 + g;
-        const float c = p.rope_cos[(size_t)pos * half + j], sn = p.rope_sin[(size_t)pos * half + j];
+        const float c = e.c, sn = e.sn;
         // hetero/cpu_model.py:200-203: (x1*cos - x2*sin, x1*sin + x2*cos)
         const float o1 = __fsub_rn(__fmul_rn(y0, c), __fmul_rn(y1, sn));
         const float o2 = __fadd_rn(__fmul_rn(y0, sn), __fmul_rn(y1, c));
@@ -106,6 +149,10 @@ __device__ __forceinline__ void store_pair(const GemvM1Params& p, int s, int g, 
         p.v_cache[((size_t)head0 * p.max_ctx + pos) * p.head_dim + (r0 % p.head_dim)] = y0;
         p.v_cache[((size_t)head1 * p.max_ctx + pos) * p.head_dim + (r1 % p.head_dim)] = y1;
     }
+}
+
+__device__ __forceinline__ void store_pair(const GemvM1Params& p, int s, int g, float y0, float y1) {
+    store_pair_in(p, s, g, y0, y1, epi_load(p, s, g));
 }
 
 
@@ -132,10 +179,23 @@ __device__ __forceinline__ uint4 lds128(const unsigned char* p) {
 // RMSNorm factor 1/sqrt(mean(x^2)+eps): thread i < 256 sums x[i], x[i+256],
 // ...; then the warp's xor tree; then the 8 warp sums in order.  Uses named
 // barrier 1 over the 512 consumer threads.
+constexpr int kNormBatch = 4;
 __device__ __forceinline__ float str_norm_factor(const GemvM1Params& p, float* red, int warp, int lane) {
     float ss = 0.0f;
-    if (threadIdx.x < kStrNormThreads)
-        for (int i = threadIdx.x; i < p.n_in; i += kStrNormThreads) ss = fmaf(p.x[i], p.x[i], ss);
+    if (threadIdx.x < kStrNormThreads) {
+        // kNormBatch loads in flight per batch, summed in index order
+        for (int i0 = threadIdx.x; i0 < p.n_in; i0 += kStrNormThreads * kNormBatch) {
+            float v[kNormBatch];
+#pragma unroll
+            for (int k = 0; k < kNormBatch; k++) {
+                const int i = i0 + k * kStrNormThreads;
+                v[k] = i < p.n_in ? p.x[i] : 0.0f;
+            }
+#pragma unroll
+            for (int k = 0; k < kNormBatch; k++)
+                if (i0 + k * kStrNormThreads < p.n_in) ss = fmaf(v[k], v[k], ss);
+        }
+    }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
     if (lane == 0 && threadIdx.x < kStrNormThreads) red[warp] = ss;
@@ -147,82 +207,121 @@ __device__ __forceinline__ float str_norm_factor(const GemvM1Params& p, float* r
     return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, p.eps)));
 }
 
-// This warp's chunk images (k-chunk kb*16 + warp for kb < nkb), built from x
-// (optionally normalised), one x load in flight while the previous chunk is
-// converted.  Image format: per lane-group the digit blocks d2, d1, d0 of 64
-// bytes in k-step order, then (2^(E-22), xsum).
-__device__ __forceinline__ void str_build_images(const GemvM1Params& p, unsigned char* img_w, int nkb, int nk,
-                                                 int warp, int lane, float norm_r) {
+// Lane (bq = lane/8, bp = lane%8) holds values [8 bp, 8 bp + 8) of lane-group
+// bq of a k-chunk.  x of chunk kc (zeros past the row end).
+__device__ __forceinline__ void str_load_x(const GemvM1Params& p, int kc, int nk, int lane, float (&dst)[8]) {
+    const int G = kc * 4 + (lane >> 3);
+    if (kc < nk && G < p.ng && p.x_bf16) {  // bf16 widens to fp32 exactly
+        const uint4 r = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(p.x) +
+                                                        (size_t)kc * 256 + lane * 8);
+        const uint32_t w4[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            dst[2 * i] = __uint_as_float(w4[i] << 16);
+            dst[2 * i + 1] = __uint_as_float(w4[i] & 0xFFFF0000u);
+        }
+    } else if (kc < nk && G < p.ng) {
+        const float4* src = reinterpret_cast<const float4*>(p.x + (size_t)kc * 256 + lane * 8);
+        const float4 a = src[0], b = src[1];
+        dst[0] = a.x; dst[1] = a.y; dst[2] = a.z; dst[3] = a.w;
+        dst[4] = b.x; dst[5] = b.y; dst[6] = b.z; dst[7] = b.w;
+    } else {
+#pragma unroll
+        for (int i = 0; i < 8; i++) dst[i] = 0.0f;
+    }
+}
+// RMSNorm weights of chunk kc (ones past the row end).
+__device__ __forceinline__ void str_load_nw(const GemvM1Params& p, int kc, int nk, int lane, float (&dst)[8]) {
+    if (kc < nk && kc * 4 + (lane >> 3) < p.ng) {
+        const float4* nw = reinterpret_cast<const float4*>(p.norm_w + (size_t)kc * 256 + lane * 8);
+        const float4 c = nw[0], d = nw[1];
+        dst[0] = c.x; dst[1] = c.y; dst[2] = c.z; dst[3] = c.w;
+        dst[4] = d.x; dst[5] = d.y; dst[6] = d.z; dst[7] = d.w;
+    } else {
+#pragma unroll
+        for (int i = 0; i < 8; i++) dst[i] = 1.0f;
+    }
+}
+
+// Digit image of chunk kc (k-block kb of this warp) from its x values
+// (normalised first when `norm`).  Image format: per lane-group the digit
+// blocks d2, d1, d0 of 64 bytes in k-step order, then (2^(E-22), xsum).
+__device__ __forceinline__ void str_build_chunk(const GemvM1Params& p, unsigned char* img_w, int kb, int kc,
+                                                int lane, const float (&xin)[8], const float (&n8)[8], bool norm,
+                                                float norm_r) {
     using C = M1<64>;
-    // lane holds values [8*(lane&7), +8) of lane-group lane>>3
     const int bq = lane >> 3, bp = lane & 7;
-    float xr0[8], xr1[8];
-    auto load_x = [&](int kc, float (&dst)[8]) {
-        const int G = kc * 4 + bq;
-        if (kc < nk && G < p.ng && p.x_bf16) {  // bf16 widens to fp32 exactly
-            const uint4 r = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(p.x) +
-                                                            (size_t)kc * 256 + lane * 8);
-            const uint32_t w4[4] = {r.x, r.y, r.z, r.w};
+    float xv[8];
 #pragma unroll
-            for (int i = 0; i < 4; i++) {
-                dst[2 * i] = __uint_as_float(w4[i] << 16);
-                dst[2 * i + 1] = __uint_as_float(w4[i] & 0xFFFF0000u);
+    for (int i = 0; i < 8; i++) xv[i] = xin[i];
+    if (norm && kc * 4 + bq < p.ng) {
+#pragma unroll
+        for (int i = 0; i < 8; i++) xv[i] = __fmul_rn(__fmul_rn(xv[i], norm_r), n8[i]);
+    }
+    float amax = 0.0f, s = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        amax = fmaxf(amax, fabsf(xv[i]));
+        s += xv[i];
+    }
+#pragma unroll
+    for (int o = 1; o < 8; o <<= 1) {
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        s += __shfl_xor_sync(0xffffffffu, s, o);
+    }
+    const int E = group_exponent(amax);
+    const float up = exp2i(kXBits - E);
+    uint32_t r[8];
+#pragma unroll
+    for (int k = 0; k < 8; k++) r[k] = digits3(xv[k], up);
+    const uint32_t e01 = prmt(prmt(r[0], r[2], 0x5140), prmt(r[4], r[6], 0x5140), 0x5410);
+    const uint32_t e11 = prmt(prmt(r[0], r[2], 0x5140), prmt(r[4], r[6], 0x5140), 0x7632);
+    const uint32_t e21 = prmt(prmt(r[0], r[2], 0x0062), prmt(r[4], r[6], 0x0062), 0x5410);
+    const uint32_t o01 = prmt(prmt(r[1], r[3], 0x5140), prmt(r[5], r[7], 0x5140), 0x5410);
+    const uint32_t o11 = prmt(prmt(r[1], r[3], 0x5140), prmt(r[5], r[7], 0x5140), 0x7632);
+    const uint32_t o21 = prmt(prmt(r[1], r[3], 0x0062), prmt(r[5], r[7], 0x0062), 0x5410);
+    unsigned char* gb = img_w + (size_t)kb * kStrImgBytes + bq * C::kImgStride;
+    *reinterpret_cast<uint2*>(gb + 0 * 64 + bp * 8) = make_uint2(e21, o21);
+    *reinterpret_cast<uint2*>(gb + 1 * 64 + bp * 8) = make_uint2(e11, o11);
+    *reinterpret_cast<uint2*>(gb + 2 * 64 + bp * 8) = make_uint2(e01, o01);
+    if (bp == 0) *reinterpret_cast<float2*>(gb + C::kMetaOff) = make_float2(exp2i(E - kXBits), s);
+}
+
+// The GEMV prologue of a warp: the RMSNorm factor when p.norm_w is set
+// (named barrier 1 over the 512 consumer threads) and this warp's chunk
+// images (k-chunk kb*16 + warp for kb < nkb).  The global loads are issued
+// ahead of their use so that their latencies overlap: without the norm, the x
+// of up to kB chunks at once; with it, the first chunk's x and norm weights
+// together with the norm factor's loads (rows with one k-block, as every
+// hidden-size row of the 7B shape; longer rows load chunk by chunk).
+__device__ __forceinline__ void str_prologue(const GemvM1Params& p, float* red, unsigned char* img_w, int nkb,
+                                             int nk, int warp, int lane) {
+    if (p.norm_w) {
+        float xr[8], nw[8];
+        str_load_x(p, warp, nk, lane, xr);
+        str_load_nw(p, warp, nk, lane, nw);
+        const float norm_r = str_norm_factor(p, red, warp, lane);
+        for (int kb = 0; kb < nkb; kb++) {
+            const int kc = kb * kStrKc + warp;
+            if (kb > 0) {
+                str_load_x(p, kc, nk, lane, xr);
+                str_load_nw(p, kc, nk, lane, nw);
             }
-        } else if (kc < nk && G < p.ng) {
-            const float4* src = reinterpret_cast<const float4*>(p.x + (size_t)kc * 256 + lane * 8);
-            const float4 a = src[0], b = src[1];
-            dst[0] = a.x; dst[1] = a.y; dst[2] = a.z; dst[3] = a.w;
-            dst[4] = b.x; dst[5] = b.y; dst[6] = b.z; dst[7] = b.w;
-        } else {
-#pragma unroll
-            for (int i = 0; i < 8; i++) dst[i] = 0.0f;
+            if (kc < nk) str_build_chunk(p, img_w, kb, kc, lane, xr, nw, true, norm_r);
         }
-    };
-    load_x(warp, xr0);
-    for (int kb = 0; kb < nkb; kb++) {
-        const int kc = kb * kStrKc + warp;
-        if (kb + 1 < nkb) load_x(kc + kStrKc, xr1);  // in flight during this build
-        if (kc < nk) {
-            float xv[8];
+    } else {
+        constexpr int kB = 3;
+        for (int kb0 = 0; kb0 < nkb; kb0 += kB) {
+            float xr[kB][8];
 #pragma unroll
-            for (int i = 0; i < 8; i++) xv[i] = xr0[i];
-            if (p.norm_w && kc * 4 + bq < p.ng) {
-                const float4* nw = reinterpret_cast<const float4*>(p.norm_w + (size_t)kc * 256 + lane * 8);
-                const float4 c = nw[0], d = nw[1];
-                const float n8[8] = {c.x, c.y, c.z, c.w, d.x, d.y, d.z, d.w};
+            for (int u = 0; u < kB; u++)
+                if (kb0 + u < nkb) str_load_x(p, (kb0 + u) * kStrKc + warp, nk, lane, xr[u]);
 #pragma unroll
-                for (int i = 0; i < 8; i++) xv[i] = __fmul_rn(__fmul_rn(xv[i], norm_r), n8[i]);
+            for (int u = 0; u < kB; u++) {
+                const int kc = (kb0 + u) * kStrKc + warp;
+                if (kb0 + u < nkb && kc < nk) str_build_chunk(p, img_w, kb0 + u, kc, lane, xr[u], xr[u], false, 1.0f);
             }
-            float amax = 0.0f, s = 0.0f;
-#pragma unroll
-            for (int i = 0; i < 8; i++) {
-                amax = fmaxf(amax, fabsf(xv[i]));
-                s += xv[i];
-            }
-#pragma unroll
-            for (int o = 1; o < 8; o <<= 1) {
-                amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-                s += __shfl_xor_sync(0xffffffffu, s, o);
-            }
-            const int E = group_exponent(amax);
-            const float up = exp2i(kXBits - E);
-            uint32_t r[8];
-#pragma unroll
-            for (int k = 0; k < 8; k++) r[k] = digits3(xv[k], up);
-            const uint32_t e01 = prmt(prmt(r[0], r[2], 0x5140), prmt(r[4], r[6], 0x5140), 0x5410);
-            const uint32_t e11 = prmt(prmt(r[0], r[2], 0x5140), prmt(r[4], r[6], 0x5140), 0x7632);
-            const uint32_t e21 = prmt(prmt(r[0], r[2], 0x0062), prmt(r[4], r[6], 0x0062), 0x5410);
-            const uint32_t o01 = prmt(prmt(r[1], r[3], 0x5140), prmt(r[5], r[7], 0x5140), 0x5410);
-            const uint32_t o11 = prmt(prmt(r[1], r[3], 0x5140), prmt(r[5], r[7], 0x5140), 0x7632);
-            const uint32_t o21 = prmt(prmt(r[1], r[3], 0x0062), prmt(r[5], r[7], 0x0062), 0x5410);
-            unsigned char* gb = img_w + (size_t)kb * kStrImgBytes + bq * C::kImgStride;
-            *reinterpret_cast<uint2*>(gb + 0 * 64 + bp * 8) = make_uint2(e21, o21);
-            *reinterpret_cast<uint2*>(gb + 1 * 64 + bp * 8) = make_uint2(e11, o11);
-            *reinterpret_cast<uint2*>(gb + 2 * 64 + bp * 8) = make_uint2(e01, o01);
-            if (bp == 0) *reinterpret_cast<float2*>(gb + C::kMetaOff) = make_float2(exp2i(E - kXBits), s);
         }
-#pragma unroll
-        for (int i = 0; i < 8; i++) xr0[i] = xr1[i];
     }
     __syncwarp();
 }
@@ -340,6 +439,40 @@ __device__ __forceinline__ void str_consume(const GemvM1Params& p, const unsigne
             }
         }
     }
+}
+
+__device__ __forceinline__ void prefetch_l1(const void* ptr) {
+    asm volatile("prefetch.global.L1 [%0];" ::"l"(ptr));
+}
+
+// Bring the inputs of this lane's first store in str_finish (strip s0 + warp,
+// lanes t == 0) into L1 before the stage loop, so the store does not wait on
+// L2 at the end: the row add and residual lines now, the RoPE lines once the
+// position has arrived (str_epi_prefetch_late, after the prologue).  Returns
+// the position for q|k|v (its load is in flight meanwhile).
+__device__ __forceinline__ int str_epi_prefetch(const GemvM1Params& p, int ns, int s0, int warp, int lane) {
+    if (warp >= ns || (lane & 3)) return 0;
+    const int r0 = (s0 + warp) * 16 + (lane >> 2);
+    if (p.row_add) prefetch_l1(p.row_add + r0);
+    if (p.mode == kEpiPlain) {
+        if (p.residual) prefetch_l1(p.residual + r0);
+        if (p.row_add && r0 + 8 < p.n_out) prefetch_l1(p.row_add + r0 + 8);
+        if (p.residual && r0 + 8 < p.n_out) prefetch_l1(p.residual + r0 + 8);
+        return 0;
+    }
+    if (p.mode == kEpiQkvRope) return *p.pos + p.tok;
+    return 0;
+}
+__device__ __forceinline__ void str_epi_prefetch_late(const GemvM1Params& p, int ns, int s0, int warp, int lane,
+                                                      int pos) {
+    if (p.mode != kEpiQkvRope || warp >= ns || (lane & 3)) return;
+    const int s = s0 + warp;
+    if (pos < 0 || pos >= p.max_ctx || s >= p.q_strips + p.k_strips) return;
+    const int half = p.head_dim >> 1, spp = half >> 3;
+    const int sl = s < p.q_strips ? s : s - p.q_strips;
+    const int j = (sl % spp) * 8 + (lane >> 2);
+    prefetch_l1(p.rope_cos + (size_t)pos * half + j);
+    prefetch_l1(p.rope_sin + (size_t)pos * half + j);
 }
 
 // Strip totals: register sums parked in the warp's slots, then per strip the
