@@ -55,6 +55,7 @@
 #include <mutex>
 
 #include "hq4_common.cuh"
+#include "hq4_host.cuh"
 #include "hq4_tmap.cuh"
 #include "hq4.h"
 
@@ -701,15 +702,8 @@ static bool weight_maps(const uint32_t* w, const uint16_t* sc, const uint16_t* b
 
 static int launch_gemm(const WeightMaps& wm, const GemmParams& prm, const GemmPlan& pl, cudaStream_t st) {
     // the shared-memory opt-in is a per-device function attribute
-    static bool attr_done[64] = {false};
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return HQ4_ERR_LAUNCH;
-    if (!attr_done[dev]) {
-        if (cudaFuncSetAttribute(gemm_w4a16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmemMax) !=
-            cudaSuccess)
-            return HQ4_ERR_LAUNCH;
-        attr_done[dev] = true;
-    }
+    static PerDeviceOnce attr_once;
+    if (smem_opt_in(attr_once, gemm_w4a16_kernel, kGemmSmemMax) != cudaSuccess) return HQ4_ERR_LAUNCH;
     // split-K partial tile [t_tile][128] fp32 lives in the (drained) rings;
     // A stages + accumulator fit the 512 TMEM columns
     if ((size_t)pl.t_tile * kGemmRows * 4 > (size_t)pl.wslots * kWSlotBytes + (size_t)pl.stages * pl.t_tile * 128 ||
@@ -1149,15 +1143,8 @@ static bool use_small(int m, bool xf32) { return (xf32 ? 2 * m : m) <= 16; }
 
 template <int NT>
 static int launch_small_nt(const WeightMaps& wm, const SmallParams& prm, const SmallPlan& pl, cudaStream_t st) {
-    static bool attr_done[64] = {false};
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return HQ4_ERR_LAUNCH;
-    if (!attr_done[dev]) {
-        if (cudaFuncSetAttribute(gemm_small_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmemMax) !=
-            cudaSuccess)
-            return HQ4_ERR_LAUNCH;
-        attr_done[dev] = true;
-    }
+    static PerDeviceOnce attr_once;  // one per instantiation, as the attribute is per kernel
+    if (smem_opt_in(attr_once, gemm_small_kernel<NT>, kGemmSmemMax) != cudaSuccess) return HQ4_ERR_LAUNCH;
     const int tcap = NT * (prm.xf32 ? 4 : 8);
     if (pl.smem > (size_t)kGemmSmemMax || (size_t)tcap * kGemmRows * 4 > (size_t)pl.wslots * small_slot_bytes(NT))
         return HQ4_ERR_SHAPE;
@@ -1347,21 +1334,21 @@ static __device__ __align__(256) unsigned char g_hq4_gemm_scratch[HQ4_GEMM_STATI
 // once per device (the first call may load the module, so it must not happen
 // while a stream is being captured); nullptr if the lookup fails.
 static void* static_scratch() {
-    static std::mutex mu;
-    static void* addr[64] = {nullptr};
+    static PerDeviceOnce once;
+    static void* addr[kMaxDevices] = {nullptr};
     int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
-    std::lock_guard<std::mutex> lock(mu);
-    if (!addr[dev]) {
+    const cudaError_t e = once.run([&](int d) {
         void* a = nullptr;
-        const cudaError_t e = cudaGetSymbolAddress(&a, g_hq4_gemm_scratch);
-        if (e != cudaSuccess || !a) {
+        const cudaError_t r = cudaGetSymbolAddress(&a, g_hq4_gemm_scratch);
+        if (r != cudaSuccess || !a) {
             (void)cudaGetLastError();  // the failed lookup does not stick to later launches
-            return nullptr;
+            return r != cudaSuccess ? r : cudaErrorInvalidSymbol;
         }
-        addr[dev] = a;
-    }
-    return addr[dev];
+        addr[d] = a;
+        return cudaSuccess;
+    });
+    if (e != cudaSuccess || cudaGetDevice(&dev) != cudaSuccess) return nullptr;
+    return addr[dev];  // written before the once-flag's release store
 }
 
 extern "C" int hq4_gemm_w4a16_static(const uint32_t* w, const uint16_t* scales, const uint16_t* biases,

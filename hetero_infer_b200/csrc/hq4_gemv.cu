@@ -45,6 +45,7 @@
 
 #include "hq4_common.cuh"
 #include "hq4_gemv_dev.cuh"
+#include "hq4_host.cuh"
 #include "hq4_tmap.cuh"
 #include "hq4.h"
 
@@ -552,25 +553,28 @@ struct GemvPlan {
 __device__ int g_hq4_status = 0;
 
 static int sm_count() {
-    static int cached = -1;
-    int dev = 0;
+    int dev = 0, n = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return 148;
-    int n = 0;
-    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
-        n = 148;
-    cached = n;
-    return cached;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    return n;
 }
 
 // Device address of g_hq4_status, looked up once per device.
 int* status_word() {
-    static int* addr[64] = {nullptr};
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
-    if (!addr[dev]) {
+    static PerDeviceOnce once;
+    static int* addr[kMaxDevices] = {nullptr};
+    const cudaError_t e = once.run([&](int d) {
         int* a = nullptr;
-        if (cudaGetSymbolAddress(reinterpret_cast<void**>(&a), g_hq4_status) == cudaSuccess) addr[dev] = a;
-    }
+        const cudaError_t r = cudaGetSymbolAddress(reinterpret_cast<void**>(&a), g_hq4_status);
+        if (r != cudaSuccess) {
+            (void)cudaGetLastError();
+            return r;
+        }
+        addr[d] = a;
+        return cudaSuccess;
+    });
+    int dev = 0;
+    if (e != cudaSuccess || cudaGetDevice(&dev) != cudaSuccess) return nullptr;
     return addr[dev];
 }
 
@@ -610,25 +614,27 @@ static int plan_gemv(int n_out, int n_in, int gs, GemvPlan& pl) {
     return HQ4_OK;
 }
 
+// HQ4_OK when the current device is an sm_100 part (checked once per device).
 static int check_device() {
-    static int ok = -1;
-    if (ok < 0) {
-        int dev = 0, major = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
-        ok = major == 10 ? 1 : 0;
-    }
-    return ok ? HQ4_OK : HQ4_ERR_DEVICE;
+    static PerDeviceOnce once;
+    static bool is_sm100[kMaxDevices] = {false};
+    const cudaError_t e = once.run([&](int d) {
+        int major = 0;
+        const cudaError_t r = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, d);
+        if (r != cudaSuccess) return r;
+        is_sm100[d] = major == 10;
+        return cudaSuccess;
+    });
+    int dev = 0;
+    if (e != cudaSuccess || cudaGetDevice(&dev) != cudaSuccess) return HQ4_ERR_DEVICE;
+    return is_sm100[dev] ? HQ4_OK : HQ4_ERR_DEVICE;
 }
 
 template <int KG>
 static int launch_m1(const GemvPlan& pl, const GemvM1Params& prm, cudaStream_t st) {
     auto kern = gemv_m1_kernel<KG>;
-    static bool attr_set = false;
-    if (!attr_set) {
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
-        attr_set = true;
-    }
+    static PerDeviceOnce attr_once;
+    if (smem_opt_in(attr_once, kern, 220 * 1024) != cudaSuccess) return HQ4_ERR_LAUNCH;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
@@ -713,15 +719,8 @@ static int launch_stream(const GemvPlan& pl, const GemvM1Params& prm, cudaStream
     if (L.bytes() > kStrSmemTarget) return HQ4_OK;  // rows too long for the chunk images: register kernel
     StreamMaps m;
     if (!stream_maps(prm, pl.n_sg, kStrSBCols >> pl.sg_shift, &m)) return HQ4_OK;
-    static bool attr_done[64] = {false};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev >= 0 && dev < 64 && !attr_done[dev]) {
-        if (cudaFuncSetAttribute(gemv_stream_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024) !=
-            cudaSuccess)
-            return HQ4_ERR_LAUNCH;
-        attr_done[dev] = true;
-    }
+    static PerDeviceOnce attr_once;
+    if (smem_opt_in(attr_once, gemv_stream_kernel, 220 * 1024) != cudaSuccess) return HQ4_ERR_LAUNCH;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;

@@ -13,6 +13,7 @@
 #include <cfloat>
 
 #include "hq4_attn.cuh"
+#include "hq4_host.cuh"
 #include "hq4_common.cuh"
 #include "hq4.h"
 
@@ -405,11 +406,8 @@ extern "C" int hq4_attention(const float* q, const float* k_cache, const float* 
     if (((uintptr_t)q | (uintptr_t)k_cache | (uintptr_t)v_cache | (uintptr_t)out) & 15) return HQ4_ERR_ALIGN;
     const size_t smem = (size_t)max_ctx * sizeof(float);
     if (smem > 200 * 1024) return HQ4_ERR_SHAPE;
-    static bool attr = false;
-    if (!attr) {
-        cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-        attr = true;
-    }
+    static PerDeviceOnce attr_once;
+    if (smem_opt_in(attr_once, attention_kernel, 200 * 1024) != cudaSuccess) return HQ4_ERR_LAUNCH;
     return launch_pdl(attention_kernel, dim3(n_heads, n_tokens), dim3(kAttnThreads), smem,
                       static_cast<cudaStream_t>(stream), q, k_cache, v_cache, out, n_heads, n_kv,
                       head_dim, max_ctx, pos, scale);

@@ -457,7 +457,14 @@ class CudaBackend:
         self.max_ctx = max_ctx
 
     def load_stage(self, model_dir, spec, index=None):
-        raise NotImplementedError("checkpoint loading is not built yet; use build_stage(cfg, spec, weights)")
+        """The stage owning `spec` from an MLX-format snapshot, and the bytes
+        it holds (hetero/backends.py:83-85 -> cpu_model.load_stage,
+        hetero/cpu_model.py:371-375): `index` is a checkpoint.WeightIndex of
+        model_dir, built here when not given."""
+        from . import checkpoint
+        idx = index if index is not None else checkpoint.WeightIndex(model_dir)
+        stage = Stage(idx.config, spec, idx.load_shard(spec), self.device, self.max_ctx)
+        return stage, idx.shard_bytes(spec)
 
     def build_stage(self, cfg, spec, weights):
         return Stage(cfg, spec, weights, self.device, self.max_ctx)
@@ -609,14 +616,17 @@ class GreedyDecoder:
     is no host round trip between steps; `generate` reads the history once.
 
     persistent: the layers of a decode step run as one persistent launch
-    (DecodePlan) -- True requires it, False keeps one launch per layer step,
-    "auto" takes the plan when the shapes fit it."""
+    (DecodePlan) -- True requires it, "auto" takes the plan when the shapes
+    fit it, False (the default, the faster path on B200 as measured) keeps one
+    launch per layer step."""
 
-    def __init__(self, stage: Stage, cache: Optional[DeviceKVCache] = None, persistent="auto"):
+    def __init__(self, stage: Stage, cache: Optional[DeviceKVCache] = None, persistent=False):
         if not (stage.spec.embed and stage.spec.head):
             raise ValueError("GreedyDecoder needs a stage with both embedding and head")
         self.stage = stage
-        self.cache = cache or stage.new_caches()
+        self.cache = cache if cache is not None else stage.new_caches()
+        # a caller's cache may not be allocated yet (DeviceKVCache(n) allocates lazily)
+        self.cache.allocate(stage.nkv, stage.hd, stage.max_ctx, stage.device)
         dev = stage.device
         self.tok = torch.zeros(1, dtype=torch.int32, device=dev)
         self.history = torch.zeros(stage.max_ctx, dtype=torch.int32, device=dev)

@@ -20,7 +20,10 @@ import numpy as np
 
 from .q4 import REF_DIR, REF_VARIANTS
 
-REF_ROOT = os.environ.get("HETERO_REF_ROOT", "/root/reference")
+# The reference checkout: $HETERO_REF_ROOT, else a directory named
+# `reference` beside this repository.
+REF_ROOT = os.environ.get("HETERO_REF_ROOT") or os.path.abspath(
+    os.path.join(os.path.dirname(os.path.abspath(__file__)), "..", "..", "reference"))
 
 
 def available() -> bool:

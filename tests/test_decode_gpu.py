@@ -92,6 +92,39 @@ def test_persistent_decode_rejects_unfit_shapes(cuda):
     from hetero_infer_b200 import cuda_model
     cfg = synth.small_config(layers=1, hidden=256, heads=4, kv_heads=2, inter=512, vocab=300)  # n_in/gs = 4
     stage = _stage(cfg, seed=1)
-    assert cuda_model.GreedyDecoder(stage).plan is None  # "auto": one launch per layer step
+    assert cuda_model.GreedyDecoder(stage, persistent="auto").plan is None  # falls back to per-layer launches
+    assert cuda_model.GreedyDecoder(stage).plan is None  # the default: per-layer launches
     with pytest.raises(ValueError):
         cuda_model.GreedyDecoder(stage, persistent=True)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("ci", range(len(CONFIGS)))
+def test_persistent_decode_logits_match_stage_oracle(cuda, ci):
+    """Every step's logits of the persistent plan against the NumPy stage
+    oracle (oracle/stage.py, pinned bit for bit to the reference's
+    cpu_model.Stage): relative L2 <= 2e-5 and the same greedy token."""
+    import torch
+    from hetero_infer_b200 import cuda_model
+    from oracle import stage as ost
+    from tests.test_stage_gpu import LOGIT_TOL, _decode_top5, rel_l2
+    cfg = synth.small_config(**CONFIGS[ci])
+    seed = 80 + ci
+    w = synth.model_weights(cfg, seed)
+    stage = cuda_model.Stage(cfg, Spec(0, cfg["num_hidden_layers"], True, True), w, max_ctx=256)
+    orc = ost.OracleStage(cfg, w, 0, cfg["num_hidden_layers"], True, True,
+                          embed_rows=lambda ids: synth.embed_rows(seed, ids, cfg["hidden_size"]))
+    dec = cuda_model.GreedyDecoder(stage, persistent=True)
+    prompt = synth.prompt_ids(40 + ci, 6, cfg["vocab_size"])
+    n = 10
+    toks, rows = _decode_top5(dec, prompt, n)
+    oc = orc.new_caches()
+    x = prompt
+    for i in range(n):
+        b = orc(x, oc, apply_head=True, last_only=True)[0, -1]
+        assert rel_l2(rows[i], b) <= LOGIT_TOL, f"step {i}: {rel_l2(rows[i], b):.2e}"
+        assert toks[i] == int(b.argmax()), f"step {i}: token {toks[i]} vs {int(b.argmax())}"
+        x = np.array([[toks[i]]])
+    dec.graph = None
+    dec.plan.close()
+    torch.cuda.synchronize()

@@ -12,6 +12,7 @@ import pytest
 import torch.multiprocessing as mp
 
 from hetero_infer_b200 import pipeline, synth
+from tests._oracle_compute import OracleCompute
 
 CFG = dict(layers=3, hidden=256, heads=4, kv_heads=2, inter=512, vocab=1000)
 SEED, N_MICRO, PROMPT, STEPS = 4, 3, 5, 4
@@ -64,9 +65,9 @@ def _rank_main(rank, world, port, cuts, q, wire="float16"):
         cfg = synth.small_config(**CFG)
         a, b = cuts[rank], cuts[rank + 1]
         w = synth.model_weights(cfg, SEED, layers=range(a, b), embed=(rank == 0), head=True)
-        comp = pipeline.OracleCompute(cfg, a, b, w, pipeline.head_rows(cfg["vocab_size"], world, rank),
-                                      embed_rows=lambda ids: synth.embed_rows(SEED, ids, cfg["hidden_size"]),
-                                      wire=wire)
+        comp = OracleCompute(cfg, a, b, w, pipeline.head_rows(cfg["vocab_size"], world, rank),
+                             embed_rows=lambda ids: synth.embed_rows(SEED, ids, cfg["hidden_size"]),
+                             wire=wire)
         pr = pipeline.PipelineRank(pipeline.Comm(rank, world, torch.device("cpu")), comp, N_MICRO)
         pr.prefill([synth.prompt_ids(100 + m, PROMPT, cfg["vocab_size"]) for m in range(N_MICRO)])
         pr.decode(STEPS)

@@ -155,12 +155,54 @@ def test_stage_matches_reference_golden_small(cuda):
     assert toks == [int(t) for t in g["tokens_float"]]
 
 
+def _decode_top5(dec, prompt, n):
+    """Greedy decode of n tokens step by step, keeping each step's logits at
+    the indices a caller asks for later: returns (tokens, list of logits rows
+    as float32 numpy arrays)."""
+    import torch
+    rows = []
+    dec.prefill(prompt)
+    torch.cuda.synchronize()
+    rows.append(dec.logits[0].cpu().numpy().copy())
+    if n > 1:
+        dec.capture()
+        torch.cuda.synchronize()
+        rows.append(dec.logits[0].cpu().numpy().copy())
+    for _ in range(n - 2):
+        dec.steps(1)
+        torch.cuda.synchronize()
+        rows.append(dec.logits[0].cpu().numpy().copy())
+    return dec.tokens()[:n], rows
+
+
+def check_top5_steps(rows, steps, rtol=1e-4):
+    """Every step's logits against the reference's recorded top 5: the same
+    top-1 token; the reference's five values reproduced at its five indices
+    within rtol; and no other index above the reference's fifth value (beyond
+    rtol).  Returns the smallest top-1 margin seen."""
+    worst = float("inf")
+    for i, (z, g) in enumerate(zip(rows, steps)):
+        idx, val = np.asarray(g["top5_idx"]), np.asarray(g["top5_val"], np.float64)
+        assert int(z.argmax()) == g["token"] == int(idx[0]), f"step {i}: token {int(z.argmax())} vs {g['token']}"
+        np.testing.assert_allclose(z[idx], val, rtol=rtol, err_msg=f"step {i}: top-5 values")
+        ours = np.argsort(-z, kind="stable")[:5]
+        for j in ours:
+            if j not in idx:
+                assert z[j] <= val[4] + rtol * abs(val[4]), f"step {i}: index {j} ({z[j]}) enters the top 5"
+        top2 = np.partition(z, -2)[-2:]
+        worst = min(worst, float(top2[1] - top2[0]))
+    return worst
+
+
 @pytest.mark.gpu
-def test_7b_greedy_decode_token_identical_to_reference(cuda):
+@pytest.mark.parametrize("persistent", [False, True])
+def test_7b_greedy_decode_token_identical_to_reference(cuda, persistent):
     """Benchmark config 4: the Qwen2-7B-shape random model, 32-token prompt, 128
-    greedy tokens on one B200 through the graph-captured decoder, against the
-    tokens the reference's NumPy backend generated (both of its kernel builds,
-    tests/golden/golden_7b.json); first-step top-5 logits within 1e-4."""
+    greedy tokens on one B200 through the graph-captured decoder (per-layer
+    launches and the persistent plan), against the tokens the reference's
+    NumPy backend generated with both of its kernel builds
+    (tests/golden/golden_7b.json), and against the reference's top-5 logits
+    (float build) at every one of the 128 steps within 1e-4."""
     import json
     import os
     import torch
@@ -175,12 +217,15 @@ def test_7b_greedy_decode_token_identical_to_reference(cuda):
     assert np.array_equal(prompt, synth.prompt_ids(gold["seed"], gold["prompt_tokens"], cfg["vocab_size"]))
     stage = cuda_model.Stage(cfg, Spec(0, cfg["num_hidden_layers"], True, True), w, max_ctx=512)
     del w
-    z = stage(prompt, stage.new_caches(), apply_head=True, last_only=True).cpu().numpy()[0, -1]
-    g0 = gold["variants"]["float"]["steps"][0]
-    assert [int(i) for i in np.argsort(-z, kind="stable")[:5]] == g0["top5_idx"]
-    np.testing.assert_allclose(z[g0["top5_idx"]], g0["top5_val"], rtol=1e-4)
-    toks = cuda_model.GreedyDecoder(stage).generate(prompt, gold["generated"])
+    dec = cuda_model.GreedyDecoder(stage, persistent=persistent)
+    assert (dec.plan is not None) == persistent
+    toks, rows = _decode_top5(dec, prompt, gold["generated"])
     for v in ("avx2", "float"):
         ref = [s["token"] for s in gold["variants"][v]["steps"]]
         assert toks == ref, f"tokens differ from the reference ({v} kernel)"
+    margin = check_top5_steps(rows, gold["variants"]["float"]["steps"])
+    assert margin > 0.0
+    dec.graph = None
+    if dec.plan is not None:
+        dec.plan.close()
     torch.cuda.synchronize()
