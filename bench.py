@@ -14,7 +14,10 @@ reference's packed layout; four copies of the layer (526 MB, larger than the
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
 N > 1 is launched by torchrun, one rank per GPU; every rank runs its own
-copy of the workload (weak scaling) and the time is the max over ranks.
+copy of the layer workload (weak scaling) and the time is the max over ranks;
+beside it every N > 1 run measures config 5, the planner's pipeline of the
+7B-shape model over the N GPUs (NCCL hand-off, row-sharded lm_head), as
+`pipeline` with its tok/s, roofline and a token-parity check on every rank.
 `--impl reference` times the reference's own CPU kernel (kernel/q4gemv.c,
 built from source into oracle/_ref/) on the host cores for the same metric.
 Prints one JSON line (rank 0).
@@ -85,17 +88,27 @@ def measured_tensor_peak() -> float:
         return 1590.0
 
 
+TRAFFIC_FILE = os.path.join("profiles", "gemv_stream_traffic.txt")
+
+
 def profiled_traffic():
-    """DRAM bytes per GEMV launch of the layer step, from the committed ncu
-    summary (profiles/gemv_stream_layer_step.md), or None."""
-    path = os.path.join(ROOT, "profiles", "gemv_stream_layer_step.md")
+    """DRAM bytes (read + write) per GEMV launch of the layer step as one ncu
+    capture measured them, with where and when that capture was taken:
+    (bytes or None, source string)."""
+    path = os.path.join(ROOT, TRAFFIC_FILE)
+    info = {}
     try:
         for line in open(path):
-            if line.startswith("traffic_bytes_per_launch:"):
-                return float(line.split(":", 1)[1].split()[0])
+            if ":" in line:
+                k, v = line.split(":", 1)
+                info[k.strip()] = v.strip()
     except OSError:
-        pass
-    return None
+        return None, "no capture"
+    try:
+        nbytes = float(info["traffic_bytes_per_launch"].split()[0])
+    except (KeyError, ValueError):
+        return None, "no capture"
+    return nbytes, f"ncu capture {TRAFFIC_FILE} ({info.get('captured', 'undated')})"
 
 
 # ---------------------------------------------------------------- clocks
@@ -248,13 +261,12 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     value = world * args.steps * STEP_BYTES / (ms_max * 1e-3) / 1e9
 
     pipe = None
-    if world > 1 and not args.no_extras:
-        pipe = {f"micro{m}": pipeline_bench(rank, world, dev, m) for m in (4, 8)}
-        pipe["micro8_int8_wire"] = pipeline_bench(rank, world, dev, 8, wire="int8")
+    if world > 1:
+        pipe = pipeline_suite(rank, world, dev)
     result = None
     if rank == 0:
         peak, peak_kind = measured_peak()
-        traffic = profiled_traffic()
+        traffic, traffic_src = profiled_traffic()
         result = {
             "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
@@ -266,20 +278,24 @@ def run_ours(args, rank: int, world: int, local_rank: int):
                          "peak_kind": peak_kind, "unit": "GB/s",
                          "frac": round(value / world / peak, 4),
                          "frac_of_8000": round(value / world / 8000.0, 4),
-                         "traffic": traffic, "algorithmic_bytes_per_launch": STEP_BYTES / len(LAUNCHES),
+                         "traffic": traffic, "traffic_source": traffic_src,
+                         "algorithmic_bytes_per_launch": STEP_BYTES / len(LAUNCHES),
                          "kernel": "gemv_stream_kernel (avg over the step's 4 launches)"},
             "clocks": sampler.summary(t_wall0, t_wall1),
             "gpu_launches": len(LAUNCHES) * args.steps,
         }
         if pipe is not None:
+            # config 5 beside the headline: the pipelined decode over the N GPUs
             result["pipeline"] = pipe
+            result["pipeline_tok_s"] = pipe["micro8"]["tok_s"]
+            result["pipeline_parity"] = pipe["parity"]
         if not args.no_extras:
             result["per_projection"] = per_projection(lib, dev, gen, stream, q4_on_device)
             result["gemv_3584x18944"] = result["per_projection"]["gate"]
             result["gemm_w4a16"] = gemm_bench(lib, dev, gen, stream, q4_on_device)
             result["e2e"] = e2e_qlinear(args, dev, cuda_model, synth, np)
             if world == 1:
-                result["decode"] = decode_bench(dev)
+                result["decode"] = decode_bench(dev, cpu_seconds=args.cpu_seconds)
             if world == 1:
                 result["cpu_baseline"] = cpu_baseline(args, budget_s=args.cpu_seconds)
     if world > 1:
@@ -403,12 +419,14 @@ def gemm_bench(lib, dev, gen, stream, q4_on_device, launches=60):
     return out
 
 
-def decode_bench(dev, n_tokens: int = 128, prompt_len: int = 32):
+def decode_bench(dev, n_tokens: int = 128, prompt_len: int = 32, cpu_seconds: float = 0.0):
     """Benchmark config 4: greedy decode of the random-init Qwen2-7B-shape model
     on one device -- 32-token prompt, then one CUDA-graph replay per generated
     token (embedding, 28 layers, head, argmax, position advance).  Decode tok/s
     over the graph-replayed steps (CUDA events); TTFT is the prefill plus first
-    token."""
+    token.  With cpu_seconds > 0 the same model's greedy decode on the host
+    cores (the reference's NumPy stage procedure over the reference's own
+    kernel) is timed beside it as s/token."""
     import numpy as np
     import torch
     from hetero_infer_b200 import cuda_model, synth
@@ -420,6 +438,7 @@ def decode_bench(dev, n_tokens: int = 128, prompt_len: int = 32):
     t0 = time.perf_counter()
     w = synth.model_weights(cfg, 0)
     stage = cuda_model.Stage(cfg, Spec, w, device=dev, max_ctx=512)
+    cpu = cpu_decode_baseline(cfg, w, cpu_seconds) if cpu_seconds > 0 else None
     del w
     t_load = time.perf_counter() - t0
     prompt = synth.prompt_ids(0, prompt_len, cfg["vocab_size"])
@@ -458,23 +477,90 @@ def decode_bench(dev, n_tokens: int = 128, prompt_len: int = 32):
         del dec
         return out, toks
 
-    res, toks = run("auto")
-    res_layers, toks_layers = run(False)
-    res.update({"hbm_ceiling_tok_s": round(measured_peak()[0] * 1e9 / per_token_bytes, 1),
-                "per_layer_launches": res_layers, "tokens_equal_per_layer_path": toks == toks_layers,
+    res, toks = run(False)
+    res_pers, toks_pers = run(True)
+    peak, peak_kind = measured_peak()
+    achieved = per_token_bytes * res["tok_s"] / 1e9
+    res.update({"hbm_ceiling_tok_s": round(peak * 1e9 / per_token_bytes, 1),
+                "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "peak_kind": peak_kind,
+                             "unit": "GB/s", "frac": round(achieved / peak, 4),
+                             "bytes_per_token": per_token_bytes,
+                             "what": "weight bytes streamed per token (28 layers' projections + lm_head, "
+                                     "algorithmic) x tok/s"},
+                "persistent_plan": res_pers, "tokens_equal_persistent_path": toks == toks_pers,
                 "model": "qwen2-7b-shape random int4 (28 layers, h3584, 28q/4kv, i18944, v152064)",
                 "setup_s": round(t_load, 1)})
+    if cpu is not None:
+        res["cpu_baseline"] = cpu
     return res
 
 
-def pipeline_bench(rank: int, world: int, dev, n_micro: int, n_tokens: int = 256, prompt_len: int = 32,
-                   wire: str = "float16"):
+def cpu_decode_baseline(cfg, w, budget_s: float, prompt_len: int = 4):
+    """Config 4 on the host cores: greedy decode of the same 7B-shape model
+    through the reference's NumPy stage procedure (oracle/stage.py, pinned bit
+    for bit to hetero/cpu_model.py:309-368) whose GEMVs call the reference's
+    own kernel built from source (kernel/q4gemv.c, AVX2 build, all cores),
+    as QLinear._gemv calls it (cpu_model.py:109-117).  A short prompt (rows
+    <= 16 take the GEMV path) then decode steps until the budget runs out;
+    s/token over the decode steps."""
+    import numpy as np
+    from hetero_infer_b200 import synth
+    from oracle import stage as ost
+    cores = cpu_cores()
+    os.environ["HETERO_KERNEL_THREADS"] = str(min(cores, 16))
+    kern, kind, what = cpu_kernel()
+    if kern is None:
+        from oracle.q4 import Oracle
+        orc = Oracle()
+    else:
+        class _RefOrc:  # the reference kernel behind the oracle stage's product calls
+            def gemv_f32(self, w_, s_, b_, x, gs):
+                return kern.gemv(w_, s_, b_, x, gs, nthreads=cores)
+
+            def dequant(self, w_, s_, b_, r0, r1, gs):
+                return kern.dequant(w_, s_, b_, r0, r1, gs, nthreads=cores)
+        orc = _RefOrc()
+    L, H = cfg["num_hidden_layers"], cfg["hidden_size"]
+    st = ost.OracleStage(cfg, w, 0, L, True, True, embed_rows=lambda ids: synth.embed_rows(0, ids, H), orc=orc)
+    caches = st.new_caches()
+    prompt = synth.prompt_ids(0, prompt_len, cfg["vocab_size"])
+    z = st(prompt, caches, apply_head=True, last_only=True)
+    tok = int(z[0, -1].argmax())
+    steps = 0
+    t0 = time.perf_counter()
+    while True:
+        z = st(np.array([[tok]]), caches, apply_head=True, last_only=True)
+        tok = int(z[0, -1].argmax())
+        steps += 1
+        if time.perf_counter() - t0 > budget_s or steps >= 64:
+            break
+    dt = time.perf_counter() - t0
+    return {"value": round(dt / steps, 4), "unit": "s/token", "tok_s": round(steps / dt, 2), "cores": cores,
+            "kind": "port" if kern is None else "reference",
+            "sample": f"{steps} greedy decode steps of the 7B-shape model after a {prompt_len}-token prompt "
+                      f"({dt:.1f} s); NumPy stage procedure of hetero/cpu_model.py (oracle/stage.py) with "
+                      f"HETERO_KERNEL_THREADS={min(cores, 16)}; GEMV: {what}"}
+
+
+def pipeline_suite(rank: int, world: int, dev, n_tokens: int = 256, prompt_len: int = 32):
     """Benchmark config 5: the 7B-shape random model split by the planner over
-    the `world` GPUs (NCCL send/recv of the fp16 hidden state between stages,
-    lm_head row-sharded over all ranks), `n_micro` independent streams in
-    flight, `n_tokens` per stream.  Aggregate decode tok/s over the pipelined
-    decode: wall clock between two device synchronisations, max over ranks
-    (the work spans the compute stream and NCCL's streams)."""
+    the `world` GPUs, hidden states handed on by NCCL send/recv, the lm_head
+    row-sharded over all ranks, 4 and 8 independent streams in flight,
+    `n_tokens` per stream; the reference's fp16 wire (4 and 8 streams) and its
+    int8 codec (8 streams).  Aggregate decode tok/s: wall clock between two
+    device synchronisations around the decode, max over ranks.
+
+    Roofline: every generated token streams the whole model's weights once
+    (split over the stages), so achieved = tok/s x weight bytes per token,
+    against world x the measured HBM peak.
+
+    Parity (checked on every rank, all-reduced): the fp32 wire carries the
+    hidden state unchanged, so the pipelined model computes the unsplit one;
+    stream 0 is fed the prompt of the reference's own 7B decode and its 128
+    tokens must equal the ones the reference's NumPy backend generated
+    (tests/golden/golden_7b.json).  The fp16 wire's tokens follow the
+    reference's pipeline, which overflows fp16 on this model."""
+    import json as _json
     import torch
     import torch.distributed as dist
     from hetero_infer_b200 import pipeline, planner, synth
@@ -482,36 +568,61 @@ def pipeline_bench(rank: int, world: int, dev, n_micro: int, n_tokens: int = 256
     plan = planner.plan_gpu_pipeline(cfg, world, layer_s=60e-6, head_s=52e-6)
     spec = plan.specs[rank]
     w = synth.model_weights(cfg, 0, layers=range(spec.start, spec.end), embed=spec.embed, head=True)
-    comp = pipeline.DeviceCompute(cfg, spec, w, pipeline.head_rows(cfg["vocab_size"], world, rank), dev,
-                                  max_ctx=512, wire=wire)
+    per_token_bytes = 28 * sum(alg_bytes(n, k) for _, n, k in PROJECTIONS) + alg_bytes(cfg["vocab_size"], HIDDEN)
+    peak, peak_kind = measured_peak()
+    rows = pipeline.head_rows(cfg["vocab_size"], world, rank)
+
+    def run(comp, prompts, n_tok):
+        comp.release_graphs()
+        pr = pipeline.PipelineRank(pipeline.Comm(rank, world, dev), comp, len(prompts))
+        pr.prefill(prompts)
+        dist.barrier(device_ids=[dev.index])
+        torch.cuda.synchronize(dev)
+        t0 = time.perf_counter()
+        pr.decode(n_tok - 1)
+        torch.cuda.synchronize(dev)
+        dt = time.perf_counter() - t0
+        t = torch.tensor([dt], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return pr, float(t.item())
+
+    out = {"cuts": plan.cuts, "head": "row-sharded over all ranks", "tokens_per_stream": n_tokens,
+           "timing": "host wall clock around the decode loop, device synchronised on both sides (sampled "
+                     "tokens stay on the device), max over ranks"}
+    for wire, micros in (("float16", (4, 8)), ("int8", (8,))):
+        comp = pipeline.DeviceCompute(cfg, spec, w, rows, dev, max_ctx=512, wire=wire)
+        for m in micros:
+            prompts = [synth.prompt_ids(1000 + i, prompt_len, cfg["vocab_size"]) for i in range(m)]
+            pr, dt = run(comp, prompts, n_tokens)
+            gen = m * (n_tokens - 1)
+            tok_s = gen / dt
+            achieved = tok_s * per_token_bytes / 1e9
+            key = f"micro{m}" + ("" if wire == "float16" else "_int8_wire")
+            out[key] = {"streams": m, "decode_tokens": gen, "tok_s": round(tok_s, 1), "seconds": round(dt, 3),
+                        "ticks": pr.ticks, "ms_per_tick": round(dt * 1e3 / pr.ticks, 4),
+                        "wire": "fp16 (reference format)" if wire == "float16" else
+                                "int8 codec (reference transport codec, on device)",
+                        "first_tokens": pr.tokens[0][:6],
+                        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": round(world * peak, 1),
+                                     "peak_kind": f"{world} x {peak_kind}", "unit": "GB/s",
+                                     "frac": round(achieved / (world * peak), 4)}}
+        del comp
+        torch.cuda.empty_cache()
+    gold = _json.load(open(os.path.join(ROOT, "tests", "golden", "golden_7b.json")))
+    comp = pipeline.DeviceCompute(cfg, spec, w, rows, dev, max_ctx=512, wire="float32")
     del w
-    pr = pipeline.PipelineRank(pipeline.Comm(rank, world, dev), comp, n_micro)
-    prompts = [synth.prompt_ids(1000 + m, prompt_len, cfg["vocab_size"]) for m in range(n_micro)]
-    pr.prefill(prompts)
-    dist.barrier(device_ids=[dev.index])
-    torch.cuda.synchronize(dev)
-    t0 = time.perf_counter()
-    pr.decode(n_tokens - 1)
-    torch.cuda.synchronize(dev)
-    dt = time.perf_counter() - t0
-    t = torch.tensor([dt], device=dev)
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    dt = float(t.item())
-    gen = n_micro * (n_tokens - 1)
-    zeros = all(t == 0 for toks in pr.tokens for t in toks)
-    return {"streams": n_micro, "tokens_per_stream": n_tokens, "decode_tokens": gen,
-            "tok_s": round(gen / dt, 1), "seconds": round(dt, 3), "ticks": pr.ticks,
-            "ms_per_tick": round(dt * 1e3 / pr.ticks, 4), "cuts": plan.cuts,
-            "head": "row-sharded over all ranks",
-            "wire": ("fp16 NCCL send/recv (reference format)" if wire == "float16" else
-                     "int8 codec NCCL send/recv (reference transport codec, encoded/decoded on device)"),
-            "first_tokens": pr.tokens[0][:6],
-            "tokens_note": ("every token 0, as the reference's own stages produce on this model: its residual "
-                            "stream exceeds fp16 range at the cut, the fp16 wire carries inf, the next RMSNorm "
-                            "NaN, and numpy argmax of NaN logits is 0 (tests/golden/golden_7b_pipe.json)")
-            if zeros else "finite logits",
-            "timing": "host wall clock around the decode loop, device synchronised on both sides "
-            "(no host sync inside it: sampled tokens stay on the device), max over ranks"}
+    gp = synth.prompt_ids(gold["seed"], gold["prompt_tokens"], cfg["vocab_size"])
+    others = [synth.prompt_ids(2000 + i, prompt_len, cfg["vocab_size"]) for i in range(3)]
+    pr, dt = run(comp, [gp] + others, gold["generated"])
+    ref = [st["token"] for st in gold["variants"]["float"]["steps"]]
+    ok = torch.tensor([1 if pr.tokens[0] == ref else 0], device=dev)
+    dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+    out["parity"] = bool(ok.item())
+    out["parity_check"] = (f"fp32-wire pipeline, stream 0 of 4: {gold['generated']} greedy tokens vs the reference "
+                           f"NumPy backend's unsplit decode (tests/golden/golden_7b.json), every rank")
+    del comp
+    torch.cuda.empty_cache()
+    return out
 
 
 def e2e_qlinear(args, dev, cuda_model, synth, np):
@@ -625,6 +736,64 @@ def run_reference(args, rank: int, world: int):
     }
 
 
+def profile_case(which: str) -> None:
+    """A short, fixed run of one kernel family for an ncu capture (a profiler
+    replays each captured launch many times, so these cases hold a few GB at
+    most and launch little before the captured kernels):
+
+      layer   the four GEMV launches of a Qwen2-7B-shape layer at batch 1
+              (q|k|v 4608x3584, o 3584x3584, gate|up 37888x3584, down
+              3584x18944), three rounds over two weight copies;
+      gemm    hq4_gemm_w4a16 on 18944x3584 at 16 tokens (register-path
+              kernel) and 256 tokens (tcgen05 kernel), bf16 activations,
+              three calls each;
+      decode  the 7B-shape stage's decode step, per-layer launches, 4 steps
+              after a 4-token prompt.
+
+    Weights are seeded random int4 with the benchmark's scale/bias law."""
+    import torch
+    from hetero_infer_b200 import _lib, ops
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    g = torch.Generator(device=dev)
+    g.manual_seed(0)
+    lib = _lib.load()
+    st = torch.cuda.current_stream().cuda_stream
+
+    def q4(n, k):
+        w = torch.randint(-2 ** 31, 2 ** 31 - 1, (n, k // 8), dtype=torch.int32, device=dev, generator=g)
+        s_ = (torch.randn(n, k // GS, device=dev, generator=g).abs() * 0.01).half()
+        return w, s_, (s_.float() * -8).half()
+
+    if which == "layer":
+        mats = [[(q4(n, k), torch.randn(1, k, device=dev, generator=g), torch.empty(1, n, device=dev), n, k)
+                 for _, n, k in LAUNCHES] for _ in range(2)]
+        for r in range(3):
+            for (w, s_, b), x, y, n, k in mats[r % 2]:
+                _lib.check(lib.hq4_gemv(w.data_ptr(), s_.data_ptr(), b.data_ptr(), x.data_ptr(), y.data_ptr(),
+                                        n, k, GS, 1, st), "hq4_gemv")
+    elif which == "gemm":
+        n, k = 18944, 3584
+        w, s_, b = q4(n, k)
+        for m in (16, 256):
+            x = torch.randn(m, k, device=dev, generator=g).to(torch.bfloat16)
+            for _ in range(3):
+                ops.q4_gemm(w, s_, b, x, GS)
+    elif which == "decode":
+        from hetero_infer_b200 import cuda_model, synth
+
+        class Spec:
+            start, end, embed, head = 0, 28, True, True
+        cfg = dict(synth.QWEN2_7B)
+        stage = cuda_model.Stage(cfg, Spec, synth.model_weights(cfg, 0), device=dev, max_ctx=64)
+        dec = cuda_model.GreedyDecoder(stage)
+        dec.generate(synth.prompt_ids(0, 4, cfg["vocab_size"]), 6)
+    else:
+        raise SystemExit(f"unknown case {which}")
+    torch.cuda.synchronize()
+    print(json.dumps({"case": which, "status": lib.hq4_device_status(0)}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -638,7 +807,12 @@ def main():
                     help="N>1: only run the config-5 pipeline (TOKENS per stream, 4 and 8 streams)")
     ap.add_argument("--decode-only", type=int, default=0, metavar="TOKENS",
                     help="only run the config-4 decode (TOKENS generated) and print its JSON")
+    ap.add_argument("--case", choices=["layer", "gemm", "decode"], default=None,
+                    help="run one short fixed case for a profiler capture and exit")
     args = ap.parse_args()
+    if args.case:
+        profile_case(args.case)
+        return
     if args.warmup < 3:
         args.warmup = 3
     rank = int(os.environ.get("RANK", "0"))
@@ -660,10 +834,7 @@ def main():
         torch.cuda.set_device(local_rank)
         dev = torch.device("cuda", local_rank)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
-        out = {f"micro{m}": pipeline_bench(rank, world, dev, m, n_tokens=max(3, args.pipeline_only))
-               for m in (4, 8)}
-        out["micro8_int8_wire"] = pipeline_bench(rank, world, dev, 8, n_tokens=max(3, args.pipeline_only),
-                                                 wire="int8")
+        out = pipeline_suite(rank, world, dev, n_tokens=max(3, args.pipeline_only))
         if rank == 0:
             print(json.dumps({"pipeline": out, "n_gpus": world}), flush=True)
         dist.destroy_process_group()

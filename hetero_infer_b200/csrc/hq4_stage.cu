@@ -200,6 +200,16 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(
 // [rows][cols] int8.  (Non-finite inputs are outside the codec's contract.)
 constexpr int kCodecThreads = 256;
 
+// kWire: each value is first rounded to fp16 and widened back, as the
+// reference's engine encodes the fp16 wire array (NumpyBackend.to_wire,
+// hetero/backends.py:100-101, then transport.encode, hetero/engine.py:97).
+template <bool kWire>
+__device__ __forceinline__ float codec_in(const float* xr, int i) {
+    const float v = xr[i];
+    return kWire ? __half2float(__float2half_rn(v)) : v;
+}
+
+template <bool kWire>
 __global__ void __launch_bounds__(kCodecThreads) act_encode_i8_kernel(const float* __restrict__ x, int rows, int cols,
                                                                      unsigned char* __restrict__ payload) {
     __shared__ float red[kCodecThreads / 32];
@@ -209,7 +219,7 @@ __global__ void __launch_bounds__(kCodecThreads) act_encode_i8_kernel(const floa
     const int r = blockIdx.x;
     const float* xr = x + (size_t)r * cols;
     float amax = 0.0f;
-    for (int i = threadIdx.x; i < cols; i += kCodecThreads) amax = fmaxf(amax, fabsf(xr[i]));
+    for (int i = threadIdx.x; i < cols; i += kCodecThreads) amax = fmaxf(amax, fabsf(codec_in<kWire>(xr, i)));
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
     if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
@@ -226,7 +236,7 @@ __global__ void __launch_bounds__(kCodecThreads) act_encode_i8_kernel(const floa
     const float sc = s_scale;
     signed char* q = reinterpret_cast<signed char*>(payload + (size_t)rows * 4 + (size_t)r * cols);
     for (int i = threadIdx.x; i < cols; i += kCodecThreads) {
-        const float v = fminf(fmaxf(rintf(__fdiv_rn(xr[i], sc)), -127.0f), 127.0f);
+        const float v = fminf(fmaxf(rintf(__fdiv_rn(codec_in<kWire>(xr, i), sc)), -127.0f), 127.0f);
         q[i] = (signed char)(int)v;
     }
 }
@@ -437,8 +447,16 @@ extern "C" int hq4_act_encode_i8(const float* x, int rows, int cols, void* paylo
     if (int rc = check_device_cap()) return rc;
     if (rows <= 0 || cols <= 0 || !x || !payload) return HQ4_ERR_SHAPE;
     if (((uintptr_t)x & 3) || ((uintptr_t)payload & 3)) return HQ4_ERR_ALIGN;
-    return launch_pdl(act_encode_i8_kernel, dim3(rows), dim3(kCodecThreads), 0, static_cast<cudaStream_t>(stream), x,
-                      rows, cols, static_cast<unsigned char*>(payload));
+    return launch_pdl(act_encode_i8_kernel<false>, dim3(rows), dim3(kCodecThreads), 0,
+                      static_cast<cudaStream_t>(stream), x, rows, cols, static_cast<unsigned char*>(payload));
+}
+
+extern "C" int hq4_act_encode_i8_wire(const float* x, int rows, int cols, void* payload, void* stream) {
+    if (int rc = check_device_cap()) return rc;
+    if (rows <= 0 || cols <= 0 || !x || !payload) return HQ4_ERR_SHAPE;
+    if (((uintptr_t)x & 3) || ((uintptr_t)payload & 3)) return HQ4_ERR_ALIGN;
+    return launch_pdl(act_encode_i8_kernel<true>, dim3(rows), dim3(kCodecThreads), 0,
+                      static_cast<cudaStream_t>(stream), x, rows, cols, static_cast<unsigned char*>(payload));
 }
 
 extern "C" int hq4_act_decode_i8(const void* payload, int rows, int cols, uint16_t* out_f16, float* out_f32,

@@ -176,17 +176,21 @@ def gemm_plan(n_out: int, n_in: int, m: int, x_is_f32: bool = False) -> dict:
     return d
 
 
-def act_encode_i8(x: torch.Tensor, payload: Optional[torch.Tensor] = None) -> torch.Tensor:
+def act_encode_i8(x: torch.Tensor, payload: Optional[torch.Tensor] = None, wire: bool = False) -> torch.Tensor:
     """int8 wire payload of fp32 activations [..., cols] (hetero/transport.py:198-211):
-    the rows' fp32 scales then the int8 rows, as a uint8 tensor."""
+    the rows' fp32 scales then the int8 rows, as a uint8 tensor.  wire=True
+    rounds every value to fp16 first, as the reference's engine encodes the
+    fp16 array its backend's to_wire made (hetero/engine.py:97)."""
     xs = x.contiguous()
     cols = int(xs.shape[-1])
     rows = xs.numel() // cols
     if payload is None:
         payload = torch.empty(rows * (4 + cols), dtype=torch.uint8, device=xs.device)
     lib = _lib.load()
-    _lib.check(lib.hq4_act_encode_i8(xs.data_ptr(), rows, cols, payload.data_ptr(),
-                                     torch.cuda.current_stream(xs.device).cuda_stream), "hq4_act_encode_i8")
+    fn, name = (lib.hq4_act_encode_i8_wire, "hq4_act_encode_i8_wire") if wire else \
+        (lib.hq4_act_encode_i8, "hq4_act_encode_i8")
+    _lib.check(fn(xs.data_ptr(), rows, cols, payload.data_ptr(), torch.cuda.current_stream(xs.device).cuda_stream),
+               name)
     return payload
 
 

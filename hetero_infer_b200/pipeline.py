@@ -234,8 +234,9 @@ class DeviceCompute:
     wire: "float16" is the reference's hand-off (backends.py:100-104; values
     beyond fp16 range become inf there and here alike); "int8" is the
     reference's int8 codec (transport.py:198-225: per-row fp32 scale + int8,
-    half the bytes; encoded and decoded on the device, bit-identical to the
-    NumPy codec); "float32" sends the fp32 hidden state unchanged, so the
+    half the bytes) applied, as its engine applies it (engine.py:97), to the
+    fp16 wire array; encoded and decoded on the device, bit-identical to the
+    NumPy codec; "float32" sends the fp32 hidden state unchanged, so the
     pipelined model computes exactly what one unsplit stage computes (not a
     reference format)."""
 
@@ -269,6 +270,11 @@ class DeviceCompute:
 
     def new_cache(self):
         return self.stage.new_caches()
+
+    def release_graphs(self) -> None:
+        """Drop the per-microbatch decode graphs (they are bound to the caches
+        of the runner that captured them); a new runner captures its own."""
+        self._graphs = {}
 
     def embed_forward(self, ids, cache):
         return self.stage(ids, cache, apply_head=False)
@@ -329,7 +335,7 @@ class DeviceCompute:
     def _encode_into(self, h, dst):
         if self.wire == "int8":
             from . import ops
-            ops.act_encode_i8(h.reshape(-1, self.hidden_dim), payload=dst)
+            ops.act_encode_i8(h.reshape(-1, self.hidden_dim), payload=dst, wire=True)
         else:
             dst.copy_(h.view(dst.shape).to(self.wire_dtype))
 

@@ -197,6 +197,12 @@ int hq4_act_encode_i8(const float* x, int rows, int cols, void* payload, void* s
 int hq4_act_decode_i8(const void* payload, int rows, int cols, uint16_t* out_f16, float* out_f32,
                       void* stream);
 
+/* The int8 frame the reference's engine sends (hetero/engine.py:97:
+ * transport.encode(backend.to_wire(y), "int8")): every value of the fp32
+ * hidden state x is rounded to fp16 first (NumpyBackend.to_wire,
+ * hetero/backends.py:100-101), then encoded as hq4_act_encode_i8 does. */
+int hq4_act_encode_i8_wire(const float* x, int rows, int cols, void* payload, void* stream);
+
 /* Greedy sampling (hetero/backends.py:106-109): numpy argmax of x[0..n) --
  * the first NaN if there is one, else the largest value, lowest index among
  * equals (the result is always in [0, n)) -- written to *idx_out; also to history[*pos] when

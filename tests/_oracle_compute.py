@@ -53,7 +53,9 @@ class OracleCompute:
     def to_wire(self, h):
         if self.wire == "int8":
             from oracle import codec
-            return torch.frombuffer(bytearray(codec.encode_i8(np.asarray(h, np.float32))), dtype=torch.uint8)
+            # the reference's engine encodes its backend's fp16 wire array (engine.py:97)
+            h16 = np.asarray(h, np.float16).astype(np.float32)
+            return torch.frombuffer(bytearray(codec.encode_i8(h16)), dtype=torch.uint8)
         return torch.from_numpy(np.ascontiguousarray(np.asarray(h, dtype=np.float16)))
 
     def from_wire(self, t):

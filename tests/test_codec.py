@@ -68,3 +68,21 @@ def test_device_codec_rejects_bad_arguments(cuda):
     assert lib.hq4_act_encode_i8(x.data_ptr(), 0, 16, p.data_ptr(), st) == -1
     assert lib.hq4_act_decode_i8(p.data_ptr(), 1, 16, None, None, st) == -1
     assert lib.hq4_act_encode_i8(x.data_ptr() + 2, 1, 4, p.data_ptr(), st) == -2
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("rows,cols", [(1, 3584), (6, 513), (2, 256)])
+def test_device_wire_encode_rounds_through_fp16(cuda, rows, cols):
+    """hq4_act_encode_i8_wire gives the bytes of the reference engine's int8
+    frame, transport.encode(backend.to_wire(y), "int8") (hetero/engine.py:97):
+    the fp32 state rounded to fp16 first, then the codec.  Values are spread
+    so the fp16 rounding changes the scales and some of the int8 digits."""
+    import torch
+    from hetero_infer_b200 import ops
+    from oracle import codec
+    rng = np.random.default_rng(rows + cols)
+    x = (rng.standard_normal((rows, cols)) * np.exp(rng.uniform(-3, 9, (rows, 1)))).astype(np.float32)
+    ref = codec.encode_i8(x.astype(np.float16).astype(np.float32))
+    assert ref != codec.encode_i8(x)  # the case distinguishes the two encodings
+    p = ops.act_encode_i8(torch.from_numpy(x).cuda(), wire=True)
+    assert p.cpu().numpy().tobytes() == ref

@@ -46,7 +46,8 @@ def reference_tokens(cuts, wire="float16"):
             for i, s in enumerate(stages):
                 h = s(h, caches[i], apply_head=True, last_only=True)
                 if i < len(stages) - 1 and wire == "int8":
-                    h = np.asarray(h, np.float32)
+                    # engine.py:97: transport.encode(backend.to_wire(y), "int8")
+                    h = np.asarray(h, np.float16).astype(np.float32)
                     h = codec.decode_i8(codec.encode_i8(h), h.shape).astype(np.float32)
                 elif i < len(stages) - 1:
                     h = np.asarray(h, np.float16).astype(np.float32)
