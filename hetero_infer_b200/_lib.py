@@ -48,6 +48,7 @@ SIGNATURES = {
     "hq4_decode_plan_create": (_I, [_P] + [_I] * 7 + [_F, _F, _P, _P, _I] + [_P] * 6),
     "hq4_decode_plan_run": (_I, [_P, _P]),
     "hq4_decode_plan_info": (_I, [_P, _P]),
+    "hq4_decode_plan_fault": (_I, [_P, _I, _LL]),
     "hq4_decode_plan_destroy": (None, [_P]),
 }
 

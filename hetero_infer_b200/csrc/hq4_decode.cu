@@ -107,9 +107,17 @@ __device__ __forceinline__ bool consumers_and(bool v) {
     return r != 0;
 }
 
+// Failure-path test hook, set on the host per plan (hq4_decode_plan_fault):
+// CTA skip_cta withholds its arrival at the first grid barrier, which then
+// never completes, and every barrier wait is bounded by barrier_ns.
+struct DecFault {
+    int skip_cta;               // -1: none
+    unsigned long long barrier_ns;
+};
+
 __global__ void __launch_bounds__(kStrThreads, 1)
 decode_kernel(const DecPhase* __restrict__ phases, const CUtensorMap* __restrict__ maps, int n_phases,
-              DecSync* sy, int* status, const DecLayout L) {
+              DecSync* sy, int* status, const DecLayout L, const DecFault F) {
     extern __shared__ unsigned char smem_raw[];
     __shared__ DecPhase sd[2];  // descriptors of phases ph (slot ph & 1)
     __shared__ int sflag;
@@ -282,7 +290,7 @@ decode_kernel(const DecPhase* __restrict__ phases, const CUtensorMap* __restrict
                         // named barrier) are published by the release; the
                         // acquire below orders the next phase's reads
                         const unsigned long long target = (unsigned long long)ph * G;  // ph barriers
-                        red_release_add_u64(&sy->arrive, 1ull);
+                        if (!(ph == 1 && (int)blockIdx.x == F.skip_cta)) red_release_add_u64(&sy->arrive, 1ull);
                         uint64_t t0 = 0;
                         for (uint32_t n = 1;; n++) {
                             if (ld_acquire_u64(&sy->arrive) >= target) break;
@@ -294,7 +302,7 @@ decode_kernel(const DecPhase* __restrict__ phases, const CUtensorMap* __restrict
                                 const uint64_t now = globaltimer_ns();
                                 if (t0 == 0) {
                                     t0 = now;
-                                } else if (now - t0 > kDecBarrierNs) {
+                                } else if (now - t0 > F.barrier_ns) {
                                     good = false;
                                     break;
                                 }
@@ -377,6 +385,7 @@ struct DecodePlan {
     DecPhase* d_phases = nullptr;
     CUtensorMap* d_maps = nullptr;
     DecSync* d_sync = nullptr;
+    DecFault fault = {-1, kDecBarrierNs};
 };
 
 static size_t dec_smem_limit() {
@@ -579,8 +588,16 @@ extern "C" int hq4_decode_plan_run(void* plan, void* stream) {
     lc.numAttrs = 1;
     const cudaError_t e = cudaLaunchKernelEx(&lc, decode_kernel, (const DecPhase*)pl->d_phases,
                                              (const CUtensorMap*)pl->d_maps, pl->n_phases, pl->d_sync,
-                                             status_word(), pl->L);
+                                             status_word(), pl->L, pl->fault);
     return e == cudaSuccess ? HQ4_OK : HQ4_ERR_LAUNCH;
+}
+
+extern "C" int hq4_decode_plan_fault(void* plan, int skip_cta, long long barrier_ns) {
+    DecodePlan* pl = static_cast<DecodePlan*>(plan);
+    if (!pl || skip_cta >= pl->grid) return HQ4_ERR_SHAPE;
+    pl->fault.skip_cta = skip_cta < 0 ? -1 : skip_cta;
+    pl->fault.barrier_ns = barrier_ns > 0 ? (unsigned long long)barrier_ns : kDecBarrierNs;
+    return HQ4_OK;
 }
 
 extern "C" int hq4_decode_plan_info(void* plan, int* info) {

@@ -588,6 +588,13 @@ class DecodePlan:
         self.stage._check(self.stage.lib.hq4_decode_plan_run(self.handle, self.stage._stream()),
                           "hq4_decode_plan_run")
 
+    def inject_fault(self, skip_cta: int = -1, barrier_ns: int = 0) -> None:
+        """Failure-path testing: CTA skip_cta withholds its first grid-barrier
+        arrival on later runs, whose waits then end after barrier_ns with
+        status bit 0 set (hq4_decode_plan_fault); (-1, 0) restores normal runs."""
+        _lib.check(self.stage.lib.hq4_decode_plan_fault(self.handle, int(skip_cta), int(barrier_ns)),
+                   "hq4_decode_plan_fault")
+
     def info(self) -> dict:
         out = (ctypes.c_int * 4)()
         _lib.check(self.stage.lib.hq4_decode_plan_info(self.handle, out), "hq4_decode_plan_info")

@@ -285,6 +285,15 @@ int hq4_decode_plan_run(void* plan, void* stream);
 /* info[0..3] = grid, ring stages, dynamic shared memory bytes, phases. */
 int hq4_decode_plan_info(void* plan, int* info);
 
+/* Failure-path testing of the plan's grid barrier (no reference
+ * counterpart; the reference's pipeline has no device waits).  skip_cta >= 0
+ * makes that CTA withhold its arrival at the plan's first grid barrier of
+ * every later run, so the barrier never completes: every CTA's wait ends
+ * after barrier_ns (<= 0: the default 1 s), status bit 0 is set, the run
+ * returns with its outputs invalid, and the barrier words are reset for the
+ * next run.  skip_cta = -1 and barrier_ns = 0 restore normal runs. */
+int hq4_decode_plan_fault(void* plan, int skip_cta, long long barrier_ns);
+
 void hq4_decode_plan_destroy(void* plan);
 
 #ifdef __cplusplus

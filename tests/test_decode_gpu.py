@@ -128,3 +128,45 @@ def test_persistent_decode_logits_match_stage_oracle(cuda, ci):
     dec.graph = None
     dec.plan.close()
     torch.cuda.synchronize()
+
+
+@pytest.mark.gpu
+def test_persistent_decode_barrier_timeout_reports_and_recovers(cuda):
+    """Failure path of the plan's grid barrier, without faulting the GPU: one
+    CTA withholds its arrival at the first barrier (hq4_decode_plan_fault),
+    so every CTA's bounded wait (20 ms here) runs out.  The launch returns,
+    status bit 0 reports it, and the barrier words are reset: after the hook
+    is cleared, a full decode through the same plan is bit-identical to the
+    per-layer launches."""
+    import time
+    import torch
+    from hetero_infer_b200 import _lib, cuda_model
+    cfg = synth.small_config(**CONFIGS[0])
+    stage = _stage(cfg, seed=17)
+    lib = _lib.load()
+    prompt = synth.prompt_ids(8, 5, cfg["vocab_size"])
+    ref = cuda_model.GreedyDecoder(stage, persistent=False)
+    dec = cuda_model.GreedyDecoder(stage, persistent=True)
+    dec.prefill(prompt)
+    torch.cuda.synchronize()
+    lib.hq4_device_status(1)
+    dec.plan.inject_fault(skip_cta=3, barrier_ns=20_000_000)
+    t0 = time.perf_counter()
+    with torch.cuda.stream(dec.stream):
+        dec.plan.run()
+    torch.cuda.synchronize()
+    took = time.perf_counter() - t0
+    assert lib.hq4_device_status(1) & 1, "the barrier timeout was not reported"
+    assert took < 10.0
+    dec.plan.inject_fault(-1, 0)
+    # a fresh decode in the same buffers: position back to 0
+    dec.cache.pos.zero_()
+    dec.cache.offset = 0
+    n = 12
+    tb = dec.generate(prompt, n)
+    ta = ref.generate(prompt, n)
+    torch.cuda.synchronize()
+    assert lib.hq4_device_status(0) == 0
+    assert ta == tb
+    assert torch.equal(ref.h, dec.h)
+    assert torch.equal(ref.logits, dec.logits)

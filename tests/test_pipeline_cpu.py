@@ -95,6 +95,65 @@ def test_gloo_pipeline_matches_single_process(cuts, wire):
         assert got[r] == ref, f"rank {r}"
 
 
+def _rank_leaves_main(rank, world, port, q):
+    """Every rank prefills; then the last rank leaves (between steps, with
+    nothing of its own in flight) and the others start decoding.  Each
+    survivor reports the exception its next collective raised and how long
+    that took; the process group's timeout is the outer bound."""
+    import datetime
+    import time
+    import torch
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=20))
+    cfg = synth.small_config(**CFG)
+    cuts = [0, 1, 2, 3]
+    a, b = cuts[rank], cuts[rank + 1]
+    w = synth.model_weights(cfg, SEED, layers=range(a, b), embed=(rank == 0), head=True)
+    comp = OracleCompute(cfg, a, b, w, pipeline.head_rows(cfg["vocab_size"], world, rank),
+                         embed_rows=lambda ids: synth.embed_rows(SEED, ids, cfg["hidden_size"]))
+    pr = pipeline.PipelineRank(pipeline.Comm(rank, world, torch.device("cpu")), comp, N_MICRO)
+    pr.prefill([synth.prompt_ids(100 + m, PROMPT, cfg["vocab_size"]) for m in range(N_MICRO)])
+    dist.barrier()
+    if rank == world - 1:
+        q.put((rank, "left", 0.0))
+    else:
+        t0 = time.perf_counter()
+        try:
+            pr.decode(STEPS)
+            q.put((rank, "no error", time.perf_counter() - t0))
+        except Exception as e:  # noqa: BLE001 -- the test checks which
+            q.put((rank, type(e).__name__, time.perf_counter() - t0))
+    q.close()
+    q.join_thread()
+    os._exit(0)  # no teardown handshake with a group that lost a member
+
+
+def test_gloo_pipeline_rank_leaving_raises_on_survivors():
+    """A stage that goes away is reported to the others as an error from their
+    next collective, within the process group's timeout, not as a hang (the
+    reference's transport surfaces a lost peer as ConnectionError,
+    hetero/transport.py:80-81,148-150)."""
+    world = 3
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank_leaves_main, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    got = {}
+    for _ in procs:
+        r, what, dt = q.get(timeout=240)
+        got[r] = (what, dt)
+    for p in procs:
+        p.join(timeout=60)
+    assert got[world - 1][0] == "left"
+    for r in range(world - 1):
+        what, dt = got[r]
+        assert what not in ("no error",), f"rank {r} finished decoding without its peer"
+        assert dt < 60.0, f"rank {r} took {dt:.1f} s to notice"
+
+
 @pytest.mark.parametrize("micro,steps,stages", [(4, 5, 2), (4, 3, 8), (8, 4, 8), (1, 3, 4), (3, 1, 2)])
 def test_admission_schedule(micro, steps, stages):
     adm = pipeline.admission_schedule(micro, steps, stages)
