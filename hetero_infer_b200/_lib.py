@@ -27,6 +27,7 @@ SIGNATURES = {
     "hq4_device_status": (_I, [_I]),
     "hq4_gemv": (_I, [_P] * 5 + [_I] * 4 + [_P]),
     "hq4_gemv_fused": (_I, [_P] * 5 + [_I] * 4 + [_P] * 3),
+    "hq4_gemv_ex": (_I, [_P] * 5 + [_I] * 4 + [_P] * 2 + [_I, _P]),
     "hq4_gemv_host": (_I, [_P] * 6 + [_I] * 4 + [_P] * 3),
     "hq4_dequant": (_I, [_P] * 4 + [_I] * 4 + [_P]),
     "hq4_embed_f16": (_I, [_P, _P, _I, _I, _I, _P, _P]),

@@ -243,6 +243,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_m1_kernel(const GemvM1Pa
     };
 
     __syncthreads();  // mbarrier initialisation visible to every thread
+    if (p.weights_after_wait) pdl_wait();
 #pragma unroll
     for (int d = 0; d < D; d++) issue(wv[d], sv[d], u0 + d < u1);
 
@@ -470,6 +471,7 @@ gemv_stream_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_consta
         }
         mbar_init_fence();
         pol = l2_policy_evict_first();  // weights are read once
+        if (p.weights_after_wait) pdl_wait();
         const int first = min(R, n_stages);
         for (int i = 0; i < first; i++) issue_stage();
     }
@@ -885,6 +887,22 @@ extern "C" int hq4_gemv_fused(const uint32_t* w, const uint16_t* scales, const u
         int rc = gemv_m1(w, scales, biases, x + (size_t)i * n_in, out + (size_t)i * n_out, n_out,
                          n_in, gs, row_add, residual ? residual + (size_t)i * n_out : nullptr, st);
         if (rc) return rc;
+    }
+    return HQ4_OK;
+}
+
+extern "C" int hq4_gemv_ex(const uint32_t* w, const uint16_t* scales, const uint16_t* biases, const float* x,
+                           float* out, int n_out, int n_in, int gs, int m, const float* row_add,
+                           const float* residual, int flags, void* stream) {
+    if (int rc = check_device()) return rc;
+    if (m <= 0 || (flags & ~HQ4_GEMV_WEIGHTS_AFTER_WAIT)) return HQ4_ERR_SHAPE;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    for (int i = 0; i < m; i++) {
+        GemvM1Params prm = gemv_params(w, scales, biases, x + (size_t)i * n_in, out + (size_t)i * n_out, n_out, n_in);
+        prm.row_add = row_add;
+        prm.residual = residual ? residual + (size_t)i * n_out : nullptr;
+        prm.weights_after_wait = (flags & HQ4_GEMV_WEIGHTS_AFTER_WAIT) ? 1 : 0;
+        if (int rc = gemv_launch(prm, gs, st)) return rc;
     }
     return HQ4_OK;
 }

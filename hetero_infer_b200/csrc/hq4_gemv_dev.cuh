@@ -38,6 +38,8 @@ struct GemvM1Params {
     // epilogue mode
     int mode;               // kEpiPlain, kEpiSiluMul or kEpiQkvRope
     int x_bf16;             // streaming kernel only: x is bf16 (no RMSNorm then)
+    int weights_after_wait; // read the weights only after the dependency wait (they may
+                            // have been written by the preceding kernel)
     // kEpiQkvRope: q|k|v rows of one decoder layer, q and k rows permuted so
     // strip rows g and g+8 are the rotation pair (d, d + head_dim/2)
     int q_strips, k_strips, head_dim, max_ctx;

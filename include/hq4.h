@@ -65,6 +65,19 @@ int hq4_gemv_fused(const uint32_t* w, const uint16_t* scales, const uint16_t* bi
                    const float* x, float* out, int n_out, int n_in, int gs, int m,
                    const float* row_add, const float* residual, void* stream);
 
+/* hq4_gemv_fused with launch options.  hq4_gemv and hq4_gemv_fused start
+ * streaming the weights before waiting for the preceding kernel on the
+ * stream (programmatic dependent launch): only x, the residual and the
+ * outputs are ordered after it.  A caller whose weights were written by the
+ * kernel immediately before (a repack, a dequantise-requantise, an upload
+ * kernel) passes HQ4_GEMV_WEIGHTS_AFTER_WAIT, and the weights are then read
+ * only after that kernel has completed.  Unknown flag bits: -1.  No reference
+ * counterpart (the reference's q4_gemv is synchronous). */
+#define HQ4_GEMV_WEIGHTS_AFTER_WAIT 1
+int hq4_gemv_ex(const uint32_t* w, const uint16_t* scales, const uint16_t* biases, const float* x,
+                float* out, int n_out, int n_in, int gs, int m, const float* row_add,
+                const float* residual, int flags, void* stream);
+
 /* hq4_gemv_fused with the activations and outputs in host memory, the
  * calling convention of q4_gemv itself (kernel/q4gemv.c:232: host x and out,
  * the call returns when out is written).  The weights stay on the device;

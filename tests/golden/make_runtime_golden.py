@@ -4,7 +4,9 @@ Writes the synthetic MLX-format snapshot of tests/golden/checkpoint_index.json
 (synth.write_snapshot) into a temporary directory, loads two stages from it
 with the reference's own build_stage and NumpyBackend (imported unmodified
 from the reference tree; its kernel is the reference's kernel/q4gemv.c built
-from source by oracle/Makefile), and runs frames through the reference's
+from source by oracle/Makefile, in its portable fp32 build -- the AVX2 build
+rounds x to int16 per call, ~5e-5 relative, which moves about one fp16
+wire element in twenty by an ulp), and runs frames through the reference's
 StageRunner.run_frame: stage A = layers [0, 2) with the embedding, stage B =
 layer [2, 3) with the head, for both wire codecs.  Two requests are
 interleaved: one prefilled in two chunks (the first without logits), one in a
@@ -50,13 +52,13 @@ def main():
     if len(sys.argv) > 1:
         os.environ["HETERO_REF_ROOT"] = sys.argv[1]
     from oracle import refmodel
-    refmodel.load_cpu_model("avx2")  # binds the reference kernel built from source
+    refmodel.load_cpu_model("float")  # binds the reference kernel built from source
     from hetero import backends, engine, shard
     from hetero_infer_b200 import synth
     cfg = synth.small_config(**CFG)
     out = {}
-    meta = {"cfg": CFG, "seed": SEED, "spec_a": SPEC_A, "spec_b": SPEC_B, "decode_steps": DECODE_STEPS,
-            "sampler": SAMPLER, "runs": {}}
+    meta = {"kernel": "kernel/q4gemv.c, portable fp32 build", "cfg": CFG, "seed": SEED, "spec_a": SPEC_A,
+            "spec_b": SPEC_B, "decode_steps": DECODE_STEPS, "sampler": SAMPLER, "runs": {}}
     with tempfile.TemporaryDirectory() as d:
         synth.write_snapshot(d, cfg, SEED, files=2, tied=False)
         be = backends.NumpyBackend()

@@ -189,3 +189,33 @@ def test_gemv_host_rejects_missing_buffers(cuda):
                              d.data_ptr(), d.data_ptr(), st) == -1
     assert lib.hq4_gemv_host(d.data_ptr(), d.data_ptr(), d.data_ptr(), None, h.data_ptr(), h.data_ptr(), 16, 64, 64,
                              0, d.data_ptr(), d.data_ptr(), st) == -1
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("n_out,n_in", [(3584, 3584), (512, 18944)])
+def test_gemv_ex_weights_written_by_the_preceding_kernel(cuda, oracle, n_out, n_in):
+    """hq4_gemv_ex with HQ4_GEMV_WEIGHTS_AFTER_WAIT: a copy kernel rewrites the
+    weight buffer immediately before each GEMV on the same stream, and every
+    product is that of the new weights (the option orders the weight reads
+    after the preceding kernel, which the default launch does not)."""
+    import torch
+    from hetero_infer_b200 import _lib
+    lib = _lib.load()
+    gs = 64
+    cases = [make_case(n_out, n_in, gs, seed=300 + i) for i in range(4)]
+    W, S, B = (to_dev(a).clone() for a in cases[0][:3])
+    st = torch.cuda.current_stream()
+    for i, (w, s, b, x) in enumerate(cases):
+        wd, sd, bd, xd = to_dev(w), to_dev(s), to_dev(b), to_dev(x)
+        y = torch.empty(1, n_out, device="cuda")
+        torch.cuda.synchronize()
+        W.copy_(wd)
+        S.copy_(sd)
+        B.copy_(bd)
+        rc = lib.hq4_gemv_ex(W.data_ptr(), S.data_ptr(), B.data_ptr(), xd.data_ptr(), y.data_ptr(), n_out, n_in,
+                             gs, 1, None, None, 1, st.cuda_stream)
+        assert rc == 0
+        ref = oracle.gemv_f32(w, s, b, x, gs)
+        assert rel_l2(y.cpu().numpy(), ref) <= OUR_TOL, f"case {i}"
+    assert lib.hq4_gemv_ex(W.data_ptr(), S.data_ptr(), B.data_ptr(), xd.data_ptr(), y.data_ptr(), n_out, n_in,
+                           gs, 1, None, None, 2, st.cuda_stream) == -1
