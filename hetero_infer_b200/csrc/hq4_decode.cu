@@ -69,7 +69,7 @@ struct DecSync {  // grid barrier words; all zero between launches
     unsigned int abort;
 };
 
-// Dynamic shared memory: [ring R x 36 KB][zero block 64 B][union][red 8 floats]
+// Dynamic shared memory: [ring R x 36 KB][zero block 64 B][union][red 16 floats]
 // [mbarriers: full R, empty R, desc_full 2, desc_empty 2].  The union holds a
 // GEMV phase's chunk images and strip slots, or attention's scratch.
 struct DecLayout {
@@ -78,7 +78,7 @@ struct DecLayout {
     __host__ __device__ size_t zero_off() const { return (size_t)ring * kStrStageBytes; }
     __host__ __device__ size_t uni_off() const { return zero_off() + 64; }
     __host__ __device__ size_t red_off() const { return uni_off() + (size_t)union_bytes; }
-    __host__ __device__ size_t bar_off() const { return red_off() + 8 * sizeof(float); }
+    __host__ __device__ size_t bar_off() const { return red_off() + kStrConsumers * sizeof(float); }
     __host__ __device__ size_t bytes() const { return bar_off() + (size_t)(2 * ring + 4) * 8 + 1024; }
 };
 
@@ -97,14 +97,6 @@ __device__ __forceinline__ unsigned int ld_relaxed_u32(const unsigned int* p) {
 }
 __device__ __forceinline__ void red_release_add_u64(unsigned long long* p, unsigned long long v) {
     asm volatile("red.release.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
-// AND of v over the 512 consumer threads (named barrier 1).
-__device__ __forceinline__ bool consumers_and(bool v) {
-    uint32_t r;
-    asm volatile(
-        "{\n .reg .pred p, q;\n setp.ne.u32 q, %1, 0;\n bar.red.and.pred p, 1, 512, q;\n selp.u32 %0, 1, 0, p;\n}\n"
-        : "=r"(r) : "r"((uint32_t)v) : "memory");
-    return r != 0;
 }
 
 // Failure-path test hook, set on the host per plan (hq4_decode_plan_fault):
@@ -350,7 +342,7 @@ decode_kernel(const DecPhase* __restrict__ phases, const CUtensorMap* __restrict
             float* partials = reinterpret_cast<float*>(uni + (size_t)kStrConsumers * nkb * kStrImgBytes);
             const int epi_pos = str_epi_prefetch(p, ns, s0, warp, lane);
             for (int i = threadIdx.x; i < kStrConsumers * ns_max * 16; i += kStrConsumers * kWarp) partials[i] = 0.0f;
-            str_prologue(p, red, img_w, nkb, nk, warp, lane);
+            str_prologue<3, 1>(p, red, img_w, nkb, nk, warp, lane);  // the kernel's register room
             str_epi_prefetch_late(p, ns, s0, warp, lane, epi_pos);
             asm volatile("bar.sync 1, 512;" ::: "memory");  // slots cleared before any warp adds into them
             StrAcc acc = {0.0f, 0.0f, 0.0f, 0.0f};

@@ -405,9 +405,16 @@ struct StreamLayout {
     __host__ __device__ size_t red_off() const {
         return part_off() + (size_t)kStrConsumers * ns_max * 16 * sizeof(float);
     }
-    __host__ __device__ size_t bar_off() const { return red_off() + 8 * sizeof(float); }
-    __host__ __device__ size_t bytes() const { return bar_off() + (size_t)2 * ring * 8 + 1024; }  // + alignment
+    __host__ __device__ size_t bar_off() const { return red_off() + kStrConsumers * sizeof(float); }
+    // full[ring], empty[ring], images built
+    __host__ __device__ size_t bytes() const { return bar_off() + (size_t)(2 * ring + 1) * 8 + 1024; }
 };
+
+// Stages a CTA requests before the dependency wait.  The rest of the ring
+// follows once the consumers have built their x images: the x loads then
+// meet fewer weight copies in flight (they wait behind them in the memory
+// system), which measured faster than filling the whole ring up front.
+constexpr int kStrEarlyStages = 3;
 
 
 __global__ void __launch_bounds__(kStrThreads, 1)
@@ -424,6 +431,7 @@ gemv_stream_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_consta
     const uint32_t bars = base_u + (uint32_t)L.bar_off();
     auto full_bar = [&](int s) { return bars + 8u * s; };
     auto empty_bar = [&](int s) { return bars + 8u * (R + s); };
+    const uint32_t images_bar = bars + 8u * (2 * R);  // every consumer warp's x images are built
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int s0 = (int)(blockIdx.x * (uint32_t)p.n_strips / gridDim.x);
@@ -469,10 +477,11 @@ gemv_stream_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_consta
             mbar_init_nofence(full_bar(s), 1);
             mbar_init_nofence(empty_bar(s), kStrConsumers);
         }
+        mbar_init_nofence(images_bar, kStrConsumers);
         mbar_init_fence();
         pol = l2_policy_evict_first();  // weights are read once
         if (p.weights_after_wait) pdl_wait();
-        const int first = min(R, n_stages);
+        const int first = min(min(R, kStrEarlyStages), n_stages);
         for (int i = 0; i < first; i++) issue_stage();
     }
     if (threadIdx.x < 4) reinterpret_cast<uint4*>(base + L.zero_off())[threadIdx.x] = make_uint4(0, 0, 0, 0);
@@ -483,8 +492,11 @@ gemv_stream_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_consta
     if (warp == kStrConsumers) {
         if (producer) {
             bool ok = true;
-            if (n_stages > R) pdl_wait();  // the waits below depend on the consumers
-            while (p_issued < n_stages) {
+            if (p_issued < n_stages) {
+                pdl_wait();  // the waits below depend on the consumers
+                ok = mbar_wait_nap(images_bar, 0, kStrWaitNs, 64);
+            }
+            while (ok && p_issued < n_stages) {
                 if (!mbar_wait_nap(empty_bar(p_slot), (p_use - 1) & 1, kStrWaitNs, 64)) {
                     ok = false;
                     break;
@@ -506,7 +518,8 @@ gemv_stream_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_consta
     // this warp's chunk images, one per k-block, built up front: the builds
     // overlap the ring filling, and the stage loop is tiles only
     unsigned char* img_w = base + L.img_off() + (size_t)warp * L.nkb * kStrImgBytes;
-    str_prologue(p, red, img_w, nkb, nk, warp, lane);
+    str_prologue<5, 2>(p, red, img_w, nkb, nk, warp, lane);
+    if (lane == 0) mbar_arrive(images_bar);
     str_epi_prefetch_late(p, ns, s0, warp, lane, epi_pos);
     bool ok = true;
     int slot = 0;

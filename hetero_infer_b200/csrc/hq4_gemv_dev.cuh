@@ -166,48 +166,26 @@ constexpr int kStrWBytes = kStrKc * kStrTileBytes;         // 32 KB
 constexpr int kStrSBCols = kStrKc * 4;                     // scale groups per stage at gs 64
 constexpr int kStrSBBytes = 16 * kStrSBCols * 2;           // 16 rows x up to 64 scale groups
 constexpr int kStrStageBytes = kStrWBytes + 2 * kStrSBBytes;  // 36 KB (a multiple of 1024)
-constexpr int kStrNormThreads = 256;                       // sum of squares as the kernel above
 constexpr int kStrImgBytes = 4 * M1<64>::kImgStride;       // one k-chunk: 4 lane-groups
 constexpr uint64_t kStrWaitNs = 1000000000ull;             // bounded waits: 1 s
 constexpr uint32_t kStrTryHintNs = 10000;                  // consumer waits: 10 us per try_wait,
 constexpr int kStrTries = 100000;                          // at most 1 s in all
+
+// AND of v over the 512 consumer threads (named barrier 1; every consumer
+// thread must arrive).
+__device__ __forceinline__ bool consumers_and(bool v) {
+    uint32_t r;
+    asm volatile(
+        "{\n .reg .pred p, q;\n setp.ne.u32 q, %1, 0;\n bar.red.and.pred p, 1, 512, q;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(r) : "r"((uint32_t)v) : "memory");
+    return r != 0;
+}
 
 __device__ __forceinline__ uint4 lds128(const unsigned char* p) {
     return *reinterpret_cast<const uint4*>(p);
 }
 
 // ---- streaming consumer steps (512 consumer threads, warps 0-15) ----------
-
-// RMSNorm factor 1/sqrt(mean(x^2)+eps): thread i < 256 sums x[i], x[i+256],
-// ...; then the warp's xor tree; then the 8 warp sums in order.  Uses named
-// barrier 1 over the 512 consumer threads.
-constexpr int kNormBatch = 4;
-__device__ __forceinline__ float str_norm_factor(const GemvM1Params& p, float* red, int warp, int lane) {
-    float ss = 0.0f;
-    if (threadIdx.x < kStrNormThreads) {
-        // kNormBatch loads in flight per batch, summed in index order
-        for (int i0 = threadIdx.x; i0 < p.n_in; i0 += kStrNormThreads * kNormBatch) {
-            float v[kNormBatch];
-#pragma unroll
-            for (int k = 0; k < kNormBatch; k++) {
-                const int i = i0 + k * kStrNormThreads;
-                v[k] = i < p.n_in ? p.x[i] : 0.0f;
-            }
-#pragma unroll
-            for (int k = 0; k < kNormBatch; k++)
-                if (i0 + k * kStrNormThreads < p.n_in) ss = fmaf(v[k], v[k], ss);
-        }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    if (lane == 0 && threadIdx.x < kStrNormThreads) red[warp] = ss;
-    asm volatile("bar.sync 1, 512;" ::: "memory");
-    float tot = 0.0f;
-#pragma unroll
-    for (int i = 0; i < kStrNormThreads / kWarp; i++) tot += red[i];
-    const float mean = __fdiv_rn(tot, (float)p.n_in);
-    return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, p.eps)));
-}
 
 // Lane (bq = lane/8, bp = lane%8) holds values [8 bp, 8 bp + 8) of lane-group
 // bq of a k-chunk.  x of chunk kc (zeros past the row end).
@@ -289,37 +267,76 @@ __device__ __forceinline__ void str_build_chunk(const GemvM1Params& p, unsigned 
     if (bp == 0) *reinterpret_cast<float2*>(gb + C::kMetaOff) = make_float2(exp2i(E - kXBits), s);
 }
 
-// The GEMV prologue of a warp: the RMSNorm factor when p.norm_w is set
-// (named barrier 1 over the 512 consumer threads) and this warp's chunk
-// images (k-chunk kb*16 + warp for kb < nkb).  The global loads are issued
-// ahead of their use so that their latencies overlap: without the norm, the x
-// of up to kB chunks at once; with it, the first chunk's x and norm weights
-// together with the norm factor's loads (rows with one k-block, as every
-// hidden-size row of the 7B shape; longer rows load chunk by chunk).
+// RMSNorm factor 1/sqrt(mean(x^2)+eps) from the per-warp sums of squares:
+// the 16 consumer warps' sums, parked in red[], added in warp order.  Uses
+// named barrier 1 over the 512 consumer threads.
+__device__ __forceinline__ float str_norm_combine(const GemvM1Params& p, float* red, float ss, int warp, int lane) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if (lane == 0) red[warp] = ss;
+    asm volatile("bar.sync 1, 512;" ::: "memory");
+    float tot = 0.0f;
+#pragma unroll
+    for (int i = 0; i < kStrConsumers; i++) tot += red[i];
+    const float mean = __fdiv_rn(tot, (float)p.n_in);
+    return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, p.eps)));
+}
+
+// The GEMV prologue of a warp: its chunk images (k-chunk kb*16 + warp for
+// kb < nkb) and, when p.norm_w is set, the RMSNorm of x applied first.  The
+// x values a warp converts are the ones it sums for the norm, so the whole
+// prologue costs one round trip to memory: every chunk's x (and norm
+// weights) is requested before the first is used.  Sum of squares: each
+// lane's 8 values per chunk in chunk order, the warp's xor tree, the warps
+// in order (str_norm_combine).  Rows longer than the chunks a pass holds in
+// registers (kProKb without the norm, kProKbNorm with it; a kernel with less
+// register room takes smaller passes, the arithmetic is the same) take
+// further passes.
+template <int kProKb, int kProKbNorm>
 __device__ __forceinline__ void str_prologue(const GemvM1Params& p, float* red, unsigned char* img_w, int nkb,
                                              int nk, int warp, int lane) {
     if (p.norm_w) {
-        float xr[8], nw[8];
-        str_load_x(p, warp, nk, lane, xr);
-        str_load_nw(p, warp, nk, lane, nw);
-        const float norm_r = str_norm_factor(p, red, warp, lane);
-        for (int kb = 0; kb < nkb; kb++) {
-            const int kc = kb * kStrKc + warp;
-            if (kb > 0) {
-                str_load_x(p, kc, nk, lane, xr);
-                str_load_nw(p, kc, nk, lane, nw);
+        constexpr int U = kProKbNorm;
+        float xr[U][8], nw[U][8];
+        float ss = 0.0f;
+        for (int kb0 = 0; kb0 < nkb; kb0 += U) {
+#pragma unroll
+            for (int u = 0; u < U; u++)
+                if (kb0 + u < nkb) {
+                    str_load_x(p, (kb0 + u) * kStrKc + warp, nk, lane, xr[u]);
+                    str_load_nw(p, (kb0 + u) * kStrKc + warp, nk, lane, nw[u]);
+                }
+#pragma unroll
+            for (int u = 0; u < U; u++)
+                if (kb0 + u < nkb)
+#pragma unroll
+                    for (int i = 0; i < 8; i++) ss = fmaf(xr[u][i], xr[u][i], ss);
+        }
+        const float norm_r = str_norm_combine(p, red, ss, warp, lane);
+        for (int kb0 = 0; kb0 < nkb; kb0 += U) {
+            if (nkb > U) {  // the registers hold the last pass: reload this one
+#pragma unroll
+                for (int u = 0; u < U; u++)
+                    if (kb0 + u < nkb) {
+                        str_load_x(p, (kb0 + u) * kStrKc + warp, nk, lane, xr[u]);
+                        str_load_nw(p, (kb0 + u) * kStrKc + warp, nk, lane, nw[u]);
+                    }
             }
-            if (kc < nk) str_build_chunk(p, img_w, kb, kc, lane, xr, nw, true, norm_r);
+#pragma unroll
+            for (int u = 0; u < U; u++) {
+                const int kc = (kb0 + u) * kStrKc + warp;
+                if (kb0 + u < nkb && kc < nk) str_build_chunk(p, img_w, kb0 + u, kc, lane, xr[u], nw[u], true, norm_r);
+            }
         }
     } else {
-        constexpr int kB = 3;
-        for (int kb0 = 0; kb0 < nkb; kb0 += kB) {
-            float xr[kB][8];
+        constexpr int U = kProKb;
+        for (int kb0 = 0; kb0 < nkb; kb0 += U) {
+            float xr[U][8];
 #pragma unroll
-            for (int u = 0; u < kB; u++)
+            for (int u = 0; u < U; u++)
                 if (kb0 + u < nkb) str_load_x(p, (kb0 + u) * kStrKc + warp, nk, lane, xr[u]);
 #pragma unroll
-            for (int u = 0; u < kB; u++) {
+            for (int u = 0; u < U; u++) {
                 const int kc = (kb0 + u) * kStrKc + warp;
                 if (kb0 + u < nkb && kc < nk) str_build_chunk(p, img_w, kb0 + u, kc, lane, xr[u], xr[u], false, 1.0f);
             }
@@ -333,6 +350,88 @@ struct StrAcc {
     float r00, r01, r10, r11;
 };
 
+// Per-lane constants of the stage arithmetic (lane g = lane/4 owns rows g and
+// g+8 of a tile, t = lane%4 its lane-group): which digit blocks of the x
+// image feed its B registers, and where its scale and bias sit in a stage's
+// swizzled scale/bias tiles.
+struct StrLane {
+    int g, t, role, off0, sbo0, sbo1;
+};
+
+__device__ __forceinline__ StrLane str_lane(const GemvM1Params& p, int warp, int lane) {
+    StrLane L;
+    L.g = lane >> 2;
+    L.t = lane & 3;
+    L.role = (L.g >> 1) == L.t ? (L.g & 1) + 1 : 0;  // 1: d2+d0, 2: d1, 0: none
+    L.off0 = L.role == 1 ? 0 : 64;
+    // scale/bias tiles carry the swizzle of their row width (128, 64 or 32 B)
+    const int sb_cols = kStrSBCols >> p.sg_shift;
+    const int sb_row = sb_cols * 2;
+    const int sb_mask = (sb_row >> 4) - 1;  // 16-byte units per row - 1: 128 B: 7, 64 B: 3, 32 B: 1
+    const int lg = (warp * 4 + L.t) >> p.sg_shift;  // scale group inside the stage
+    auto sb_off = [&](int row) {
+        const int o = row * sb_row + lg * 2;
+        return o ^ (((o >> 7) & sb_mask) << 4);
+    };
+    L.sbo0 = sb_off(L.g);
+    L.sbo1 = sb_off(L.g + 8);
+    return L;
+}
+
+// One stage's tile for this warp (k-chunk `warp` of the stage, image `img`
+// of that chunk): the lane's shares of rows g and g+8, zero when its
+// lane-group lies past the row end (gok false).  Exact digit dots on the
+// integer tensor cores, then scale * dot * 2^(E-22) + bias * xsum in fp32.
+__device__ __forceinline__ void str_tile(const StrLane& L, const unsigned char* st, const unsigned char* img,
+                                         const unsigned char* zero_blk, bool gok, int warp, float& a0f,
+                                         float& a1f) {
+    using C = M1<64>;
+    const int g = L.g, t = L.t;
+    const unsigned char* gb = img + t * C::kImgStride;
+    const uint4* src0 = reinterpret_cast<const uint4*>(L.role ? gb + L.off0 : zero_blk);
+    const uint4* src1 = reinterpret_cast<const uint4*>(L.role == 1 ? gb + 128 : zero_blk);
+    const float2 meta = *reinterpret_cast<const float2*>(gb + C::kMetaOff);
+    const unsigned char* wt = st + warp * kStrTileBytes;
+    // rows g and g+8; 16-byte chunks 2t and 2t+1 of the row, swizzled
+    const int c0 = ((2 * t) ^ g) << 4, c1 = ((2 * t + 1) ^ g) << 4;
+    const uint4 ra = lds128(wt + g * 128 + c0), rb = lds128(wt + g * 128 + c1);
+    const uint4 rc = lds128(wt + (g + 8) * 128 + c0), rd = lds128(wt + (g + 8) * 128 + c1);
+    const uint32_t w0[8] = {ra.x, ra.y, ra.z, ra.w, rb.x, rb.y, rb.z, rb.w};
+    const uint32_t w1[8] = {rc.x, rc.y, rc.z, rc.w, rd.x, rd.y, rd.z, rd.w};
+    int c0e[4] = {0, 0, 0, 0}, c0o[4] = {0, 0, 0, 0}, c1e[4] = {0, 0, 0, 0}, c1o[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int ks = 0; ks < C::kKSteps; ks += 2) {
+        const uint4 q0 = src0[ks >> 1], q1 = src1[ks >> 1];
+        uint32_t a0, a1, a2, a3;
+        unpack_u8(w0[ks], a0, a2);
+        unpack_u8(w1[ks], a1, a3);
+        mma_u8s8_16832(c0e, a0, a1, a2, a3, q0.x, q0.y);
+        mma_u8s8_16832(c1e, a0, a1, a2, a3, q1.x, q1.y);
+        unpack_u8(w0[ks + 1], a0, a2);
+        unpack_u8(w1[ks + 1], a1, a3);
+        mma_u8s8_16832(c0o, a0, a1, a2, a3, q0.z, q0.w);
+        mma_u8s8_16832(c1o, a0, a1, a2, a3, q1.z, q1.w);
+    }
+    const unsigned char* ss = st + kStrWBytes;
+    const unsigned char* sbi = st + kStrWBytes + kStrSBBytes;
+    a0f = 0.0f;
+    a1f = 0.0f;
+    if (gok) {
+        const float dot0 = fmaf((float)(c0e[0] + c0o[0]), 65536.0f,
+                                fmaf((float)(c0e[1] + c0o[1]), 256.0f, (float)(c1e[0] + c1o[0])));
+        const float dot1 = fmaf((float)(c0e[2] + c0o[2]), 65536.0f,
+                                fmaf((float)(c0e[3] + c0o[3]), 256.0f, (float)(c1e[2] + c1o[2])));
+        const float s0 = h2f(*reinterpret_cast<const uint16_t*>(ss + L.sbo0));
+        const float b0 = h2f(*reinterpret_cast<const uint16_t*>(sbi + L.sbo0));
+        const float s1 = h2f(*reinterpret_cast<const uint16_t*>(ss + L.sbo1));
+        const float b1 = h2f(*reinterpret_cast<const uint16_t*>(sbi + L.sbo1));
+        a0f = fmaf(s0 * meta.x, dot0, 0.0f);
+        a0f = fmaf(b0, meta.y, a0f);
+        a1f = fmaf(s1 * meta.x, dot1, 0.0f);
+        a1f = fmaf(b1, meta.y, a1f);
+    }
+}
+
 // The stage loop of one GEMV: ns strips x nkb k-blocks through the ring
 // (stages k-block-major, strip-minor), starting at ring position (slot,
 // phase), which it advances.  `stages` is the ring's first stage, `full` /
@@ -343,74 +442,21 @@ __device__ __forceinline__ void str_consume(const GemvM1Params& p, const unsigne
                                             int nkb, int nk, const unsigned char* img_w,
                                             const unsigned char* zero_blk, float* partials, int ns_max, int warp,
                                             int lane, StrAcc& acc) {
-    using C = M1<64>;
-    const int g = lane >> 2, t = lane & 3;
-    const int role = (g >> 1) == t ? (g & 1) + 1 : 0;  // 1: d2+d0, 2: d1, 0: none
-    const int off0 = role == 1 ? 0 : 64;
+    const StrLane L = str_lane(p, warp, lane);
+    const int g = L.g, t = L.t;
     // CTAs with one or two strips keep each strip's lane sums in registers
     // across k-blocks; more strips go through the shared-memory slots per stage
     const bool regacc = ns <= 2;
-    // scale/bias tiles carry the swizzle of their row width (128, 64 or 32 B)
-    const int sb_cols = kStrSBCols >> p.sg_shift;
-    const int sb_row = sb_cols * 2;
-    const int sb_mask = (sb_row >> 4) - 1;  // 16-byte units per row - 1: 128 B: 7, 64 B: 3, 32 B: 1
-    const int lg = (warp * 4 + t) >> p.sg_shift;  // scale group inside the stage
-    auto sb_off = [&](int row) {
-        const int o = row * sb_row + lg * 2;
-        return o ^ (((o >> 7) & sb_mask) << 4);
-    };
-    const int sbo0 = sb_off(g), sbo1 = sb_off(g + 8);
     for (int kb = 0; kb < nkb; kb++) {
         const int kc = kb * kStrKc + warp;
         const bool active = kc < nk;
         const unsigned char* img = img_w + (size_t)kb * kStrImgBytes;
         const bool gok = kc * 4 + t < p.ng;
-        const unsigned char* gb = img + t * C::kImgStride;
-        const uint4* src0 = reinterpret_cast<const uint4*>(role ? gb + off0 : zero_blk);
-        const uint4* src1 = reinterpret_cast<const uint4*>(role == 1 ? gb + 128 : zero_blk);
-        const float2 meta = *reinterpret_cast<const float2*>(gb + C::kMetaOff);
         for (int j = 0; j < ns; j++) {
             if (ok && !mbar_wait_tries(full + 8u * slot, phase, kStrTryHintNs, kStrTries)) ok = false;
             if (ok && active) {
-                const unsigned char* st = stages + (size_t)slot * kStrStageBytes;
-                const unsigned char* wt = st + warp * kStrTileBytes;
-                // rows g and g+8; 16-byte chunks 2t and 2t+1 of the row, swizzled
-                const int c0 = ((2 * t) ^ g) << 4, c1 = ((2 * t + 1) ^ g) << 4;
-                const uint4 ra = lds128(wt + g * 128 + c0), rb = lds128(wt + g * 128 + c1);
-                const uint4 rc = lds128(wt + (g + 8) * 128 + c0), rd = lds128(wt + (g + 8) * 128 + c1);
-                const uint32_t w0[8] = {ra.x, ra.y, ra.z, ra.w, rb.x, rb.y, rb.z, rb.w};
-                const uint32_t w1[8] = {rc.x, rc.y, rc.z, rc.w, rd.x, rd.y, rd.z, rd.w};
-                int c0e[4] = {0, 0, 0, 0}, c0o[4] = {0, 0, 0, 0}, c1e[4] = {0, 0, 0, 0}, c1o[4] = {0, 0, 0, 0};
-#pragma unroll
-                for (int ks = 0; ks < C::kKSteps; ks += 2) {
-                    const uint4 q0 = src0[ks >> 1], q1 = src1[ks >> 1];
-                    uint32_t a0, a1, a2, a3;
-                    unpack_u8(w0[ks], a0, a2);
-                    unpack_u8(w1[ks], a1, a3);
-                    mma_u8s8_16832(c0e, a0, a1, a2, a3, q0.x, q0.y);
-                    mma_u8s8_16832(c1e, a0, a1, a2, a3, q1.x, q1.y);
-                    unpack_u8(w0[ks + 1], a0, a2);
-                    unpack_u8(w1[ks + 1], a1, a3);
-                    mma_u8s8_16832(c0o, a0, a1, a2, a3, q0.z, q0.w);
-                    mma_u8s8_16832(c1o, a0, a1, a2, a3, q1.z, q1.w);
-                }
-                const unsigned char* ss = st + kStrWBytes;
-                const unsigned char* sbi = st + kStrWBytes + kStrSBBytes;
-                float a0f = 0.0f, a1f = 0.0f;
-                if (gok) {
-                    const float dot0 = fmaf((float)(c0e[0] + c0o[0]), 65536.0f,
-                                            fmaf((float)(c0e[1] + c0o[1]), 256.0f, (float)(c1e[0] + c1o[0])));
-                    const float dot1 = fmaf((float)(c0e[2] + c0o[2]), 65536.0f,
-                                            fmaf((float)(c0e[3] + c0o[3]), 256.0f, (float)(c1e[2] + c1o[2])));
-                    const float s0 = h2f(*reinterpret_cast<const uint16_t*>(ss + sbo0));
-                    const float b0 = h2f(*reinterpret_cast<const uint16_t*>(sbi + sbo0));
-                    const float s1 = h2f(*reinterpret_cast<const uint16_t*>(ss + sbo1));
-                    const float b1 = h2f(*reinterpret_cast<const uint16_t*>(sbi + sbo1));
-                    a0f = fmaf(s0 * meta.x, dot0, 0.0f);
-                    a0f = fmaf(b0, meta.y, a0f);
-                    a1f = fmaf(s1 * meta.x, dot1, 0.0f);
-                    a1f = fmaf(b1, meta.y, a1f);
-                }
+                float a0f, a1f;
+                str_tile(L, stages + (size_t)slot * kStrStageBytes, img, zero_blk, gok, warp, a0f, a1f);
                 if (regacc) {
                     if (j == 0) {
                         acc.r00 += a0f;

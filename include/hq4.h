@@ -65,14 +65,14 @@ int hq4_gemv_fused(const uint32_t* w, const uint16_t* scales, const uint16_t* bi
                    const float* x, float* out, int n_out, int n_in, int gs, int m,
                    const float* row_add, const float* residual, void* stream);
 
-/* hq4_gemv_fused with launch options.  hq4_gemv and hq4_gemv_fused start
+/* hq4_gemv_fused with launch options.  No reference counterpart (the
+ * reference's q4_gemv is synchronous).  hq4_gemv and hq4_gemv_fused start
  * streaming the weights before waiting for the preceding kernel on the
  * stream (programmatic dependent launch): only x, the residual and the
  * outputs are ordered after it.  A caller whose weights were written by the
  * kernel immediately before (a repack, a dequantise-requantise, an upload
  * kernel) passes HQ4_GEMV_WEIGHTS_AFTER_WAIT, and the weights are then read
- * only after that kernel has completed.  Unknown flag bits: -1.  No reference
- * counterpart (the reference's q4_gemv is synchronous). */
+ * only after that kernel has completed.  Unknown flag bits: -1. */
 #define HQ4_GEMV_WEIGHTS_AFTER_WAIT 1
 int hq4_gemv_ex(const uint32_t* w, const uint16_t* scales, const uint16_t* biases, const float* x,
                 float* out, int n_out, int n_in, int gs, int m, const float* row_add,

@@ -34,6 +34,14 @@ def _ref_decode(header, payload):
     return codec.decode_i8(payload, shape).astype(np.float32)
 
 
+def _f16_ulps(a, b):
+    """Distance in fp16 units in the last place between two fp16 arrays."""
+    def key(x):
+        i = np.asarray(x, np.float16).view(np.int16).astype(np.int32)
+        return np.where(i < 0, -(i & 0x7FFF), i)
+    return np.abs(key(a) - key(b))
+
+
 def _stages(tmp_path, meta, codec, sampler=None):
     from hetero_infer_b200 import cuda_model, planner, runtime
     cfg = synth.small_config(**meta["cfg"])
@@ -63,7 +71,12 @@ def test_stage_runner_frames_match_reference(cuda, tmp_path, codec):
         assert len(pa) == len(ref_p)
         ours, ref = _ref_decode(ha, pa), _ref_decode(ev["a_out"], ref_p)
         if codec == "fp16":
-            np.testing.assert_allclose(ours, ref, rtol=2.0 ** -10, atol=1e-6, err_msg=f"frame {i}")
+            # the same fp32 state up to summation order: at most one fp16 ulp
+            # apart, or (near zero, where cancellation leaves fp32 sums a few
+            # 1e-7 of the row's scale apart) within 1e-5 of the row's largest value
+            near = np.abs(ours - ref) <= 1e-5 * np.abs(ref).max(axis=-1, keepdims=True)
+            assert np.all((_f16_ulps(ours, ref) <= 1) | near), f"frame {i}"
+            assert np.mean(ours != ref) < 0.03, f"frame {i}"  # ~1% of elements sit on a rounding edge
         else:
             step = np.abs(ref).max(axis=-1, keepdims=True) / 127.0
             assert np.all(np.abs(ours - ref) <= 1.01 * step + 1e-6), f"frame {i}"
