@@ -42,6 +42,7 @@ SIGNATURES = {
     "hq4_act_decode_i8": (_I, [_P, _I, _I, _P, _P, _P]),
     "hq4_act_encode_i8_wire": (_I, [_P, _I, _I, _P, _P]),
     "hq4_argmax": (_I, [_P, _I, _P, _P, _I, _P, _P, _P]),
+    "hq4_sample": (_I, [_P, _I, _F, _F, ctypes.c_double, _P, _P]),
     "hq4_synth_embed_f16": (_I, [ctypes.c_longlong, _I, _I, _F, _P, _P]),
     "hq4_argmax_pair": (_I, [_P, _I, _I, _P, _P]),
     "hq4_pick_token": (_I, [_P, _I, _P, _P, _I, _P]),

@@ -927,10 +927,22 @@ extern "C" int hq4_gemv_host(const uint32_t* w, const uint16_t* scales, const ui
     if (m <= 0 || n_out <= 0 || n_in <= 0 || !x_host || !out_host || !x_dev || !out_dev) return HQ4_ERR_SHAPE;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     const size_t in_bytes = (size_t)m * n_in * sizeof(float), out_bytes = (size_t)m * n_out * sizeof(float);
+    // Pinned, device-mapped host output: the GEMV's epilogue stores straight
+    // into it (the products cross the bus once, from the kernel), which saves
+    // the separate device-to-host copy and its latency.  Other host memory
+    // takes the copy.
+    float* out_direct = nullptr;
+    cudaPointerAttributes pa;
+    if (cudaPointerGetAttributes(&pa, out_host) == cudaSuccess && pa.type == cudaMemoryTypeHost && pa.devicePointer &&
+        ((uintptr_t)pa.devicePointer & 3) == 0)
+        out_direct = static_cast<float*>(pa.devicePointer);
+    else
+        (void)cudaGetLastError();  // an unregistered pointer is not an error here
     if (cudaMemcpyAsync(x_dev, x_host, in_bytes, cudaMemcpyHostToDevice, st) != cudaSuccess) return HQ4_ERR_LAUNCH;
-    if (int rc = hq4_gemv_fused(w, scales, biases, x_dev, out_dev, n_out, n_in, gs, m, row_add, nullptr, stream))
+    if (int rc = hq4_gemv_fused(w, scales, biases, x_dev, out_direct ? out_direct : out_dev, n_out, n_in, gs, m,
+                                row_add, nullptr, stream))
         return rc;
-    if (cudaMemcpyAsync(out_host, out_dev, out_bytes, cudaMemcpyDeviceToHost, st) != cudaSuccess)
+    if (!out_direct && cudaMemcpyAsync(out_host, out_dev, out_bytes, cudaMemcpyDeviceToHost, st) != cudaSuccess)
         return HQ4_ERR_LAUNCH;
     return cudaStreamSynchronize(st) == cudaSuccess ? HQ4_OK : HQ4_ERR_LAUNCH;
 }

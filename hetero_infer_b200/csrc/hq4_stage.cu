@@ -423,6 +423,209 @@ extern "C" int hq4_attention(const float* q, const float* k_cache, const float* 
                       head_dim, max_ctx, pos, scale);
 }
 
+// ---- temperature / top-p sampling -----------------------------------------
+// NumpyBackend.sample (hetero/backends.py:110-120) for temperature > 0, on a
+// cluster of 8 CTAs that splits the vocabulary in contiguous slices held in
+// shared memory: z = x / T; z -= max; p = exp(z) / sum; with top_p < 1 the
+// nucleus -- the elements whose strictly larger elements hold less than
+// top_p of the mass -- renormalised; then the draw of rng.choice for the
+// caller's uniform variate u: the first index whose cumulative probability,
+// divided by the total, exceeds u.  Every reduction runs in a fixed order and
+// every CTA combines the 8 slice totals in rank order, so all CTAs agree.
+// The nucleus bound is found by bisection on the bit patterns of the
+// probabilities (non-negative floats order as their bits).  Sums differ from
+// NumPy's only in rounding order; an exact tie in probability at the nucleus
+// edge keeps every tied element (NumPy's unstable argsort keeps some).
+constexpr int kSampleThreads = 1024;
+constexpr int kSampleCluster = 8;
+
+struct SampleShared {
+    float red[kSampleThreads / 32];
+    float cl[2];  // this CTA's slice total, double-buffered between reductions
+    int icl[2];
+    float bcast;
+    int ibcast;
+};
+
+// Sum over the cluster of every thread's v: warp trees, the 32 warp sums in
+// order, the 8 CTA sums in rank order.  `k` alternates the exchange buffer.
+__device__ __forceinline__ float sample_cluster_sum(SampleShared& sh, float v, int& k) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if ((threadIdx.x & 31) == 0) sh.red[threadIdx.x >> 5] = v;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float b = 0.0f;
+        for (int w = 0; w < kSampleThreads / 32; w++) b += sh.red[w];
+        sh.cl[k] = b;
+    }
+    cluster_sync();
+    if (threadIdx.x == 0) {
+        float t = 0.0f;
+        for (int r = 0; r < kSampleCluster; r++) {
+            float x;
+            asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(x) : "r"(map_to_rank(smem_u32(&sh.cl[k]), r))
+                         : "memory");
+            t += x;
+        }
+        sh.bcast = t;
+    }
+    __syncthreads();
+    k ^= 1;
+    return sh.bcast;
+}
+__device__ __forceinline__ float sample_cluster_max(SampleShared& sh, float v, int& k) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    if ((threadIdx.x & 31) == 0) sh.red[threadIdx.x >> 5] = v;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float b = sh.red[0];
+        for (int w = 1; w < kSampleThreads / 32; w++) b = fmaxf(b, sh.red[w]);
+        sh.cl[k] = b;
+    }
+    cluster_sync();
+    if (threadIdx.x == 0) {
+        float t = -INFINITY;
+        for (int r = 0; r < kSampleCluster; r++) {
+            float x;
+            asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(x) : "r"(map_to_rank(smem_u32(&sh.cl[k]), r))
+                         : "memory");
+            t = fmaxf(t, x);
+        }
+        sh.bcast = t;
+    }
+    __syncthreads();
+    k ^= 1;
+    return sh.bcast;
+}
+__device__ __forceinline__ int sample_cluster_min(SampleShared& sh, int v, int& k) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = min(v, __shfl_xor_sync(0xffffffffu, v, o));
+    if ((threadIdx.x & 31) == 0) sh.red[threadIdx.x >> 5] = __int_as_float(v);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int b = __float_as_int(sh.red[0]);
+        for (int w = 1; w < kSampleThreads / 32; w++) b = min(b, __float_as_int(sh.red[w]));
+        sh.icl[k] = b;
+    }
+    cluster_sync();
+    if (threadIdx.x == 0) {
+        int t = 0x7fffffff;
+        for (int r = 0; r < kSampleCluster; r++) {
+            int x;
+            asm volatile("ld.shared::cluster.b32 %0, [%1];" : "=r"(x) : "r"(map_to_rank(smem_u32(&sh.icl[k]), r))
+                         : "memory");
+            t = min(t, x);
+        }
+        sh.ibcast = t;
+    }
+    __syncthreads();
+    k ^= 1;
+    return sh.ibcast;
+}
+
+__global__ void __launch_bounds__(kSampleThreads) sample_cluster_kernel(const float* __restrict__ x, int n, float temp,
+                                                                       float top_p, double u, int* __restrict__ tok,
+                                                                       int* status) {
+    extern __shared__ float ps[];  // this CTA's slice of the distribution
+    __shared__ SampleShared sh;
+    pdl_launch_dependents();
+    pdl_wait();
+    const int rank = (int)cluster_ctarank();
+    const int chunk = (n + kSampleCluster - 1) / kSampleCluster;
+    const int lo = min(n, rank * chunk), cnt = min(n, lo + chunk) - lo;
+    // thread t owns the contiguous run [t*E, t*E + E) of the slice
+    const int E = (chunk + kSampleThreads - 1) / kSampleThreads;
+    const int a = min(cnt, (int)threadIdx.x * E), b = min(cnt, a + E);
+    int k = 0;
+    float mx = -INFINITY;
+    for (int i = a; i < b; i++) {
+        const float z = __fdiv_rn(x[lo + i], temp);  // z = logits / temperature
+        ps[i] = z;
+        mx = fmaxf(mx, z);
+    }
+    mx = sample_cluster_max(sh, mx, k);
+    float s = 0.0f;
+    for (int i = a; i < b; i++) {
+        const float e = expf(__fsub_rn(ps[i], mx));  // z -= z.max(); p = exp(z)
+        ps[i] = e;
+        s += e;
+    }
+    const float tot = sample_cluster_sum(sh, s, k);
+    for (int i = a; i < b; i++) ps[i] = __fdiv_rn(ps[i], tot);  // p /= p.sum()
+    if (top_p < 1.0f) {
+        // smallest bit pattern c whose strictly larger probabilities hold less
+        // than top_p: the nucleus is every p with bits >= c
+        unsigned int lo_c = 0u, hi_c = 0x3F800001u;  // mass above hi_c (> 1.0f) is zero
+        while (hi_c - lo_c > 1u) {
+            const unsigned int mid = lo_c + ((hi_c - lo_c) >> 1);
+            float m = 0.0f;
+            for (int i = a; i < b; i++)
+                if (__float_as_uint(ps[i]) > mid) m += ps[i];
+            if (sample_cluster_sum(sh, m, k) < top_p) hi_c = mid;
+            else lo_c = mid;
+        }
+        float m = 0.0f;
+        for (int i = a; i < b; i++) {
+            const float v = __float_as_uint(ps[i]) >= hi_c ? ps[i] : 0.0f;
+            ps[i] = v;
+            m += v;
+        }
+        const float kept = sample_cluster_sum(sh, m, k);
+        for (int i = a; i < b; i++) ps[i] = __fdiv_rn(ps[i], kept);  // p = masked / masked.sum()
+    }
+    // the draw: cumulative probability in index order -- the thread's run in
+    // order, after the runs before it (the CTA's threads, then the slices of
+    // lower ranks) -- over its total, the first entry above u
+    float run = 0.0f;
+    for (int i = a; i < b; i++) run += ps[i];
+    // exclusive prefix of the runs: warp scan, then the warps, then the CTAs
+    float inc = run;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const float y = __shfl_up_sync(0xffffffffu, inc, o);
+        if ((threadIdx.x & 31) >= o) inc += y;
+    }
+    if ((threadIdx.x & 31) == 31) sh.red[threadIdx.x >> 5] = inc;
+    __syncthreads();
+    float before = inc - run;
+    for (int w = 0; w < (int)(threadIdx.x >> 5); w++) before += sh.red[w];
+    float cta_total = 0.0f;
+    for (int w = 0; w < kSampleThreads / 32; w++) cta_total += sh.red[w];
+    __syncthreads();
+    if (threadIdx.x == 0) sh.cl[k] = cta_total;
+    cluster_sync();
+    float grand = 0.0f, lower = 0.0f;
+    for (int r = 0; r < kSampleCluster; r++) {
+        float y;
+        asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(y) : "r"(map_to_rank(smem_u32(&sh.cl[k]), r))
+                     : "memory");
+        if (r < rank) lower += y;
+        grand += y;
+    }
+    k ^= 1;
+    int pick = 0x7fffffff;
+    float c = lower + before;
+    for (int i = a; i < b; i++) {
+        c += ps[i];
+        if ((double)__fdiv_rn(c, grand) > u) {
+            pick = lo + i;
+            break;
+        }
+    }
+    pick = sample_cluster_min(sh, pick, k);
+    if (rank == 0 && threadIdx.x == 0) {
+        if (pick == 0x7fffffff || !(grand > 0.0f) || grand != grand) {
+            // no entry above u (u >= 1) or no usable distribution (NaN logits)
+            pick = n - 1;
+            if (status && !(grand > 0.0f)) atomicOr(status, 8);
+        }
+        *tok = pick;
+    }
+    cluster_sync();  // the other CTAs' shared memory stays alive until every remote read is done
+}
+
 static int launch_argmax_cluster(cudaStream_t st, const float* x, int n, int* idx_out, int* history, int hist_len,
                                  const int* pos, float* val_out, int* pair, int offset) {
     cudaLaunchAttribute attr[2];
@@ -478,6 +681,34 @@ extern "C" int hq4_argmax(const float* x, int n, int* idx_out, int* history, int
     if (history && (!pos || hist_len <= 0)) return HQ4_ERR_SHAPE;
     return launch_argmax_cluster(static_cast<cudaStream_t>(stream), x, n, idx_out, history, hist_len, pos, val_out,
                                  nullptr, 0);
+}
+
+extern "C" int hq4_sample(const float* x, int n, float temperature, float top_p, double u, int* tok,
+                          void* stream) {
+    if (int rc = check_device_cap()) return rc;
+    if (n <= 0 || !x || !tok || !(temperature > 0.0f) || !(top_p > 0.0f)) return HQ4_ERR_SHAPE;
+    const int chunk = (n + kSampleCluster - 1) / kSampleCluster;
+    const size_t smem = (size_t)chunk * sizeof(float);
+    if (smem > 200 * 1024) return HQ4_ERR_SHAPE;
+    static PerDeviceOnce attr_once;
+    if (smem_opt_in(attr_once, sample_cluster_kernel, 200 * 1024) != cudaSuccess) return HQ4_ERR_LAUNCH;
+    cudaLaunchAttribute attr[2];
+    attr[0] = pdl_attr();
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = kSampleCluster;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cudaLaunchConfig_t lc = {};
+    lc.gridDim = dim3(kSampleCluster);
+    lc.blockDim = dim3(kSampleThreads);
+    lc.dynamicSmemBytes = smem;
+    lc.stream = static_cast<cudaStream_t>(stream);
+    lc.attrs = attr;
+    lc.numAttrs = 2;
+    return cudaLaunchKernelEx(&lc, sample_cluster_kernel, x, n, temperature, top_p, u, tok, status_word()) ==
+                   cudaSuccess
+               ? HQ4_OK
+               : HQ4_ERR_LAUNCH;
 }
 
 extern "C" int hq4_argmax_pair(const float* x, int n, int offset, int* pair, void* stream) {

@@ -78,6 +78,8 @@ class QLinear:
         self._ptrs = (self.w.data_ptr(), self.scales.data_ptr(), self.biases.data_ptr(),
                       None if self.bias is None else self.bias.data_ptr())
         self._stage = None  # (rows, pinned x, pinned y, device x, device y, x view, y view)
+        self._dev_idx = None
+        self._host_fn = _lib.load().hq4_gemv_host
 
     def forward_device(self, x: torch.Tensor, out: Optional[torch.Tensor] = None,
                        residual: Optional[torch.Tensor] = None) -> torch.Tensor:
@@ -101,21 +103,25 @@ class QLinear:
         if isinstance(x, torch.Tensor) and x.is_cuda:
             return self.forward_device(x)
         # host path: NumPy in, NumPy out (the reference's calling convention);
-        # one C call copies x in, runs the GEMV, copies the result back and
-        # waits -- q4_gemv's own synchronous host-buffer contract
+        # one C call copies x in, runs the GEMV (whose epilogue writes the
+        # pinned output directly) and waits -- q4_gemv's own synchronous
+        # host-buffer contract
         xa = np.asarray(x, dtype=np.float32)
         lead = xa.shape[:-1]
         flat = xa.reshape(-1, self.n_in)
         m = flat.shape[0]
         *_, hxn, hyn, (hxp, hyp, dxp, dyp) = self._staging(m)
         np.copyto(hxn[:m], flat)
-        w, s, b, bias = self._ptrs
-        idx = self.device.index if self.device.index is not None else torch.cuda.current_device()
+        idx = self._dev_idx
+        if idx is None:
+            idx = self._dev_idx = (self.device.index if self.device.index is not None
+                                   else torch.cuda.current_device())
         if torch.cuda.current_device() != idx:
             with torch.cuda.device(idx):
                 return self.__call__(x)
-        rc = _lib.load().hq4_gemv_host(w, s, b, bias, hxp, hyp, self.n_out, self.n_in, self.group_size, m,
-                                       dxp, dyp, _raw_stream(idx))
+        w, s, b, bias = self._ptrs
+        rc = self._host_fn(w, s, b, bias, hxp, hyp, self.n_out, self.n_in, self.group_size, m, dxp, dyp,
+                           _raw_stream(idx))
         if rc:
             _lib.check(rc, "hq4_gemv_host")
         return hyn[:m].copy().reshape(*lead, self.n_out)
@@ -490,30 +496,28 @@ class CudaBackend:
         return torch.from_numpy(np.asarray(a, dtype=np.float32)).to(self.device)
 
     def sample(self, logits, temperature: float, top_p: float, rng) -> int:
+        """NumpyBackend.sample (hetero/backends.py:106-120) on the device:
+        numpy's argmax at temperature 0 (hq4_argmax), else the temperature /
+        top-p draw (hq4_sample) with the uniform variate taken from `rng` --
+        one rng.random(), the variate rng.choice itself consumes -- so a seeded
+        generator advances exactly as the reference's does."""
         from . import _lib
-        if temperature <= 0 and isinstance(logits, torch.Tensor) and logits.is_cuda:
-            z = logits.reshape(-1).contiguous()
-            idx = torch.empty(1, dtype=torch.int32, device=z.device)
-            lib = _lib.load()
-            _lib.check(lib.hq4_argmax(z.data_ptr(), z.numel(), idx.data_ptr(), None, 0, None, None,
-                                      torch.cuda.current_stream(z.device).cuda_stream), "hq4_argmax")
-            return int(idx.item())
-        # temperature / top-p sampling: the reference's own NumPy procedure
-        z = logits.reshape(-1).float().cpu().numpy() if isinstance(logits, torch.Tensor) else \
-            np.asarray(logits, dtype=np.float32).reshape(-1)
+        if isinstance(logits, torch.Tensor):
+            z = logits.reshape(-1).to(self.device, torch.float32).contiguous()
+        else:
+            z = torch.from_numpy(np.ascontiguousarray(np.asarray(logits, dtype=np.float32).reshape(-1))).to(
+                self.device)
+        lib = _lib.load()
+        out = torch.empty(1, dtype=torch.int32, device=z.device)
+        st = torch.cuda.current_stream(z.device).cuda_stream
         if temperature <= 0:
-            return int(z.argmax())
-        z = z / temperature
-        z -= z.max()
-        p = np.exp(z)
-        p /= p.sum()
-        if top_p < 1.0:
-            order = np.argsort(-p)
-            keep = np.cumsum(p[order]) - p[order] < top_p
-            masked = np.zeros_like(p)
-            masked[order[keep]] = p[order[keep]]
-            p = masked / masked.sum()
-        return int(rng.choice(len(p), p=p))
+            _lib.check(lib.hq4_argmax(z.data_ptr(), z.numel(), out.data_ptr(), None, 0, None, None, st),
+                       "hq4_argmax")
+        else:
+            u = float(rng.random())
+            _lib.check(lib.hq4_sample(z.data_ptr(), z.numel(), float(temperature), float(top_p), u,
+                                      out.data_ptr(), st), "hq4_sample")
+        return int(out.item())
 
     def peak_bytes(self) -> int:
         return int(torch.cuda.max_memory_allocated(self.device))

@@ -38,7 +38,8 @@ int hq4_version(void);
  * when a kernel's bounded wait (a bulk copy or pipeline barrier) ran out --
  * that kernel's output is not valid; bit 1 when hq4_embed_f16 met a token id
  * outside [0, vocab) -- that row was written as zeros; bit 2 when
- * hq4_gemm_w4a16 met an activation outside fp16 range.  Non-zero `clear`
+ * hq4_gemm_w4a16 met an activation outside fp16 range; bit 3 when hq4_sample
+ * met logits without a usable distribution (NaN).  Non-zero `clear`
  * resets it.  No counterpart in the reference: its CPU kernel cannot stall,
  * its table indexing raises IndexError on a bad id, and it computes in fp32. */
 int hq4_device_status(int clear);
@@ -84,7 +85,9 @@ int hq4_gemv_ex(const uint32_t* w, const uint16_t* scales, const uint16_t* biase
  * x_host [m][n_in] is copied to x_dev, the product (+ row_add) is written to
  * out_dev and copied to out_host, and the call waits for `stream`.  x_dev and
  * out_dev are caller-owned device buffers of at least m*n_in and m*n_out
- * floats; pinned host buffers keep the copies at full speed. */
+ * floats; pinned host buffers keep the copies at full speed.  When out_host
+ * is pinned and mapped for the device (cudaHostAlloc / pinned tensors), the
+ * kernel writes the products into it directly and out_dev is not used. */
 int hq4_gemv_host(const uint32_t* w, const uint16_t* scales, const uint16_t* biases,
                   const float* row_add, const float* x_host, float* out_host, int n_out, int n_in,
                   int gs, int m, float* x_dev, float* out_dev, void* stream);
@@ -223,6 +226,19 @@ int hq4_act_encode_i8_wire(const float* x, int rows, int cols, void* payload, vo
  * when val_out is not NULL (a row-sharded head reduces (value, index) pairs). */
 int hq4_argmax(const float* x, int n, int* idx_out, int* history, int hist_len, const int* pos,
                float* val_out, void* stream);
+
+/* Temperature / top-p sampling (hetero/backends.py:110-120, temperature > 0;
+ * temperature 0 is hq4_argmax): z = x / temperature, p = exp(z - max z) /
+ * sum; with top_p < 1 only the nucleus is kept (every probability whose
+ * strictly larger probabilities hold less than top_p of the mass) and
+ * renormalised; then the draw rng.choice(n, p=p) makes for the uniform
+ * variate u in [0, 1) -- the caller draws u = rng.random() from the same
+ * generator, so the generator advances as the reference's does -- written to
+ * *tok.  n up to 8 x 51200.  Sums are fp32 in a fixed order that differs from
+ * NumPy's, so a draw can differ only where u falls within rounding of a
+ * cumulative boundary.  Non-finite logits set status bit 3.  -1 for
+ * temperature <= 0 or top_p <= 0. */
+int hq4_sample(const float* x, int n, float temperature, float top_p, double u, int* tok, void* stream);
 
 /* Fill an fp16 [vocab][hidden] table with the benchmark's counter-based
  * synthetic N(0, std) embedding (seeded; see hetero_infer_b200/synth.py,

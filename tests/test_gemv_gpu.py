@@ -219,3 +219,36 @@ def test_gemv_ex_weights_written_by_the_preceding_kernel(cuda, oracle, n_out, n_
         assert rel_l2(y.cpu().numpy(), ref) <= OUR_TOL, f"case {i}"
     assert lib.hq4_gemv_ex(W.data_ptr(), S.data_ptr(), B.data_ptr(), xd.data_ptr(), y.data_ptr(), n_out, n_in,
                            gs, 1, None, None, 2, st.cuda_stream) == -1
+
+
+@pytest.mark.gpu
+def test_gemv_host_pinned_output_written_by_the_kernel(cuda, oracle):
+    """hq4_gemv_host writes a pinned (device-mapped) output straight from the
+    GEMV's epilogue and copies into any other host buffer: both give the same
+    bits, equal to the device path, for several calls in a row."""
+    import torch
+    from hetero_infer_b200 import _lib
+    lib = _lib.load()
+    n_out, n_in, gs = 18944, 3584, 64
+    w, s, b, x = make_case(n_out, n_in, gs, seed=77)
+    wd, sd, bd = to_dev(w), to_dev(s), to_dev(b)
+    xh = torch.from_numpy(x).pin_memory()
+    dx = torch.empty(1, n_in, device="cuda")
+    dy = torch.empty(1, n_out, device="cuda")
+    st = torch.cuda.current_stream().cuda_stream
+    pinned = torch.empty(1, n_out).pin_memory()
+    pageable = np.empty((1, n_out), np.float32)
+    ref = torch.empty(1, n_out, device="cuda")
+    assert lib.hq4_gemv(wd.data_ptr(), sd.data_ptr(), bd.data_ptr(), to_dev(x).data_ptr(), ref.data_ptr(), n_out, n_in,
+                        gs, 1, st) == 0
+    ref = ref.cpu().numpy()
+    for _ in range(3):
+        pinned.fill_(float("nan"))
+        assert lib.hq4_gemv_host(wd.data_ptr(), sd.data_ptr(), bd.data_ptr(), None, xh.data_ptr(), pinned.data_ptr(),
+                                 n_out, n_in, gs, 1, dx.data_ptr(), dy.data_ptr(), st) == 0
+        assert np.array_equal(pinned.numpy(), ref)
+        pageable.fill(np.nan)
+        assert lib.hq4_gemv_host(wd.data_ptr(), sd.data_ptr(), bd.data_ptr(), None, xh.data_ptr(),
+                                 pageable.ctypes.data, n_out, n_in, gs, 1, dx.data_ptr(), dy.data_ptr(), st) == 0
+        assert np.array_equal(pageable, ref)
+    assert rel_l2(ref, oracle.gemv_f32(w, s, b, x, gs)) <= OUR_TOL
