@@ -628,7 +628,11 @@ static GemmPlan plan_gemm(int n_out, int n_in, int m) {
     const int ctas = pl.row_tiles * pl.n_tt;
     const int nsb = (n_in / 64 + 3) / 4;
     int ks = 1;
-    if (ctas < sms) ks = std::min({8, nsb, std::max(1, sms / ctas)});
+    if (ctas < sms) {
+        static SplitPicker picker;
+        ks = picker.pick((const void*)gemm_w4a16_kernel, kGemmThreads, pl.smem, kGemmSmemMax, ctas,
+                         std::min({8, nsb, std::max(1, sms / ctas)}));
+    }
     pl.ks = ks;
     pl.ws_bytes = (size_t)pl.n_tt * pl.t_tile * (size_t)n_in * 2;
     return pl;
@@ -1133,7 +1137,15 @@ static SmallPlan plan_small(int n_out, int n_in, int m, bool xf32) {
     const int sms = sm_count_gemm();
     const int nsb = (n_in / 64 + 3) / 4;
     int ks = 1;
-    if (pl.row_tiles < sms) ks = std::min({8, nsb, std::max(1, sms / pl.row_tiles)});
+    if (pl.row_tiles < sms) {
+        static SplitPicker picker;
+        const void* kern = pl.nt == 1   ? (const void*)gemm_small_kernel<1>
+                           : pl.nt == 2 ? (const void*)gemm_small_kernel<2>
+                           : pl.nt == 4 ? (const void*)gemm_small_kernel<4>
+                                        : (const void*)gemm_small_kernel<8>;
+        ks = picker.pick(kern, kGemmThreads, pl.smem, kGemmSmemMax, pl.row_tiles,
+                         std::min({8, nsb, std::max(1, sms / pl.row_tiles)}));
+    }
     pl.ks = ks;
     pl.ws_bytes = (size_t)nsb * 4 * pl.nt * kFragBlock;
     return pl;

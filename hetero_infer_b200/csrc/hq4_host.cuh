@@ -41,4 +41,72 @@ inline cudaError_t smem_opt_in(PerDeviceOnce& once, Kern kern, int bytes) {
     return once.run([&](int) { return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes); });
 }
 
+// Split-K factor for `tiles` output tiles of `kern` (one CTA per tile and
+// split, the splits of a tile launched as one 1 x ks x 1 cluster): the ks in
+// [1, kmax] with the most splits per wave, the fewer splits on a tie.  A
+// cluster's CTAs share one GPC, so a device holds fewer clusters of ks than
+// SMs / ks (28 clusters of 5 do not fit 148 SMs at one CTA per SM); the
+// device's own count (cudaOccupancyMaxActiveClusters) is cached per
+// (device, kernel, ks, threads, shared memory).  `smem_limit` is the
+// kernel's dynamic shared-memory opt-in, the same value its launcher sets.
+class SplitPicker {
+public:
+    int pick(const void* kern, int threads, size_t smem, int smem_limit, int tiles, int kmax) {
+        int dev = 0;
+        if (cudaGetDevice(&dev) != cudaSuccess || tiles <= 0) return 1;
+        int best = 1;
+        double best_score = 0.0;
+        for (int ks = 1; ks <= kmax; ks++) {
+            const int cap = capacity(dev, kern, threads, smem, smem_limit, ks);
+            if (cap <= 0) continue;
+            const int waves = (tiles + cap - 1) / cap;
+            const double score = (double)ks / waves;
+            if (score > best_score) {
+                best_score = score;
+                best = ks;
+            }
+        }
+        return best;
+    }
+
+private:
+    struct Entry {
+        int dev, threads, ks, cap;
+        const void* kern;
+        size_t smem;
+    };
+    int capacity(int dev, const void* kern, int threads, size_t smem, int smem_limit, int ks) {
+        std::lock_guard<std::mutex> lock(mu_);
+        for (int i = 0; i < n_; i++) {
+            const Entry& e = cache_[i];
+            if (e.dev == dev && e.kern == kern && e.threads == threads && e.smem == smem && e.ks == ks) return e.cap;
+        }
+        int cap = 0;
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_limit) == cudaSuccess) {
+            cudaLaunchAttribute a;
+            a.id = cudaLaunchAttributeClusterDimension;
+            a.val.clusterDim.x = 1;
+            a.val.clusterDim.y = (unsigned)ks;
+            a.val.clusterDim.z = 1;
+            cudaLaunchConfig_t lc = {};
+            lc.gridDim = dim3(1, (unsigned)ks, 1);
+            lc.blockDim = dim3((unsigned)threads);
+            lc.dynamicSmemBytes = smem;
+            lc.attrs = &a;
+            lc.numAttrs = 1;
+            if (cudaOccupancyMaxActiveClusters(&cap, kern, &lc) != cudaSuccess) cap = 0;
+        }
+        if (cap <= 0) {
+            (void)cudaGetLastError();  // a refused query leaves no sticky error
+            return 0;
+        }
+        if (n_ < kCache) cache_[n_++] = Entry{dev, threads, ks, cap, kern, smem};
+        return cap;
+    }
+    static constexpr int kCache = 256;
+    std::mutex mu_;
+    Entry cache_[kCache];
+    int n_ = 0;
+};
+
 }  // namespace hq4
