@@ -55,7 +55,9 @@
 #include <mutex>
 
 #include "hq4_common.cuh"
+#include "hq4_gemv_dev.cuh"
 #include "hq4_host.cuh"
+#include "hq4_mt.cuh"
 #include "hq4_tmap.cuh"
 #include "hq4.h"
 
@@ -162,11 +164,6 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16
 }
 __device__ __forceinline__ void tmem_wait_st() {
     asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-}
-__device__ __forceinline__ float ld_cluster_f32(uint32_t addr) {
-    float v;
-    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
-    return v;
 }
 
 // Shared-memory matrix descriptor: K-major, 128-byte swizzle, rows of 128 B
@@ -441,6 +438,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     bulk_load_g2s(b_base + (uint32_t)(s * b_stage), src + (size_t)i * b_stage, (uint32_t)b_stage,
                                   full_bar(s), pol_x);
                 }
+                // the weight ring is full: ask L2 for the rest of this CTA's rows
+                // now, so each row is read from DRAM in one pass
+                if (j + 1 == min(DW, nsb))
+                    for (int jj = DW; jj < nsb; jj++) tma_prefetch_l2_2d(&tm_w, (kb0 + 4 * jj) * 8, row0);
             }
         }
     } else if (lane == 0) {
@@ -1037,6 +1038,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 }
                 bulk_load_g2s(dst + kWSlotBytes, p.xw + (size_t)(sb0 + j) * b_bytes, (uint32_t)b_bytes,
                               full_bar(slot), pol_x);
+                // the ring is full: ask L2 for the rest of this CTA's rows now, so
+                // each weight row is read from DRAM in one pass, not 128 bytes
+                // per super-block as the ring drains
+                if (j + 1 == min(DW, nsb))
+                    for (int jj = DW; jj < nsb; jj++) tma_prefetch_l2_2d(&tm_w, (kb0 + 4 * jj) * 8, row0);
                 if (++slot == DW) {
                     slot = 0;
                     ph ^= 1u;
@@ -1243,6 +1249,28 @@ extern "C" int hq4_gemm_w4a16(const uint32_t* w, const uint16_t* scales, const u
                                       static_cast<cudaStream_t>(stream), &used);
         if (rc || used) return rc;
     }
+    if (m <= kMtMaxTok) {
+        // a few tokens: the multi-token streaming kernel (the one-token
+        // kernel's exact digit product, tokens sharing the weight fragments)
+        MtParams mp = {};
+        mp.w = w;
+        mp.sc = scales;
+        mp.bi = biases;
+        mp.x = x;
+        mp.x_stride = n_in;
+        mp.x_bf16 = xf32 ? 0 : 1;
+        mp.out = out;
+        mp.out_stride = n_out;
+        mp.n_out = n_out;
+        mp.n_in = n_in;
+        mp.m = m;
+        mp.row_add = row_add;
+        mp.residual = residual;
+        mp.mode = kEpiPlain;
+        bool used = false;
+        const int rc = gemv_mt_pass(mp, gs, static_cast<cudaStream_t>(stream), &used);
+        if (rc || used) return rc;
+    }
     int* status = status_word();
     if (!status) return HQ4_ERR_LAUNCH;
     WeightMaps wm;
@@ -1307,6 +1335,11 @@ extern "C" int hq4_gemm_plan(int n_out, int n_in, int m, int x_is_f32, int* info
     if (m == 1 && gemv_stream_fits_gs64(n_out, n_in)) {
         for (int i = 0; i < 7; i++) info[i] = 0;
         info[7] = 2;  // streaming GEMV
+        return HQ4_OK;
+    }
+    if (m >= 2 && gemv_mt_fits(n_out, n_in, 64, m)) {
+        for (int i = 0; i < 7; i++) info[i] = 0;
+        info[7] = 3;  // multi-token streaming kernel
         return HQ4_OK;
     }
     if (use_small(m, x_is_f32 != 0)) {

@@ -46,6 +46,7 @@
 #include "hq4_common.cuh"
 #include "hq4_gemv_dev.cuh"
 #include "hq4_host.cuh"
+#include "hq4_mt.cuh"
 #include "hq4_tmap.cuh"
 #include "hq4.h"
 
@@ -859,6 +860,31 @@ int gemv_launch_stage(const uint32_t* w, const uint16_t* scales, const uint16_t*
 
 int check_device_cap() { return check_device(); }
 
+// Two or more fp32 tokens through the multi-token streaming kernel (passes
+// of up to 8 tokens); *used is false when the shape or pointers do not suit
+// it.
+static int gemv_tokens_mt(const uint32_t* w, const uint16_t* sc, const uint16_t* bi, const float* x, float* out,
+                          int n_out, int n_in, int gs, int m, const float* row_add, const float* residual,
+                          int weights_after_wait, cudaStream_t st, bool* used) {
+    *used = false;
+    if (m < 2) return HQ4_OK;
+    MtParams mp = {};
+    mp.w = w;
+    mp.sc = sc;
+    mp.bi = bi;
+    mp.x = x;
+    mp.x_stride = n_in;
+    mp.out = out;
+    mp.out_stride = n_out;
+    mp.n_out = n_out;
+    mp.n_in = n_in;
+    mp.row_add = row_add;
+    mp.residual = residual;
+    mp.mode = kEpiPlain;
+    mp.weights_after_wait = weights_after_wait;
+    return gemv_mt_tokens(mp, gs, m, st, used);
+}
+
 }  // namespace hq4
 
 using namespace hq4;
@@ -882,6 +908,10 @@ extern "C" int hq4_gemv(const uint32_t* w, const uint16_t* scales, const uint16_
     if (int rc = check_device()) return rc;
     if (m <= 0) return HQ4_ERR_SHAPE;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
+    bool used = false;
+    if (int rc = gemv_tokens_mt(w, scales, biases, x, out, n_out, n_in, gs, m, nullptr, nullptr, 0, st, &used))
+        return rc;
+    if (used) return HQ4_OK;
     for (int i = 0; i < m; i++) {
         int rc = gemv_m1(w, scales, biases, x + (size_t)i * n_in, out + (size_t)i * n_out, n_out,
                          n_in, gs, nullptr, nullptr, st);
@@ -896,6 +926,10 @@ extern "C" int hq4_gemv_fused(const uint32_t* w, const uint16_t* scales, const u
     if (int rc = check_device()) return rc;
     if (m <= 0) return HQ4_ERR_SHAPE;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
+    bool used = false;
+    if (int rc = gemv_tokens_mt(w, scales, biases, x, out, n_out, n_in, gs, m, row_add, residual, 0, st, &used))
+        return rc;
+    if (used) return HQ4_OK;
     for (int i = 0; i < m; i++) {
         int rc = gemv_m1(w, scales, biases, x + (size_t)i * n_in, out + (size_t)i * n_out, n_out,
                          n_in, gs, row_add, residual ? residual + (size_t)i * n_out : nullptr, st);
@@ -910,6 +944,11 @@ extern "C" int hq4_gemv_ex(const uint32_t* w, const uint16_t* scales, const uint
     if (int rc = check_device()) return rc;
     if (m <= 0 || (flags & ~HQ4_GEMV_WEIGHTS_AFTER_WAIT)) return HQ4_ERR_SHAPE;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
+    bool used = false;
+    if (int rc = gemv_tokens_mt(w, scales, biases, x, out, n_out, n_in, gs, m, row_add, residual,
+                                (flags & HQ4_GEMV_WEIGHTS_AFTER_WAIT) ? 1 : 0, st, &used))
+        return rc;
+    if (used) return HQ4_OK;
     for (int i = 0; i < m; i++) {
         GemvM1Params prm = gemv_params(w, scales, biases, x + (size_t)i * n_in, out + (size_t)i * n_out, n_out, n_in);
         prm.row_add = row_add;

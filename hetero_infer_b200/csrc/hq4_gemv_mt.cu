@@ -1,0 +1,830 @@
+// Multi-token streaming W4A16 product (a few tokens per pass over the weights):
+//   out[j][r] = sum_k x[j][k] * (q[r][k] * scale[r][k/gs] + bias[r][k/gs])
+// for microbatched decode and prompt chunks.  The reference computes the
+// same product in QLinear (hetero/cpu_model.py:118-136): one q4gemv call per
+// token (kernel/q4gemv.c:232-301), dequantisation plus a BLAS matmul for a
+// prompt.
+//
+// The weight stream is the one-token streaming GEMV's (hq4_gemv.cu): one
+// producer thread brings 16-row strips x 16 k-chunks of 256 values (32 KB of
+// packed words plus the strip's scales and biases) through a ring of shared-
+// memory stages with TMA, and consumer warp w takes k-chunk w of every stage.
+// The arithmetic is that kernel's exact digit product, laid out so that the
+// tokens share each weight fragment:
+// * x of a (64-value group, token) is a 22-bit fixed-point integer (the
+//   group's exponent E, v = rint(x 2^(22-E))) written as three balanced s8
+//   digits d2, d1, d0, one MMA column per digit;
+// * in an m16n8k32 integer MMA all 32 k-slots belong to one group (words 2t
+//   and 2t+1 of the group for lane t: even nibbles of a word in one register,
+//   odd ones in the other, 3 instructions per word), so the 8 columns are 8
+//   (token, digit) pairs and a group is 2 MMAs per 8 columns: 16 MMAs per
+//   16 x 256 tile serve 4 tokens (2 column tiles), 24 serve 8 (3 tiles);
+// * lane t of the accumulator holds columns 2t, 2t+1 of every tile: its
+//   tokens are t, t+4 and their digits sit in its own columns, so a token's
+//   dot (d2 2^16 + d1 2^8 + d0, exact integers, two fp32 roundings) and its
+//   scale and bias (s 2^(E-22) dot + b sum(x)) stay lane-local.
+// The digits of bf16 x are exact; fp32 x carries 22 bits below its group's
+// maximum, as in the one-token kernel.  Every sum runs in a fixed order
+// (deterministic).
+//
+// Stages run strip-major (a strip's k-blocks back to back), so a warp keeps
+// its share of the strip in registers.  At the strip's end each warp parks
+// its 16-row x token tile in one of two partial slots, and warps 0-7 sum the
+// slot over the 16 warps in warp order one strip later (mbarriers, no CTA-
+// wide barrier per stage) and apply the epilogue of the one-token kernel:
+// plain with row add and residual, SiLU(gate) * up, or q|k|v with RoPE and
+// the cache writes.  When the x image of a CTA's whole row does not fit
+// beside the ring, K is split over a thread-block cluster: each CTA takes a
+// range of k-chunks of the cluster's strips, parks its per-strip sums, and
+// after a cluster barrier the sums are added over the ranks in rank order
+// through distributed shared memory (deterministic, no atomics, no global
+// scratch).
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include <cuda.h>
+
+#include <algorithm>
+#include <mutex>
+#include <unordered_map>
+
+#include "hq4.h"
+#include "hq4_common.cuh"
+#include "hq4_gemv_dev.cuh"
+#include "hq4_host.cuh"
+#include "hq4_mt.cuh"
+#include "hq4_tmap.cuh"
+
+namespace hq4 {
+
+int* status_word();
+int check_device_cap();
+
+// Column tiles (8 MMA columns each) per pass and the tokens they carry: lane
+// t holds 2 CT columns, 3 per token, so 4 * floor(2 CT / 3) tokens.
+__host__ __device__ constexpr int mt_tokens(int ct) { return 4 * ((2 * ct) / 3); }
+// Image bytes of one k-chunk: per column tile 4 groups x 32 lanes x 16 B of B
+// fragments, then per (group, token) the fp32 pair (2^(E-22), sum of x).
+__host__ __device__ constexpr int mt_img_bytes(int ct) { return ct * 2048 + 4 * kMtMaxTok * 8; }
+constexpr int kMtEarlyStages = 3;          // stages issued before the x images are built
+constexpr int kMtPartSlots = 4;            // strips whose per-warp tiles wait for their sum
+constexpr size_t kMtSmemTarget = 220 * 1024;
+constexpr int kMtMaxRing = 5;
+
+struct MtLayout {
+    int ring, ns_max, nch_max, ct, ks;
+    __host__ __device__ int tok() const { return mt_tokens(ct); }
+    __host__ __device__ size_t img_off() const { return (size_t)ring * kStrStageBytes; }
+    __host__ __device__ size_t part_off() const { return img_off() + (size_t)nch_max * mt_img_bytes(ct); }
+    __host__ __device__ size_t res_off() const {
+        return part_off() + (size_t)kMtPartSlots * kStrConsumers * 16 * tok() * 4;
+    }
+    __host__ __device__ size_t red_off() const {
+        return res_off() + (ks > 1 ? (size_t)ns_max * 16 * tok() * 4 : 0);
+    }
+    __host__ __device__ size_t nf_off() const { return red_off() + (size_t)kMtMaxTok * kStrConsumers * 4; }
+    __host__ __device__ size_t bar_off() const { return nf_off() + (size_t)kMtMaxTok * 4; }
+    // full[ring], empty[ring], images built, partial full[slots], partial empty[slots]
+    __host__ __device__ size_t bytes() const {
+        return bar_off() + (size_t)(2 * ring + 1 + 2 * kMtPartSlots) * 8 + 1024;
+    }
+};
+
+// RMSNorm factors 1/sqrt(mean(x_j^2) + eps) of the pass's tokens into nf[]:
+// thread i sums squares of x values 4i..4i+3 (mod 2048) in k order, the warp's
+// xor tree, then the warps in order.  Named barrier 1 over the consumers.
+__device__ __forceinline__ void mt_norm_factors(const MtParams& p, float* red, float* nf, int warp, int lane) {
+    const int tid = warp * 32 + lane;
+    for (int j = 0; j < p.m; j++) {
+        const float* xr = static_cast<const float*>(p.x) + (size_t)j * p.x_stride;
+        float ss = 0.0f;
+        for (int k = tid * 4; k < p.n_in; k += kStrConsumers * 32 * 4) {
+            const float4 v = *reinterpret_cast<const float4*>(xr + k);
+            ss = fmaf(v.x, v.x, ss);
+            ss = fmaf(v.y, v.y, ss);
+            ss = fmaf(v.z, v.z, ss);
+            ss = fmaf(v.w, v.w, ss);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        if (lane == 0) red[j * kStrConsumers + warp] = ss;
+    }
+    asm volatile("bar.sync 1, 512;" ::: "memory");
+    if (tid < p.m) {
+        float tot = 0.0f;
+#pragma unroll
+        for (int w = 0; w < kStrConsumers; w++) tot += red[tid * kStrConsumers + w];
+        const float mean = __fdiv_rn(tot, (float)p.n_in);
+        nf[tid] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, p.eps)));
+    }
+    asm volatile("bar.sync 1, 512;" ::: "memory");
+}
+
+// The digit columns of this warp's k-chunks (local chunk lc = warp + 16 i of
+// the CTA's range starting at c0).  Lane (g, t) supplies B column g of every
+// column tile ct: the column's owner in the accumulator is lane-group g/2,
+// its flat index f = 2 ct + g%2 among that lane-group's columns, token
+// g/2 + 4 (f / 3), digit f % 3 (d2, d1, d0).  A lane therefore serves one
+// token at 2 column tiles and two at 3: per token it requests its x values
+// 16t..16t+15 of the chunk's 4 groups together (one round trip to memory,
+// which under the weight stream is the prologue's cost), the four lanes of
+// a column share each group's exponent and sum through two shuffles, and the
+// digits go out as the two MMAs' B registers: even k to b0, odd k to b1.
+template <int CT>
+__device__ __forceinline__ void mt_build(const MtParams& p, unsigned char* img, int c0, int nch, const float* nf,
+                                         int warp, int lane) {
+    constexpr int T = mt_tokens(CT), NSG = T / 4;
+    const int g = lane >> 2, t = lane & 3, h = g & 1;
+    for (int lc = warp; lc < nch; lc += kStrConsumers) {
+        unsigned char* cimg = img + (size_t)lc * mt_img_bytes(CT);
+        const int kbase = (c0 + lc) * 256 + 16 * t;
+#pragma unroll
+        for (int sg = 0; sg < NSG; sg++) {
+            const int j = (g >> 1) + 4 * sg;
+            const bool valid = j < p.m;
+            float v[4][16];
+            if (!valid) {
+#pragma unroll
+                for (int u = 0; u < 4; u++)
+#pragma unroll
+                    for (int i = 0; i < 16; i++) v[u][i] = 0.0f;
+            } else if (p.x_bf16) {  // bf16 widens to fp32 exactly
+                uint4 r[4][2];
+#pragma unroll
+                for (int u = 0; u < 4; u++) {
+                    const uint4* src = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.x) +
+                                                                      (size_t)j * p.x_stride + kbase + 64 * u);
+                    r[u][0] = src[0];
+                    r[u][1] = src[1];
+                }
+#pragma unroll
+                for (int u = 0; u < 4; u++) {
+                    const uint32_t wv[8] = {r[u][0].x, r[u][0].y, r[u][0].z, r[u][0].w,
+                                            r[u][1].x, r[u][1].y, r[u][1].z, r[u][1].w};
+#pragma unroll
+                    for (int i = 0; i < 8; i++) {
+                        v[u][2 * i] = __uint_as_float(wv[i] << 16);
+                        v[u][2 * i + 1] = __uint_as_float(wv[i] & 0xFFFF0000u);
+                    }
+                }
+            } else {
+#pragma unroll
+                for (int u = 0; u < 4; u++) {
+                    const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(p.x) +
+                                                                        (size_t)j * p.x_stride + kbase + 64 * u);
+#pragma unroll
+                    for (int i = 0; i < 4; i++) {
+                        const float4 q = src[i];
+                        v[u][4 * i] = q.x;
+                        v[u][4 * i + 1] = q.y;
+                        v[u][4 * i + 2] = q.z;
+                        v[u][4 * i + 3] = q.w;
+                    }
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                if (valid && !p.x_bf16 && p.norm_w) {
+                    const float4* nw = reinterpret_cast<const float4*>(p.norm_w + kbase + 64 * u);
+                    const float r = nf[j];
+#pragma unroll
+                    for (int i = 0; i < 4; i++) {
+                        const float4 q = nw[i];
+                        v[u][4 * i] = __fmul_rn(__fmul_rn(v[u][4 * i], r), q.x);
+                        v[u][4 * i + 1] = __fmul_rn(__fmul_rn(v[u][4 * i + 1], r), q.y);
+                        v[u][4 * i + 2] = __fmul_rn(__fmul_rn(v[u][4 * i + 2], r), q.z);
+                        v[u][4 * i + 3] = __fmul_rn(__fmul_rn(v[u][4 * i + 3], r), q.w);
+                    }
+                }
+                float amax = 0.0f, sum = 0.0f;
+#pragma unroll
+                for (int i = 0; i < 16; i++) {
+                    amax = fmaxf(amax, fabsf(v[u][i]));
+                    sum += v[u][i];
+                }
+                amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+                amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+                sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+                sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+                const int E = group_exponent(amax);
+                const float up = exp2i(kXBits - E);
+                uint32_t dw[16];
+#pragma unroll
+                for (int i = 0; i < 16; i++) dw[i] = digits3(v[u][i], up);
+#pragma unroll
+                for (int ct = 0; ct < CT; ct++) {
+                    const int f = 2 * ct + h;
+                    if (f / 3 != sg) continue;
+                    const int sh = 8 * (2 - f % 3);  // d2 is byte 2 of the digit word, d0 byte 0
+                    uint32_t d[16];
+#pragma unroll
+                    for (int i = 0; i < 16; i++) d[i] = (dw[i] >> sh) & 0xFFu;
+                    *reinterpret_cast<uint4*>(cimg + ct * 2048 + u * 512 + lane * 16) =
+                        make_uint4(d[0] | (d[2] << 8) | (d[4] << 16) | (d[6] << 24),
+                                   d[1] | (d[3] << 8) | (d[5] << 16) | (d[7] << 24),
+                                   d[8] | (d[10] << 8) | (d[12] << 16) | (d[14] << 24),
+                                   d[9] | (d[11] << 8) | (d[13] << 16) | (d[15] << 24));
+                }
+                // (2^(E-22), sum) of (group u, token j), from the lane of its d2 column
+                if (t == 0 && h == ((3 * sg) & 1))
+                    *reinterpret_cast<float2*>(cimg + CT * 2048 + (u * kMtMaxTok + j) * 8) =
+                        make_float2(exp2i(E - kXBits), sum);
+            }
+        }
+        // columns past the last token slot (2 column tiles: the lane-groups'
+        // fourth column) multiply zeros
+#pragma unroll
+        for (int ct = 0; ct < CT; ct++) {
+            if ((2 * ct + h) / 3 < NSG) continue;
+#pragma unroll
+            for (int u = 0; u < 4; u++)
+                *reinterpret_cast<uint4*>(cimg + ct * 2048 + u * 512 + lane * 16) = make_uint4(0, 0, 0, 0);
+        }
+    }
+}
+
+// Scale-tile byte offset of (row, scale group gi) inside a stage (the tile
+// carries the swizzle of its row width, as the one-token kernel's).
+__device__ __forceinline__ int mt_sb_off(int row, int gi, int sb_row, int sb_mask) {
+    const int o = row * sb_row + gi * 2;
+    return o ^ (((o >> 7) & sb_mask) << 4);
+}
+
+// Per-lane constants of the tile arithmetic: the scale-tile offsets of this
+// warp's 4 groups in rows g and g+8 (at one scale per group the four are 8
+// consecutive bytes inside one swizzle unit: one 8-byte load per row).
+struct MtLane {
+    int so[2][4];
+    bool vec;
+};
+__device__ __forceinline__ MtLane mt_lane(int warp, int lane, int sg_shift, int sb_row, int sb_mask) {
+    MtLane L;
+    const int g = lane >> 2;
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+        const int gi = (warp * 4 + u) >> sg_shift;
+        L.so[0][u] = mt_sb_off(g, gi, sb_row, sb_mask);
+        L.so[1][u] = mt_sb_off(g + 8, gi, sb_row, sb_mask);
+    }
+    L.vec = sg_shift == 0;
+    return L;
+}
+
+// One stage tile of this warp (16 rows x k-chunk `warp`) against the chunk
+// image `cimg`, accumulated into acc[sigma] = rows (g, g+8) of token t + 4 sigma.
+template <int CT>
+__device__ __forceinline__ void mt_tile(const unsigned char* st, const unsigned char* cimg, int warp, int lane,
+                                        const MtLane& L, float (&acc)[mt_tokens(CT) / 4][2]) {
+    constexpr int NS = mt_tokens(CT) / 4;
+    const int g = lane >> 2, t = lane & 3;
+    const unsigned char* wt = st + warp * kStrTileBytes;
+    const unsigned char* ss = st + kStrWBytes;
+    const unsigned char* sbi = st + kStrWBytes + kStrSBBytes;
+    uint32_t sc[2][4], bc[2][4];  // fp16 bits of the 4 groups' scales and biases, rows g and g+8
+    if (L.vec) {
+#pragma unroll
+        for (int r = 0; r < 2; r++) {
+            const uint2 a = *reinterpret_cast<const uint2*>(ss + L.so[r][0]);
+            const uint2 b = *reinterpret_cast<const uint2*>(sbi + L.so[r][0]);
+            sc[r][0] = a.x & 0xFFFFu, sc[r][1] = a.x >> 16, sc[r][2] = a.y & 0xFFFFu, sc[r][3] = a.y >> 16;
+            bc[r][0] = b.x & 0xFFFFu, bc[r][1] = b.x >> 16, bc[r][2] = b.y & 0xFFFFu, bc[r][3] = b.y >> 16;
+        }
+    } else {
+#pragma unroll
+        for (int r = 0; r < 2; r++)
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                sc[r][u] = *reinterpret_cast<const uint16_t*>(ss + L.so[r][u]);
+                bc[r][u] = *reinterpret_cast<const uint16_t*>(sbi + L.so[r][u]);
+            }
+    }
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+        const float s0 = h2f(sc[0][u]), s1 = h2f(sc[1][u]);
+        const float b0 = h2f(bc[0][u]), b1 = h2f(bc[1][u]);
+        // words 2t, 2t+1 of group u in rows g and g+8 (128-byte swizzle)
+        const int c16 = 2 * u + (t >> 1);
+        const int wo = ((c16 ^ g) << 4) + (t & 1) * 8;
+        const uint2 w0 = *reinterpret_cast<const uint2*>(wt + g * 128 + wo);
+        const uint2 w1 = *reinterpret_cast<const uint2*>(wt + (g + 8) * 128 + wo);
+        uint32_t e0, o0, e1, o1, e2, o2, e3, o3;
+        unpack_u8(w0.x, e0, o0);
+        unpack_u8(w1.x, e1, o1);
+        unpack_u8(w0.y, e2, o2);
+        unpack_u8(w1.y, e3, o3);
+        int c[CT][4];
+#pragma unroll
+        for (int ct = 0; ct < CT; ct++) {
+            const uint4 B = *reinterpret_cast<const uint4*>(cimg + ct * 2048 + u * 512 + lane * 16);
+            mma_u8s8_16832_first(c[ct], e0, e1, o0, o1, B.x, B.y);
+            mma_u8s8_16832(c[ct], e2, e3, o2, o3, B.z, B.w);
+        }
+#pragma unroll
+        for (int sg = 0; sg < NS; sg++) {
+            // columns 3 sg (d2), 3 sg + 1 (d1), 3 sg + 2 (d0) of this lane's flat list
+            const int f2 = 3 * sg, f1 = 3 * sg + 1, f0 = 3 * sg + 2;
+            const float2 meta = *reinterpret_cast<const float2*>(cimg + CT * 2048 + (u * kMtMaxTok + t + 4 * sg) * 8);
+            // dot = d2 2^16 + d1 2^8 + d0: the low two digits combined exactly in
+            // 32 bits (|d1 sum| * 2^8 < 2^25), then one fp32 rounding
+            const int lo0 = c[f1 >> 1][f1 & 1] * 256 + c[f0 >> 1][f0 & 1];
+            const int lo1 = c[f1 >> 1][2 + (f1 & 1)] * 256 + c[f0 >> 1][2 + (f0 & 1)];
+            const float dot0 = fmaf((float)c[f2 >> 1][f2 & 1], 65536.0f, (float)lo0);
+            const float dot1 = fmaf((float)c[f2 >> 1][2 + (f2 & 1)], 65536.0f, (float)lo1);
+            acc[sg][0] = fmaf(s0 * meta.x, dot0, fmaf(b0, meta.y, acc[sg][0]));
+            acc[sg][1] = fmaf(s1 * meta.x, dot1, fmaf(b1, meta.y, acc[sg][1]));
+        }
+    }
+}
+
+// Store rows (g, g+8) of strip s for token j of the pass, as the one-token
+// kernel's store_pair_in does for its token.
+__device__ __forceinline__ void mt_store(const MtParams& p, int s, int g, int j, float y0, float y1) {
+    if (p.mode == kEpiPlain) {
+        const int r[2] = {s * 16 + g, s * 16 + g + 8};
+        const float yv[2] = {y0, y1};
+#pragma unroll
+        for (int q = 0; q < 2; q++) {
+            if (r[q] >= p.n_out) continue;
+            const size_t o = (size_t)j * p.out_stride + r[q];
+            float y = yv[q];
+            if (p.row_add) y += p.row_add[r[q]];
+            if (p.residual) y += p.residual[o];
+            p.out[o] = y;
+        }
+        return;
+    }
+    if (p.mode == kEpiSiluMul) {
+        // strip s holds gate rows 8s..8s+7 (g) and the matching up rows (g+8)
+        const int r = s * 8 + g;
+        if (r < p.n_out / 2) p.out[(size_t)j * p.out_stride + r] = __fmul_rn(silu_ref(y0), y1);
+        return;
+    }
+    // kEpiQkvRope
+    if (p.row_add) {
+        y0 = __fadd_rn(y0, p.row_add[s * 16 + g]);
+        y1 = __fadd_rn(y1, p.row_add[s * 16 + g + 8]);
+    }
+    const int half = p.head_dim >> 1;
+    const int spp = half >> 3;  // strips per head (8 rotation pairs per strip)
+    const int pos = *p.pos + p.tok0 + j;
+    if (pos < 0 || pos >= p.max_ctx) return;  // outside the cache: write nothing
+    if (s < p.q_strips + p.k_strips) {
+        const bool is_q = s < p.q_strips;
+        const int sl = is_q ? s : s - p.q_strips;
+        const int head = sl / spp, jj = (sl % spp) * 8 + g;
+        const float c = p.rope_cos[(size_t)pos * half + jj], sn = p.rope_sin[(size_t)pos * half + jj];
+        // hetero/cpu_model.py:200-203: (x1*cos - x2*sin, x1*sin + x2*cos)
+        const float o1 = __fsub_rn(__fmul_rn(y0, c), __fmul_rn(y1, sn));
+        const float o2 = __fadd_rn(__fmul_rn(y0, sn), __fmul_rn(y1, c));
+        float* dst = is_q ? p.q_out + (size_t)j * p.q_stride + (size_t)head * p.head_dim
+                          : p.k_cache + ((size_t)head * p.max_ctx + pos) * p.head_dim;
+        dst[jj] = o1;
+        dst[jj + half] = o2;
+    } else {
+        const int r0 = (s - p.q_strips - p.k_strips) * 16 + g;  // natural v row order
+        const int r1 = r0 + 8;
+        const int head0 = r0 / p.head_dim, head1 = r1 / p.head_dim;
+        p.v_cache[((size_t)head0 * p.max_ctx + pos) * p.head_dim + (r0 % p.head_dim)] = y0;
+        p.v_cache[((size_t)head1 * p.max_ctx + pos) * p.head_dim + (r1 % p.head_dim)] = y1;
+    }
+}
+
+// Sums of rows (g, g+8) of strip s for token `lane` -> the epilogue.
+__device__ __forceinline__ void mt_emit(const MtParams& p, int s, int g, int lane, int tok, float y0, float y1,
+                                        bool store) {
+    if (store && lane < tok && lane < p.m) mt_store(p, s, g, lane, y0, y1);
+}
+
+template <int CT>
+__global__ void __launch_bounds__(kStrThreads, 1)
+    gemv_mt_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_w1,
+                   const __grid_constant__ CUtensorMap tm_s, const __grid_constant__ CUtensorMap tm_b,
+                   const MtParams p, const MtLayout L) {
+    extern __shared__ unsigned char smem_raw[];
+    const uint32_t raw_u = smem_u32(smem_raw);
+    unsigned char* base = smem_raw + (((raw_u + 1023u) & ~1023u) - raw_u);
+    const uint32_t base_u = smem_u32(base);
+    const int R = L.ring;
+    unsigned char* img = base + L.img_off();
+    float* part = reinterpret_cast<float*>(base + L.part_off());
+    float* res = reinterpret_cast<float*>(base + L.res_off());
+    float* red = reinterpret_cast<float*>(base + L.red_off());
+    float* nf = reinterpret_cast<float*>(base + L.nf_off());
+    const uint32_t bars = base_u + (uint32_t)L.bar_off();
+    auto full_bar = [&](int s) { return bars + 8u * s; };
+    auto empty_bar = [&](int s) { return bars + 8u * (R + s); };
+    const uint32_t images_bar = bars + 8u * (2 * R);
+    auto pfull_bar = [&](int s) { return bars + 8u * (2 * R + 1 + s); };
+    auto pempty_bar = [&](int s) { return bars + 8u * (2 * R + 1 + kMtPartSlots + s); };
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int ks = p.ks;
+    const int rank = (int)blockIdx.y;  // cluster rank: the cluster is 1 x ks x 1
+    const int cl = (int)blockIdx.x;
+    const int s0 = (int)((long long)cl * p.n_strips / p.n_clusters);
+    const int s1 = (int)((long long)(cl + 1) * p.n_strips / p.n_clusters);
+    const int ns = s1 - s0;
+    const int align = 2 << p.sg_shift;
+    const int c0 = mt_chunk_start(rank, ks, p.n_chunks, align), c1 = mt_chunk_start(rank + 1, ks, p.n_chunks, align);
+    const int nch = c1 - c0;
+    const int nkb = (nch + kStrKc - 1) / kStrKc;
+    const int n_stages = ns * nkb;
+    const int sg_cols = kStrSBCols >> p.sg_shift;
+    const uint32_t sb_bytes = 16u * sg_cols * 2u;
+    const int sb_row = sg_cols * 2, sb_mask = (sb_row >> 4) - 1;
+
+    // ---- producer (warp 16, one thread): stages strip-major
+    const bool producer = warp == kStrConsumers && lane == 0;
+    int p_issued = 0, p_slot = 0, p_use = 0, p_kb = 0, p_j = 0;
+    uint64_t pol = 0;
+    auto issue_stage = [&]() {
+        const int strip = s0 + p_j;
+        const int cbase = c0 + p_kb * kStrKc;
+        const int nval = min(kStrKc, nch - p_kb * kStrKc);
+        // a whole box unless it would reach into the next rank's chunks (a
+        // box past the row end reads zeros and costs no traffic)
+        const bool whole = nval == kStrKc || c1 == p.n_chunks;
+        const uint32_t dst = base_u + (uint32_t)p_slot * kStrStageBytes;
+        mbar_arrive_expect_tx(full_bar(p_slot),
+                              (uint32_t)(whole ? kStrWBytes : nval * kStrTileBytes) + 2u * sb_bytes);
+        if (whole) {
+            tma_load_3d(dst, &tm_w, 0, strip * 16, cbase, full_bar(p_slot), pol);
+        } else {
+            for (int i = 0; i < nval; i++)
+                tma_load_3d(dst + (uint32_t)(i * kStrTileBytes), &tm_w1, 0, strip * 16, cbase + i, full_bar(p_slot),
+                            pol);
+        }
+        const int gx = (cbase * 4) >> p.sg_shift;
+        tma_load_2d(dst + kStrWBytes, &tm_s, gx, strip * 16, full_bar(p_slot), pol);
+        tma_load_2d(dst + kStrWBytes + kStrSBBytes, &tm_b, gx, strip * 16, full_bar(p_slot), pol);
+        p_issued++;
+        if (++p_slot == R) {
+            p_slot = 0;
+            p_use++;
+        }
+        if (++p_kb == nkb) {
+            p_kb = 0;
+            p_j++;
+        }
+    };
+    if (producer) {
+        prefetch_tensormap(&tm_w);
+        prefetch_tensormap(&tm_w1);
+        prefetch_tensormap(&tm_s);
+        prefetch_tensormap(&tm_b);
+        for (int s = 0; s < R; s++) {
+            mbar_init_nofence(full_bar(s), 1);
+            mbar_init_nofence(empty_bar(s), kStrConsumers);
+        }
+        mbar_init_nofence(images_bar, kStrConsumers);
+        for (int s = 0; s < kMtPartSlots; s++) {
+            mbar_init_nofence(pfull_bar(s), kStrConsumers);
+            mbar_init_nofence(pempty_bar(s), kStrConsumers);
+        }
+        mbar_init_fence();
+        pol = l2_policy_evict_first();  // weights are read once
+        if (p.weights_after_wait) pdl_wait();
+        const int first = min(min(R, kMtEarlyStages), n_stages);
+        for (int i = 0; i < first; i++) issue_stage();
+    }
+    __syncthreads();  // barriers initialised
+    pdl_launch_dependents();
+
+    bool ok = true;
+    if (warp == kStrConsumers) {
+        if (producer) {
+            if (p_issued < n_stages) {
+                pdl_wait();
+                ok = mbar_wait_nap(images_bar, 0, kStrWaitNs, 64);
+            }
+            while (ok && p_issued < n_stages) {
+                if (!mbar_wait_nap(empty_bar(p_slot), (p_use - 1) & 1, kStrWaitNs, 64)) {
+                    ok = false;
+                    break;
+                }
+                issue_stage();
+            }
+            if (!ok && p.status) atomicOr(p.status, 1);
+            // every issued copy lands before the CTA may exit
+            for (int k = max(0, p_issued - R); k < p_issued; k++)
+                if (!mbar_wait_nap(full_bar(k % R), (k / R) & 1, kStrWaitNs, 64) && p.status) atomicOr(p.status, 1);
+        }
+        __syncwarp();
+    } else {
+        // ---- consumers (warps 0-15)
+        constexpr int T = mt_tokens(CT), NS = T / 4;
+        pdl_wait();  // x, norm weights, residual and the outputs follow the previous kernel
+        if (!p.x_bf16 && p.norm_w) mt_norm_factors(p, red, nf, warp, lane);
+        mt_build<CT>(p, img, c0, nch, nf, warp, lane);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(images_bar);
+        const MtLane ML = mt_lane(warp, lane, p.sg_shift, sb_row, sb_mask);
+        int slot = 0;
+        uint32_t phase = 0;
+        const int g = lane >> 2, t = lane & 3;
+        // every warp sums a share of strip si's partial slot over the 16 warps:
+        // rows (warp % 8, warp % 8 + 8) x the T/2 tokens of half warp / 8, T
+        // values.  Lane l takes value l % T of the warps l / T + 32 / T * i
+        // (i < T / 2, in order), then a fixed xor tree over the lane groups;
+        // lanes 0..T/2-1 end with (row warp % 8, row + 8) of one token each.
+        // The slot's barriers are polled, not slept on: they complete within
+        // a stage.
+        const int rg = warp & 7, th = warp >> 3;
+        const int lv = lane % T, lw = lane / T;
+        const int lrow = rg + 8 * (lv / (T / 2)), ltok = th * (T / 2) + lv % (T / 2);
+        auto reduce = [&](int si) {
+            const int ps = si % kMtPartSlots;
+            const uint32_t use = (uint32_t)(si / kMtPartSlots);
+            if (ok && !mbar_wait_spin(pfull_bar(ps), use & 1u, kStrWaitNs)) ok = false;
+            float y = 0.0f;
+            if (ok) {
+                const float* src = part + (size_t)ps * kStrConsumers * 16 * T + lrow * T + ltok;
+#pragma unroll
+                for (int i = 0; i < T / 2; i++) y += src[(size_t)(lw + (32 / T) * i) * 16 * T];
+            }
+#pragma unroll
+            for (int o = T; o < 32; o <<= 1) y += __shfl_xor_sync(0xffffffffu, y, o);
+            __syncwarp();
+            if (ok && lane == 0) mbar_arrive(pempty_bar(ps));
+            const float y1 = __shfl_down_sync(0xffffffffu, y, T / 2);  // row + 8 of the same token
+            const bool mine = lane < T / 2;
+            if (ks == 1) {
+                if (ok && mine && ltok < p.m) mt_store(p, s0 + si, rg, ltok, y, y1);
+            } else if (mine) {
+                res[((size_t)si * 16 + rg) * T + ltok] = y;
+                res[((size_t)si * 16 + rg + 8) * T + ltok] = y1;
+            }
+        };
+        for (int si = 0; si < ns; si++) {
+            float acc[NS][2];
+#pragma unroll
+            for (int sg = 0; sg < NS; sg++) acc[sg][0] = acc[sg][1] = 0.0f;
+            for (int kb = 0; kb < nkb; kb++) {
+                if (ok && !mbar_wait_tries(full_bar(slot), phase, kStrTryHintNs, kStrTries)) ok = false;
+                const int lc = kb * kStrKc + warp;
+                if (ok && lc < nch)
+                    mt_tile<CT>(base + (size_t)slot * kStrStageBytes, img + (size_t)lc * mt_img_bytes(CT), warp,
+                                lane, ML, acc);
+                __syncwarp();
+                // a slot whose copy never arrived is not handed back
+                if (ok && lane == 0) mbar_arrive(empty_bar(slot));
+                if (++slot == R) {
+                    slot = 0;
+                    phase ^= 1u;
+                }
+            }
+            // park the strip's tile in its partial slot once the strip that
+            // used the slot before has been summed
+            const int ps = si % kMtPartSlots;
+            const uint32_t use = (uint32_t)(si / kMtPartSlots);
+            if (ok && use > 0 && !mbar_wait_spin(pempty_bar(ps), (use - 1) & 1u, kStrWaitNs)) ok = false;
+            if (ok) {
+                float* dst = part + ((size_t)ps * kStrConsumers + warp) * 16 * T;
+#pragma unroll
+                for (int sg = 0; sg < NS; sg++) {
+                    dst[g * T + t + 4 * sg] = acc[sg][0];
+                    dst[(g + 8) * T + t + 4 * sg] = acc[sg][1];
+                }
+            }
+            __syncwarp();
+            if (ok && lane == 0) mbar_arrive(pfull_bar(ps));
+            if (si > 0) reduce(si - 1);
+        }
+        if (ns > 0) reduce(ns - 1);
+        if (!ok && lane == 0 && p.status) atomicOr(p.status, 1);
+    }
+
+    // ---- split K: the cluster's ranks' strip sums, added in rank order
+    if (ks > 1) {
+        constexpr int T = mt_tokens(CT);
+        __syncwarp();
+        cluster_sync();  // every rank's strip sums are parked
+        if (warp < kStrConsumers) {
+            const uint32_t res_u = smem_u32(res);
+            for (int u = rank + ks * warp; u < ns * 8; u += ks * kStrConsumers) {
+                const int si = u >> 3, gg = u & 7;
+                float y0 = 0.0f, y1 = 0.0f;
+                if (lane < T) {
+                    const uint32_t a0 = res_u + (uint32_t)((((size_t)si * 16 + gg) * T + lane) * 4);
+                    const uint32_t a1 = res_u + (uint32_t)((((size_t)si * 16 + gg + 8) * T + lane) * 4);
+                    for (int q = 0; q < ks; q++) {
+                        y0 += ld_cluster_f32(map_to_rank(a0, (uint32_t)q));
+                        y1 += ld_cluster_f32(map_to_rank(a1, (uint32_t)q));
+                    }
+                }
+                mt_emit(p, s0 + si, gg, lane, T, y0, y1, true);
+            }
+        }
+        __syncwarp();
+        cluster_sync();  // no rank leaves while others read its sums
+    }
+}
+
+// ---- host side -------------------------------------------------------------
+struct MtKey {
+    const void* w;
+    const void* s;
+    const void* b;
+    int n_out, n_in, sg_cols, dev;
+    bool operator==(const MtKey& o) const {
+        return w == o.w && s == o.s && b == o.b && n_out == o.n_out && n_in == o.n_in && sg_cols == o.sg_cols &&
+               dev == o.dev;
+    }
+};
+struct MtKeyHash {
+    size_t operator()(const MtKey& k) const {
+        size_t h = std::hash<const void*>()(k.w);
+        h = h * 1000003u ^ std::hash<const void*>()(k.s);
+        h = h * 1000003u ^ std::hash<const void*>()(k.b);
+        h = h * 1000003u ^ (size_t)k.n_out * 31u ^ (size_t)k.n_in * 131u ^ (size_t)k.sg_cols ^ ((size_t)k.dev << 40);
+        return h;
+    }
+};
+struct MtMaps {
+    CUtensorMap tw, tw1, ts, tb;
+};
+
+// Packed words as (32 words, rows, chunks) with 16-row boxes of 16 chunks
+// (a stage) and of 1 chunk (a stage cut at a rank's range end); scales and
+// biases as sg_cols x 16-row boxes.  Cached by (pointers, shape, device).
+static bool mt_maps(const MtParams& p, int sg_cols, MtMaps* out) {
+    static std::mutex mu;
+    static std::unordered_map<MtKey, MtMaps, MtKeyHash> cache;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return false;
+    const MtKey key{p.w, p.sc, p.bi, p.n_out, p.n_in, sg_cols, dev};
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) {
+        *out = it->second;
+        return true;
+    }
+    MtMaps m;
+    if (!make_map_chunks(&m.tw, p.w, p.n_out, p.n_in / 8, 16, kStrKc) ||
+        !make_map_chunks(&m.tw1, p.w, p.n_out, p.n_in / 8, 16, 1) ||
+        !make_map_2d_sw(&m.ts, p.sc, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, p.n_out, p.n_sg, sg_cols, 16,
+                        sb_swizzle(sg_cols)) ||
+        !make_map_2d_sw(&m.tb, p.bi, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, p.n_out, p.n_sg, sg_cols, 16,
+                        sb_swizzle(sg_cols)))
+        return false;
+    if (cache.size() >= 4096) cache.clear();
+    cache.emplace(key, m);
+    *out = m;
+    return true;
+}
+
+static int sm_count_mt() {
+    int dev = 0, n = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) return 148;
+    return n;
+}
+
+// Column tiles for a pass of m tokens: 2 (4 tokens) or 3 (8 tokens).
+static int mt_ct(int m) { return m <= mt_tokens(2) ? 2 : 3; }
+static const void* mt_kernel_of(int ct) {
+    return ct == 2 ? (const void*)gemv_mt_kernel<2> : (const void*)gemv_mt_kernel<3>;
+}
+
+struct MtPlan {
+    int ct, ks, n_clusters;
+    MtLayout L;
+};
+
+// The K split and ring for a pass of m tokens: the split (1..8 ranks) with the
+// fewest weight chunks on the busiest CTA (strips per cluster x chunks per
+// rank), among those whose image fits beside a ring of at least 3 stages and
+// whose clusters the device holds at once; the smaller split on a tie.
+// False if none fits.
+static bool mt_plan(int n_out, int n_in, int m, int sg_shift, MtPlan& pl) {
+    static SplitPicker caps;
+    const int align = 2 << sg_shift;
+    const int n_strips = (n_out + 15) / 16, n_chunks = n_in / 256;
+    const int sms = sm_count_mt();
+    pl.ct = mt_ct(m);
+    const void* kern = mt_kernel_of(pl.ct);
+    long long best = -1;
+    for (int ks = 1; ks <= 8 && ks <= n_chunks; ks++) {
+        MtLayout L;
+        L.ct = pl.ct;
+        L.ks = ks;
+        L.nch_max = 0;
+        for (int r = 0; r < ks; r++)
+            L.nch_max = std::max(L.nch_max, mt_chunk_start(r + 1, ks, n_chunks, align) -
+                                                mt_chunk_start(r, ks, n_chunks, align));
+        int n_clusters = std::min(n_strips, sms / ks);
+        if (n_clusters <= 0) break;
+        L.ns_max = (n_strips + n_clusters - 1) / n_clusters;
+        L.ring = kMtMaxRing;
+        while (L.ring > 3 && L.bytes() > kMtSmemTarget) L.ring--;
+        if (L.bytes() > kMtSmemTarget) continue;
+        if (ks > 1) {
+            const int cap = caps.capacity(kern, kStrThreads, L.bytes(), (int)kMtSmemTarget, ks);
+            if (cap <= 0) continue;
+            if (cap < n_clusters) {
+                n_clusters = cap;
+                L.ns_max = (n_strips + n_clusters - 1) / n_clusters;
+                L.ring = kMtMaxRing;
+                while (L.ring > 3 && L.bytes() > kMtSmemTarget) L.ring--;
+                if (L.bytes() > kMtSmemTarget) continue;
+            }
+        }
+        const long long cost = (long long)L.ns_max * L.nch_max;
+        if (best < 0 || cost < best) {
+            best = cost;
+            pl.ks = ks;
+            pl.n_clusters = n_clusters;
+            pl.L = L;
+        }
+    }
+    return best >= 0;
+}
+
+template <int CT>
+static int mt_launch_t(const MtMaps& m, const MtParams& prm, const MtPlan& pl, cudaStream_t st) {
+    static PerDeviceOnce attr_once;
+    if (smem_opt_in(attr_once, gemv_mt_kernel<CT>, (int)kMtSmemTarget) != cudaSuccess) return HQ4_ERR_LAUNCH;
+    cudaLaunchAttribute attr[2];
+    int na = 0;
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    na++;
+    if (pl.ks > 1) {
+        attr[na].id = cudaLaunchAttributeClusterDimension;
+        attr[na].val.clusterDim.x = 1;
+        attr[na].val.clusterDim.y = (unsigned)pl.ks;
+        attr[na].val.clusterDim.z = 1;
+        na++;
+    }
+    cudaLaunchConfig_t lc = {};
+    lc.gridDim = dim3((unsigned)pl.n_clusters, (unsigned)pl.ks, 1);
+    lc.blockDim = dim3(kStrThreads);
+    lc.dynamicSmemBytes = pl.L.bytes();
+    lc.stream = st;
+    lc.attrs = attr;
+    lc.numAttrs = na;
+    return cudaLaunchKernelEx(&lc, gemv_mt_kernel<CT>, m.tw, m.tw1, m.ts, m.tb, prm, pl.L) == cudaSuccess
+               ? HQ4_OK
+               : HQ4_ERR_LAUNCH;
+}
+
+static bool mt_shape_ok(int n_out, int n_in, int gs, int* sg_shift) {
+    if (n_out <= 0 || n_in <= 0 || n_in % 256 || gs < 64 || gs % 64) return false;
+    int s = 0;
+    while ((64 << s) < gs) s++;
+    if ((64 << s) != gs || s > 2 || (n_in / gs) % 8) return false;
+    *sg_shift = s;
+    return true;
+}
+
+int gemv_mt_pass(MtParams prm, int gs, cudaStream_t st, bool* used) {
+    *used = false;
+    int sgs = 0;
+    if (prm.m <= 0 || prm.m > kMtMaxTok || !mt_shape_ok(prm.n_out, prm.n_in, gs, &sgs)) return HQ4_OK;
+    if (prm.x_bf16 && prm.norm_w) return HQ4_OK;  // the norm prologue takes fp32 x
+    if ((((uintptr_t)prm.sc | (uintptr_t)prm.bi) & 15) || ((uintptr_t)prm.w & 15) || ((uintptr_t)prm.x & 15) ||
+        (prm.norm_w && ((uintptr_t)prm.norm_w & 15)) || (prm.x_stride % 8))
+        return HQ4_OK;
+    MtPlan pl;
+    if (!mt_plan(prm.n_out, prm.n_in, prm.m, sgs, pl)) return HQ4_OK;
+    prm.n_chunks = prm.n_in / 256;
+    prm.sg_shift = sgs;
+    prm.n_sg = prm.n_in / gs;
+    prm.n_strips = (prm.n_out + 15) / 16;
+    prm.ks = pl.ks;
+    prm.n_clusters = pl.n_clusters;
+    prm.status = status_word();
+    MtMaps m;
+    if (!mt_maps(prm, kStrSBCols >> sgs, &m)) return HQ4_OK;
+    *used = true;
+    return pl.ct == 2 ? mt_launch_t<2>(m, prm, pl, st) : mt_launch_t<3>(m, prm, pl, st);
+}
+
+bool gemv_mt_fits(int n_out, int n_in, int gs, int m) {
+    int sgs = 0;
+    MtPlan pl;
+    return m > 0 && m <= kMtMaxTok && mt_shape_ok(n_out, n_in, gs, &sgs) && mt_plan(n_out, n_in, m, sgs, pl);
+}
+
+int gemv_mt_tokens(MtParams prm, int gs, int m_total, cudaStream_t st, bool* used) {
+    *used = false;
+    if (m_total <= 0 || !gemv_mt_fits(prm.n_out, prm.n_in, gs, std::min(m_total, kMtMaxTok))) return HQ4_OK;
+    const size_t xe = prm.x_bf16 ? 2 : 4;  // bytes per x element
+    for (int t0 = 0; t0 < m_total; t0 += kMtMaxTok) {
+        MtParams q = prm;
+        q.m = std::min(kMtMaxTok, m_total - t0);
+        q.x = static_cast<const unsigned char*>(prm.x) + (size_t)t0 * prm.x_stride * xe;
+        q.out = prm.out ? prm.out + (size_t)t0 * prm.out_stride : nullptr;
+        q.residual = prm.residual ? prm.residual + (size_t)t0 * prm.out_stride : nullptr;
+        q.q_out = prm.q_out ? prm.q_out + (size_t)t0 * prm.q_stride : nullptr;
+        q.tok0 = prm.tok0 + t0;
+        bool u = false;
+        const int rc = gemv_mt_pass(q, gs, st, &u);
+        if (rc) return rc;
+        if (!u) return t0 == 0 ? HQ4_OK : HQ4_ERR_LAUNCH;  // the shape fits every pass once it fits one
+        *used = true;
+    }
+    return HQ4_OK;
+}
+
+}  // namespace hq4

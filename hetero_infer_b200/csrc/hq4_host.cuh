@@ -69,6 +69,14 @@ public:
         return best;
     }
 
+    // Clusters of ks CTAs (1 x ks x 1) of `kern` the current device holds at
+    // once; 0 when the query fails.
+    int capacity(const void* kern, int threads, size_t smem, int smem_limit, int ks) {
+        int dev = 0;
+        if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+        return capacity(dev, kern, threads, smem, smem_limit, ks);
+    }
+
 private:
     struct Entry {
         int dev, threads, ks, cap;

@@ -15,6 +15,7 @@
 #include "hq4_attn.cuh"
 #include "hq4_host.cuh"
 #include "hq4_common.cuh"
+#include "hq4_mt.cuh"
 #include "hq4.h"
 
 namespace hq4 {
@@ -738,6 +739,26 @@ extern "C" int hq4_gemv_norm(const uint32_t* w, const uint16_t* scales, const ui
     if (m <= 0 || (silu_mul && n_out % 16)) return HQ4_ERR_SHAPE;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     const int n_store = silu_mul ? n_out / 2 : n_out;
+    if (m >= 2) {  // a prompt: the multi-token kernel, passes of up to 8 tokens
+        MtParams mp = {};
+        mp.w = w;
+        mp.sc = scales;
+        mp.bi = biases;
+        mp.x = x;
+        mp.x_stride = n_in;
+        mp.out = out;
+        mp.out_stride = n_store;
+        mp.n_out = n_out;
+        mp.n_in = n_in;
+        mp.row_add = silu_mul ? nullptr : row_add;
+        mp.residual = silu_mul ? nullptr : residual;
+        mp.norm_w = norm_w;
+        mp.eps = eps;
+        mp.mode = silu_mul ? 1 : 0;  // kEpiSiluMul : kEpiPlain
+        bool used = false;
+        if (int rc = gemv_mt_tokens(mp, gs, m, st, &used)) return rc;
+        if (used) return HQ4_OK;
+    }
     for (int i = 0; i < m; i++) {
         int rc = gemv_launch_stage(w, scales, biases, x + (size_t)i * n_in, out + (size_t)i * n_store,
                                    n_out, n_in, gs, silu_mul ? nullptr : row_add,
@@ -760,6 +781,36 @@ extern "C" int hq4_qkv_rope(const uint32_t* w, const uint16_t* scales, const uin
     const int half = head_dim / 2;
     const int q_strips = n_heads * half / 8, k_strips = n_kv * half / 8;
     const int n_out = (n_heads + 2 * n_kv) * head_dim;
+    if (m >= 2) {  // a prompt: the multi-token kernel, passes of up to 8 tokens
+        MtParams mp = {};
+        mp.w = w;
+        mp.sc = scales;
+        mp.bi = biases;
+        mp.x = x;
+        mp.x_stride = n_in;
+        mp.out = q_out;
+        mp.out_stride = n_heads * head_dim;
+        mp.n_out = n_out;
+        mp.n_in = n_in;
+        mp.row_add = bias;
+        mp.norm_w = norm_w;
+        mp.eps = eps;
+        mp.mode = 2;  // kEpiQkvRope
+        mp.q_strips = q_strips;
+        mp.k_strips = k_strips;
+        mp.head_dim = head_dim;
+        mp.max_ctx = max_ctx;
+        mp.pos = pos;
+        mp.rope_cos = rope_cos;
+        mp.rope_sin = rope_sin;
+        mp.q_out = q_out;
+        mp.q_stride = n_heads * head_dim;
+        mp.k_cache = k_cache;
+        mp.v_cache = v_cache;
+        bool used = false;
+        if (int rc = gemv_mt_tokens(mp, gs, m, st, &used)) return rc;
+        if (used) return HQ4_OK;
+    }
     for (int i = 0; i < m; i++) {
         int rc = gemv_launch_stage(w, scales, biases, x + (size_t)i * n_in, q_out, n_out, n_in, gs, bias,
                                    nullptr, norm_w, eps, 2, q_strips, k_strips, head_dim, max_ctx, i, pos,

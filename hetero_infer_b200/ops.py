@@ -172,7 +172,7 @@ def gemm_plan(n_out: int, n_in: int, m: int, x_is_f32: bool = False) -> dict:
     _lib.check(lib.hq4_gemm_plan(n_out, n_in, m, 1 if x_is_f32 else 0, info), "hq4_gemm_plan")
     keys = ("row_tiles", "ksplit", "token_tiles", "tile_tokens", "stages", "smem", "weight_slots", "kernel")
     d = dict(zip(keys, list(info)))
-    d["kernel"] = {0: "tcgen05", 1: "mma.sync", 2: "gemv"}[d["kernel"]]
+    d["kernel"] = {0: "tcgen05", 1: "mma.sync", 2: "gemv", 3: "gemv_mt"}[d["kernel"]]
     return d
 
 

@@ -136,7 +136,12 @@ long long hq4_gemm_workspace_bytes(int n_out, int n_in, int m);
  * weights exact as 128+q in bf16, for up to 16 bf16 / 8 fp32 tokens; 2: one
  * token through the streaming GEMV of hq4_gemv, info[0..6] then 0 -- reported
  * for group size 64 with 16-byte aligned scales and biases, which that kernel
- * needs; other one-token calls take kernel 1).  No reference counterpart. */
+ * needs; other one-token calls take kernel 1; 3: 2..8 tokens through the
+ * multi-token streaming kernel, the one-token kernel's exact digit product
+ * with the tokens sharing each weight fragment, info[0..6] then 0 --
+ * reported for group size 64 where n_in is a multiple of 256 and the x
+ * image fits shared memory; kernels 1 and 0 take the rest).  No reference
+ * counterpart. */
 int hq4_gemm_plan(int n_out, int n_in, int m, int x_is_f32, int* info);
 
 /* hq4_gemm_w4a16 without a caller workspace: the workspace is a fixed

@@ -1,10 +1,13 @@
 """W4A16 tcgen05 GEMM (hq4_gemm_w4a16) on the GPU.
 
-Two kernels sit behind the entry point (hq4_gemm_plan says which):
-* register path (up to 16 bf16 / 8 fp32 tokens): weights exact, fp32 x as
-  bf16 hi + lo -- checked against the full-precision product (the
-  reference's float path, out = x . (q*s+b)^T, hetero/cpu_model.py QLinear,
-  kernel/q4gemv.c:113-139 per token) to 2e-5 (bf16 x) / 5e-5 (fp32 x);
+Four kernels sit behind the entry point (hq4_gemm_plan says which):
+* multi-token streaming kernel (2..8 tokens where its x image fits): the
+  one-token kernel's exact digit product -- checked against the full-
+  precision product (the reference's float path, out = x . (q*s+b)^T,
+  hetero/cpu_model.py QLinear, kernel/q4gemv.c:113-139 per token) to 2e-6;
+* register path (the other token counts up to 16 bf16 / 8 fp32): weights
+  exact, fp32 x as bf16 hi + lo -- checked against the full-precision
+  product to 2e-5 (bf16 x) / 5e-5 (fp32 x);
 * one token: hq4_gemv's streaming kernel (weights exact, x widened to fp32)
   -- the register path's bars;
 * tcgen05 path: weights rounded once to fp16, x to fp16 -- checked against
@@ -19,6 +22,7 @@ from hetero_infer_b200 import synth
 
 EXACT_TOL = 1e-5
 SPEC_TOL = 1e-3
+MT_TOL = 4e-6
 
 
 def rel_l2(a, b):
@@ -79,6 +83,14 @@ SHAPES = [
     (18944, 3584, 1, 64, "bf16"),         # one token: the streaming GEMV
     (3584, 18944, 1, 64, "f32"),          # one token, fp32 x
     (512, 1024, 1, 128, "bf16"),          # one token, gs 128
+    (18944, 3584, 4, 64, "bf16"),         # multi-token kernel, config 3
+    (18944, 3584, 8, 64, "bf16"),         # multi-token kernel, three column tiles
+    (3584, 18944, 4, 64, "bf16"),         # multi-token kernel, K split over a cluster
+    (3584, 18944, 8, 64, "f32"),
+    (4608, 3584, 5, 64, "f32"),
+    (1000, 512, 3, 64, "f32"),            # ragged last strip
+    (256, 2048, 6, 256, "bf16"),          # scale groups of 256
+    (512, 2048, 7, 128, "f32"),           # scale groups of 128
 ]
 
 
@@ -95,7 +107,9 @@ def test_gemm_matches_exact_and_reference(cuda, ci):
     exact, spec = _refs(dw, ds, db, x, gs)
     plan = ops.gemm_plan(n_out, n_in, m, xd == "f32")
     e1, e2 = rel_l2(y, exact), rel_l2(y, spec)
-    if plan["kernel"] in ("mma.sync", "gemv"):
+    if plan["kernel"] == "gemv_mt":
+        assert e2 <= MT_TOL, f"{SHAPES[ci]}: vs full precision {e2:.2e} ({plan})"
+    elif plan["kernel"] in ("mma.sync", "gemv"):
         assert e2 <= (5e-5 if xd == "f32" else 2e-5), f"{SHAPES[ci]}: vs full precision {e2:.2e} ({plan})"
     else:
         assert e1 <= EXACT_TOL, f"{SHAPES[ci]}: vs fp16-operand product {e1:.2e} ({plan})"
@@ -119,7 +133,7 @@ def test_gemm_row_add_residual_and_reference_oracle(cuda, oracle, m):
     res = torch.randn(m, n_out, device="cuda")
     y = ops.q4_gemm(dw, ds, db, x, gs, row_add=ra, residual=res)
     exact, spec = _refs(dw, ds, db, x, gs)
-    if ops.gemm_plan(n_out, n_in, m)["kernel"] == "mma.sync":
+    if ops.gemm_plan(n_out, n_in, m)["kernel"] in ("mma.sync", "gemv_mt"):
         assert rel_l2(y, spec + ra.double() + res.double()) <= 2e-5
     else:
         assert rel_l2(y, exact + ra.double() + res.double()) <= EXACT_TOL
@@ -159,8 +173,8 @@ def test_gemm_error_codes(cuda):
 @pytest.mark.gpu
 def test_gemm_range_flag(cuda):
     """The tcgen05 path carries x in fp16: bf16 activations beyond fp16 range
-    set status bit 2 (no silent inf).  The register path keeps bf16 and
-    computes such inputs exactly, with no flag."""
+    set status bit 2 (no silent inf).  The register and multi-token paths
+    keep bf16 and compute such inputs exactly, with no flag."""
     import torch
     from hetero_infer_b200 import _lib, ops
     lib = _lib.load()
@@ -175,7 +189,7 @@ def test_gemm_range_flag(cuda):
     torch.cuda.synchronize()
     assert lib.hq4_device_status(1) & 4
     xs = x[:8].contiguous()
-    assert ops.gemm_plan(256, 512, 8)["kernel"] == "mma.sync"
+    assert ops.gemm_plan(256, 512, 8)["kernel"] in ("mma.sync", "gemv_mt")
     y = ops.q4_gemm(dw, ds, db, xs, 64)
     torch.cuda.synchronize()
     assert lib.hq4_device_status(1) & 4 == 0
@@ -199,7 +213,7 @@ def test_gemm_back_to_back_calls(cuda, shape):
         for dw, ds, db, x in cases:
             outs.append(ops.q4_gemm(dw, ds, db, x, 64, workspace=ws))
     torch.cuda.synchronize()
-    small = ops.gemm_plan(n_out, n_in, m)["kernel"] == "mma.sync"
+    small = ops.gemm_plan(n_out, n_in, m)["kernel"] in ("mma.sync", "gemv_mt")
     for j, y in enumerate(outs):
         dw, ds, db, x = cases[j % 3]
         exact, spec = _refs(dw, ds, db, x, 64)

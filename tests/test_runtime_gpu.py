@@ -76,7 +76,9 @@ def test_stage_runner_frames_match_reference(cuda, tmp_path, codec):
             # 1e-7 of the row's scale apart) within 1e-5 of the row's largest value
             near = np.abs(ours - ref) <= 1e-5 * np.abs(ref).max(axis=-1, keepdims=True)
             assert np.all((_f16_ulps(ours, ref) <= 1) | near), f"frame {i}"
-            assert np.mean(ours != ref) < 0.03, f"frame {i}"  # ~1% of elements sit on a rounding edge
+            # 1-3% of elements sit on a rounding edge (prompt frames go through the
+            # multi-token kernel, whose fp32 sums run in another order)
+            assert np.mean(ours != ref) < 0.05, f"frame {i}"
         else:
             step = np.abs(ref).max(axis=-1, keepdims=True) / 127.0
             assert np.all(np.abs(ours - ref) <= 1.01 * step + 1e-6), f"frame {i}"
