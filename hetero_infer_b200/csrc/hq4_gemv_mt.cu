@@ -27,18 +27,24 @@
 // maximum, as in the one-token kernel.  Every sum runs in a fixed order
 // (deterministic).
 //
+// x is converted once per CTA, before the stage loop.  For passes of up to
+// 4 tokens a CTA's k-range is at most 16 chunks (K is split over a cluster
+// where it is longer), so warp w owns chunk w and keeps its digit registers
+// (the MMAs' B operands) and each group's (2^(E-22), sum(x)) in registers for
+// the whole pass; the two lanes of a token's columns split its values.  For
+// 8-token passes the digits of the CTA's k-range wait in a shared-memory
+// image.
+//
 // Stages run strip-major (a strip's k-blocks back to back), so a warp keeps
-// its share of the strip in registers.  At the strip's end each warp parks
-// its 16-row x token tile in one of two partial slots, and warps 0-7 sum the
-// slot over the 16 warps in warp order one strip later (mbarriers, no CTA-
-// wide barrier per stage) and apply the epilogue of the one-token kernel:
-// plain with row add and residual, SiLU(gate) * up, or q|k|v with RoPE and
-// the cache writes.  When the x image of a CTA's whole row does not fit
-// beside the ring, K is split over a thread-block cluster: each CTA takes a
-// range of k-chunks of the cluster's strips, parks its per-strip sums, and
-// after a cluster barrier the sums are added over the ranks in rank order
-// through distributed shared memory (deterministic, no atomics, no global
-// scratch).
+// its share of a strip in registers.  At the strip's end each warp parks its
+// 16-row x token sums in shared memory; every 32/T strips all consumer
+// threads add the parked sums over the 16 warps in warp order (between two
+// named barriers, no per-stage synchronisation) and apply the epilogue of the
+// one-token kernel: plain with row add and residual, SiLU(gate) * up, or
+// q|k|v with RoPE and the cache writes.  With K split over a cluster each
+// CTA parks its per-strip sums, and after a cluster barrier they are added
+// over the ranks in rank order through distributed shared memory
+// (deterministic, no atomics, no global scratch).
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
@@ -67,27 +73,33 @@ __host__ __device__ constexpr int mt_tokens(int ct) { return 4 * ((2 * ct) / 3);
 // fragments, then per (group, token) the fp32 pair (2^(E-22), sum of x).
 __host__ __device__ constexpr int mt_img_bytes(int ct) { return ct * 2048 + 4 * kMtMaxTok * 8; }
 constexpr int kMtEarlyStages = 3;          // stages issued before the x images are built
-constexpr int kMtPartSlots = 4;            // strips whose per-warp tiles wait for their sum
+// Per-warp strip sums wait in shared memory for a batch of 32 / T strips (32
+// KB) before the 16 warps add them up together.
+constexpr int kMtPartFloats = 8192;
+__host__ __device__ constexpr int mt_batch(int tok) { return kMtPartFloats / (kStrConsumers * 16 * tok); }
 constexpr size_t kMtSmemTarget = 220 * 1024;
 constexpr int kMtMaxRing = 5;
+
+// Passes of up to 4 tokens (2 column tiles) keep each warp's x digits in
+// registers (one k-chunk per warp: the CTA's k-range is at most 16 chunks);
+// 8-token passes keep a shared-memory image of the CTA's k-range.
+__host__ __device__ constexpr bool mt_reg(int ct) { return ct == 2; }
 
 struct MtLayout {
     int ring, ns_max, nch_max, ct, ks;
     __host__ __device__ int tok() const { return mt_tokens(ct); }
     __host__ __device__ size_t img_off() const { return (size_t)ring * kStrStageBytes; }
-    __host__ __device__ size_t part_off() const { return img_off() + (size_t)nch_max * mt_img_bytes(ct); }
-    __host__ __device__ size_t res_off() const {
-        return part_off() + (size_t)kMtPartSlots * kStrConsumers * 16 * tok() * 4;
+    __host__ __device__ size_t part_off() const {
+        return img_off() + (mt_reg(ct) ? 0 : (size_t)nch_max * mt_img_bytes(ct));
     }
+    __host__ __device__ size_t res_off() const { return part_off() + (size_t)kMtPartFloats * 4; }
     __host__ __device__ size_t red_off() const {
         return res_off() + (ks > 1 ? (size_t)ns_max * 16 * tok() * 4 : 0);
     }
     __host__ __device__ size_t nf_off() const { return red_off() + (size_t)kMtMaxTok * kStrConsumers * 4; }
     __host__ __device__ size_t bar_off() const { return nf_off() + (size_t)kMtMaxTok * 4; }
-    // full[ring], empty[ring], images built, partial full[slots], partial empty[slots]
-    __host__ __device__ size_t bytes() const {
-        return bar_off() + (size_t)(2 * ring + 1 + 2 * kMtPartSlots) * 8 + 1024;
-    }
+    // full[ring], empty[ring], images built
+    __host__ __device__ size_t bytes() const { return bar_off() + (size_t)(2 * ring + 1) * 8 + 1024; }
 };
 
 // RMSNorm factors 1/sqrt(mean(x_j^2) + eps) of the pass's tokens into nf[]:
@@ -120,16 +132,107 @@ __device__ __forceinline__ void mt_norm_factors(const MtParams& p, float* red, f
     asm volatile("bar.sync 1, 512;" ::: "memory");
 }
 
+// x values 16t..16t+15 of each of the 4 groups of the chunk whose first
+// value is kbase - 16t, for token j (zeros when !valid), RMSNorm applied
+// when p.norm_w: every value requested before any is used (one round trip
+// to memory, which under the weight stream is the prologue's cost).
+__device__ __forceinline__ void mt_load_x(const MtParams& p, int j, bool valid, int kbase, const float* nf,
+                                          float (&v)[4][16]) {
+    if (!valid) {
+#pragma unroll
+        for (int u = 0; u < 4; u++)
+#pragma unroll
+            for (int i = 0; i < 16; i++) v[u][i] = 0.0f;
+        return;
+    }
+    if (p.x_bf16) {  // bf16 widens to fp32 exactly
+        uint4 r[4][2];
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            const uint4* src = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.x) +
+                                                              (size_t)j * p.x_stride + kbase + 64 * u);
+            r[u][0] = src[0];
+            r[u][1] = src[1];
+        }
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            const uint32_t wv[8] = {r[u][0].x, r[u][0].y, r[u][0].z, r[u][0].w,
+                                    r[u][1].x, r[u][1].y, r[u][1].z, r[u][1].w};
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                v[u][2 * i] = __uint_as_float(wv[i] << 16);
+                v[u][2 * i + 1] = __uint_as_float(wv[i] & 0xFFFF0000u);
+            }
+        }
+        return;
+    }
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+        const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(p.x) + (size_t)j * p.x_stride +
+                                                            kbase + 64 * u);
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const float4 q = src[i];
+            v[u][4 * i] = q.x;
+            v[u][4 * i + 1] = q.y;
+            v[u][4 * i + 2] = q.z;
+            v[u][4 * i + 3] = q.w;
+        }
+    }
+    if (p.norm_w) {
+        const float r = nf[j];
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            const float4* nw = reinterpret_cast<const float4*>(p.norm_w + kbase + 64 * u);
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const float4 q = nw[i];
+                v[u][4 * i] = __fmul_rn(__fmul_rn(v[u][4 * i], r), q.x);
+                v[u][4 * i + 1] = __fmul_rn(__fmul_rn(v[u][4 * i + 1], r), q.y);
+                v[u][4 * i + 2] = __fmul_rn(__fmul_rn(v[u][4 * i + 2], r), q.z);
+                v[u][4 * i + 3] = __fmul_rn(__fmul_rn(v[u][4 * i + 3], r), q.w);
+            }
+        }
+    }
+}
+
+// One group's exponent E and sum over the four lanes of a column (two
+// shuffles each) and its 16 values' digit words (d2 d1 d0 in bytes 2 1 0).
+__device__ __forceinline__ void mt_group(const float (&v)[16], int& E, float& sum, uint32_t (&dw)[16]) {
+    float amax = 0.0f;
+    sum = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 16; i++) {
+        amax = fmaxf(amax, fabsf(v[i]));
+        sum += v[i];
+    }
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+    E = group_exponent(amax);
+    const float up = exp2i(kXBits - E);
+#pragma unroll
+    for (int i = 0; i < 16; i++) dw[i] = digits3(v[i], up);
+}
+
+// The two MMAs' B registers of digit di (0: d2, 1: d1, 2: d0): even k to
+// b0, odd k to b1, values 0-7 for the first MMA, 8-15 for the second.
+__device__ __forceinline__ uint4 mt_frag(const uint32_t (&dw)[16], int di) {
+    // byte b of two words into bytes 0, 1 (prmt selector nibbles b, b + 4)
+    const uint32_t b = 2 - di, sel = b | ((b + 4) << 4);
+    auto word = [&](int i) {  // bytes b of dw[i], dw[i+2], dw[i+4], dw[i+6]
+        return prmt(prmt(dw[i], dw[i + 2], sel), prmt(dw[i + 4], dw[i + 6], sel), 0x5410);
+    };
+    return make_uint4(word(0), word(1), word(8), word(9));
+}
+
 // The digit columns of this warp's k-chunks (local chunk lc = warp + 16 i of
-// the CTA's range starting at c0).  Lane (g, t) supplies B column g of every
-// column tile ct: the column's owner in the accumulator is lane-group g/2,
-// its flat index f = 2 ct + g%2 among that lane-group's columns, token
-// g/2 + 4 (f / 3), digit f % 3 (d2, d1, d0).  A lane therefore serves one
-// token at 2 column tiles and two at 3: per token it requests its x values
-// 16t..16t+15 of the chunk's 4 groups together (one round trip to memory,
-// which under the weight stream is the prologue's cost), the four lanes of
-// a column share each group's exponent and sum through two shuffles, and the
-// digits go out as the two MMAs' B registers: even k to b0, odd k to b1.
+// the CTA's range starting at c0) into the shared-memory image.  Lane (g, t)
+// supplies B column g of every column tile ct: the column's owner in the
+// accumulator is lane-group g/2, its flat index f = 2 ct + g%2 among that
+// lane-group's columns, token g/2 + 4 (f / 3), digit f % 3 (d2, d1, d0).  A
+// lane therefore serves one token at 2 column tiles and two at 3.
 template <int CT>
 __device__ __forceinline__ void mt_build(const MtParams& p, unsigned char* img, int c0, int nch, const float* nf,
                                          int warp, int lane) {
@@ -141,89 +244,19 @@ __device__ __forceinline__ void mt_build(const MtParams& p, unsigned char* img, 
 #pragma unroll
         for (int sg = 0; sg < NSG; sg++) {
             const int j = (g >> 1) + 4 * sg;
-            const bool valid = j < p.m;
             float v[4][16];
-            if (!valid) {
-#pragma unroll
-                for (int u = 0; u < 4; u++)
-#pragma unroll
-                    for (int i = 0; i < 16; i++) v[u][i] = 0.0f;
-            } else if (p.x_bf16) {  // bf16 widens to fp32 exactly
-                uint4 r[4][2];
-#pragma unroll
-                for (int u = 0; u < 4; u++) {
-                    const uint4* src = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.x) +
-                                                                      (size_t)j * p.x_stride + kbase + 64 * u);
-                    r[u][0] = src[0];
-                    r[u][1] = src[1];
-                }
-#pragma unroll
-                for (int u = 0; u < 4; u++) {
-                    const uint32_t wv[8] = {r[u][0].x, r[u][0].y, r[u][0].z, r[u][0].w,
-                                            r[u][1].x, r[u][1].y, r[u][1].z, r[u][1].w};
-#pragma unroll
-                    for (int i = 0; i < 8; i++) {
-                        v[u][2 * i] = __uint_as_float(wv[i] << 16);
-                        v[u][2 * i + 1] = __uint_as_float(wv[i] & 0xFFFF0000u);
-                    }
-                }
-            } else {
-#pragma unroll
-                for (int u = 0; u < 4; u++) {
-                    const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(p.x) +
-                                                                        (size_t)j * p.x_stride + kbase + 64 * u);
-#pragma unroll
-                    for (int i = 0; i < 4; i++) {
-                        const float4 q = src[i];
-                        v[u][4 * i] = q.x;
-                        v[u][4 * i + 1] = q.y;
-                        v[u][4 * i + 2] = q.z;
-                        v[u][4 * i + 3] = q.w;
-                    }
-                }
-            }
+            mt_load_x(p, j, j < p.m, kbase, nf, v);
 #pragma unroll
             for (int u = 0; u < 4; u++) {
-                if (valid && !p.x_bf16 && p.norm_w) {
-                    const float4* nw = reinterpret_cast<const float4*>(p.norm_w + kbase + 64 * u);
-                    const float r = nf[j];
-#pragma unroll
-                    for (int i = 0; i < 4; i++) {
-                        const float4 q = nw[i];
-                        v[u][4 * i] = __fmul_rn(__fmul_rn(v[u][4 * i], r), q.x);
-                        v[u][4 * i + 1] = __fmul_rn(__fmul_rn(v[u][4 * i + 1], r), q.y);
-                        v[u][4 * i + 2] = __fmul_rn(__fmul_rn(v[u][4 * i + 2], r), q.z);
-                        v[u][4 * i + 3] = __fmul_rn(__fmul_rn(v[u][4 * i + 3], r), q.w);
-                    }
-                }
-                float amax = 0.0f, sum = 0.0f;
-#pragma unroll
-                for (int i = 0; i < 16; i++) {
-                    amax = fmaxf(amax, fabsf(v[u][i]));
-                    sum += v[u][i];
-                }
-                amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
-                amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
-                sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-                sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-                const int E = group_exponent(amax);
-                const float up = exp2i(kXBits - E);
+                int E;
+                float sum;
                 uint32_t dw[16];
-#pragma unroll
-                for (int i = 0; i < 16; i++) dw[i] = digits3(v[u][i], up);
+                mt_group(v[u], E, sum, dw);
 #pragma unroll
                 for (int ct = 0; ct < CT; ct++) {
                     const int f = 2 * ct + h;
-                    if (f / 3 != sg) continue;
-                    const int sh = 8 * (2 - f % 3);  // d2 is byte 2 of the digit word, d0 byte 0
-                    uint32_t d[16];
-#pragma unroll
-                    for (int i = 0; i < 16; i++) d[i] = (dw[i] >> sh) & 0xFFu;
-                    *reinterpret_cast<uint4*>(cimg + ct * 2048 + u * 512 + lane * 16) =
-                        make_uint4(d[0] | (d[2] << 8) | (d[4] << 16) | (d[6] << 24),
-                                   d[1] | (d[3] << 8) | (d[5] << 16) | (d[7] << 24),
-                                   d[8] | (d[10] << 8) | (d[12] << 16) | (d[14] << 24),
-                                   d[9] | (d[11] << 8) | (d[13] << 16) | (d[15] << 24));
+                    if (f / 3 == sg)
+                        *reinterpret_cast<uint4*>(cimg + ct * 2048 + u * 512 + lane * 16) = mt_frag(dw, f % 3);
                 }
                 // (2^(E-22), sum) of (group u, token j), from the lane of its d2 column
                 if (t == 0 && h == ((3 * sg) & 1))
@@ -231,14 +264,112 @@ __device__ __forceinline__ void mt_build(const MtParams& p, unsigned char* img, 
                         make_float2(exp2i(E - kXBits), sum);
             }
         }
-        // columns past the last token slot (2 column tiles: the lane-groups'
-        // fourth column) multiply zeros
+        // columns past the last token slot multiply zeros
 #pragma unroll
         for (int ct = 0; ct < CT; ct++) {
             if ((2 * ct + h) / 3 < NSG) continue;
 #pragma unroll
             for (int u = 0; u < 4; u++)
                 *reinterpret_cast<uint4*>(cimg + ct * 2048 + u * 512 + lane * 16) = make_uint4(0, 0, 0, 0);
+        }
+    }
+}
+
+// The same columns in registers, for a CTA whose k-range is at most 16
+// chunks (warp w's chunk is w): B[ct][u] the lane's B registers, M[sg][u]
+// the (2^(E-22), sum) of group u of token t + 4 sg -- the token this lane
+// accumulates, whose values lane 8t converted.  The two lanes of a token's
+// columns (g and g^1, lanes l and l^4) split its 16 values: lane g%2 = h
+// loads and converts values 8h..8h+7 of each group, the group's exponent
+// and sum take one more shuffle level, and the partners swap digit words.
+template <int CT>
+__device__ __forceinline__ void mt_build_reg(const MtParams& p, int c0, int nch, const float* nf, int warp, int lane,
+                                             uint4 (&B)[CT][4], float2 (&M)[mt_tokens(CT) / 4][4]) {
+    constexpr int NSG = mt_tokens(CT) / 4;
+    const int g = lane >> 2, t = lane & 3, h = g & 1;
+    const bool has = warp < nch;
+    const int kbase = (c0 + warp) * 256 + 16 * t + 8 * h;
+#pragma unroll
+    for (int ct = 0; ct < CT; ct++)
+#pragma unroll
+        for (int u = 0; u < 4; u++) B[ct][u] = make_uint4(0, 0, 0, 0);
+#pragma unroll
+    for (int sg = 0; sg < NSG; sg++) {
+        const int j = (g >> 1) + 4 * sg;
+        const bool valid = has && j < p.m;
+        float v[4][8];
+        if (!valid) {
+#pragma unroll
+            for (int u = 0; u < 4; u++)
+#pragma unroll
+                for (int i = 0; i < 8; i++) v[u][i] = 0.0f;
+        } else if (p.x_bf16) {  // bf16 widens to fp32 exactly
+            uint4 r[4];
+#pragma unroll
+            for (int u = 0; u < 4; u++)
+                r[u] = *reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.x) + (size_t)j * p.x_stride +
+                                                       kbase + 64 * u);
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const uint32_t wv[4] = {r[u].x, r[u].y, r[u].z, r[u].w};
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    v[u][2 * i] = __uint_as_float(wv[i] << 16);
+                    v[u][2 * i + 1] = __uint_as_float(wv[i] & 0xFFFF0000u);
+                }
+            }
+        } else {
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(p.x) +
+                                                                    (size_t)j * p.x_stride + kbase + 64 * u);
+                const float4 a = src[0], b = src[1];
+                v[u][0] = a.x; v[u][1] = a.y; v[u][2] = a.z; v[u][3] = a.w;
+                v[u][4] = b.x; v[u][5] = b.y; v[u][6] = b.z; v[u][7] = b.w;
+            }
+            if (p.norm_w) {
+                const float r = nf[j];
+#pragma unroll
+                for (int u = 0; u < 4; u++) {
+                    const float4* nw = reinterpret_cast<const float4*>(p.norm_w + kbase + 64 * u);
+                    const float4 a = nw[0], b = nw[1];
+                    const float wn[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+                    for (int i = 0; i < 8; i++) v[u][i] = __fmul_rn(__fmul_rn(v[u][i], r), wn[i]);
+                }
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            float amax = 0.0f, sum = 0.0f;
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                amax = fmaxf(amax, fabsf(v[u][i]));
+                sum += v[u][i];
+            }
+#pragma unroll
+            for (int o = 1; o <= 4; o <<= 1) {
+                amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+                sum += __shfl_xor_sync(0xffffffffu, sum, o);
+            }
+            const int E = group_exponent(amax);
+            const float up = exp2i(kXBits - E);
+            uint32_t dw[16];
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                const uint32_t own = digits3(v[u][i], up);
+                const uint32_t other = __shfl_xor_sync(0xffffffffu, own, 4);
+                dw[i] = h ? other : own;
+                dw[8 + i] = h ? own : other;
+            }
+#pragma unroll
+            for (int ct = 0; ct < CT; ct++) {
+                const int f = 2 * ct + h;
+                if (f / 3 == sg) B[ct][u] = mt_frag(dw, f % 3);
+            }
+            const float mx = __shfl_sync(0xffffffffu, exp2i(E - kXBits), 8 * t);
+            const float ms = __shfl_sync(0xffffffffu, sum, 8 * t);
+            M[sg][u] = make_float2(mx, ms);
         }
     }
 }
@@ -270,10 +401,12 @@ __device__ __forceinline__ MtLane mt_lane(int warp, int lane, int sg_shift, int 
     return L;
 }
 
-// One stage tile of this warp (16 rows x k-chunk `warp`) against the chunk
-// image `cimg`, accumulated into acc[sigma] = rows (g, g+8) of token t + 4 sigma.
-template <int CT>
-__device__ __forceinline__ void mt_tile(const unsigned char* st, const unsigned char* cimg, int warp, int lane,
+// One stage tile of this warp (16 rows x k-chunk `warp`) against its x
+// digits (registers B, M when REG, else the chunk image `cimg`), accumulated
+// into acc[sigma] = rows (g, g+8) of token t + 4 sigma.
+template <int CT, bool REG>
+__device__ __forceinline__ void mt_tile(const unsigned char* st, const unsigned char* cimg, const uint4 (&Br)[CT][4],
+                                        const float2 (&Mr)[mt_tokens(CT) / 4][4], int warp, int lane,
                                         const MtLane& L, float (&acc)[mt_tokens(CT) / 4][2]) {
     constexpr int NS = mt_tokens(CT) / 4;
     const int g = lane >> 2, t = lane & 3;
@@ -315,7 +448,7 @@ __device__ __forceinline__ void mt_tile(const unsigned char* st, const unsigned 
         int c[CT][4];
 #pragma unroll
         for (int ct = 0; ct < CT; ct++) {
-            const uint4 B = *reinterpret_cast<const uint4*>(cimg + ct * 2048 + u * 512 + lane * 16);
+            const uint4 B = REG ? Br[ct][u] : *reinterpret_cast<const uint4*>(cimg + ct * 2048 + u * 512 + lane * 16);
             mma_u8s8_16832_first(c[ct], e0, e1, o0, o1, B.x, B.y);
             mma_u8s8_16832(c[ct], e2, e3, o2, o3, B.z, B.w);
         }
@@ -323,7 +456,8 @@ __device__ __forceinline__ void mt_tile(const unsigned char* st, const unsigned 
         for (int sg = 0; sg < NS; sg++) {
             // columns 3 sg (d2), 3 sg + 1 (d1), 3 sg + 2 (d0) of this lane's flat list
             const int f2 = 3 * sg, f1 = 3 * sg + 1, f0 = 3 * sg + 2;
-            const float2 meta = *reinterpret_cast<const float2*>(cimg + CT * 2048 + (u * kMtMaxTok + t + 4 * sg) * 8);
+            const float2 meta =
+                REG ? Mr[sg][u] : *reinterpret_cast<const float2*>(cimg + CT * 2048 + (u * kMtMaxTok + t + 4 * sg) * 8);
             // dot = d2 2^16 + d1 2^8 + d0: the low two digits combined exactly in
             // 32 bits (|d1 sum| * 2^8 < 2^25), then one fp32 rounding
             const int lo0 = c[f1 >> 1][f1 & 1] * 256 + c[f0 >> 1][f0 & 1];
@@ -414,8 +548,6 @@ __global__ void __launch_bounds__(kStrThreads, 1)
     auto full_bar = [&](int s) { return bars + 8u * s; };
     auto empty_bar = [&](int s) { return bars + 8u * (R + s); };
     const uint32_t images_bar = bars + 8u * (2 * R);
-    auto pfull_bar = [&](int s) { return bars + 8u * (2 * R + 1 + s); };
-    auto pempty_bar = [&](int s) { return bars + 8u * (2 * R + 1 + kMtPartSlots + s); };
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int ks = p.ks;
@@ -477,18 +609,18 @@ __global__ void __launch_bounds__(kStrThreads, 1)
             mbar_init_nofence(empty_bar(s), kStrConsumers);
         }
         mbar_init_nofence(images_bar, kStrConsumers);
-        for (int s = 0; s < kMtPartSlots; s++) {
-            mbar_init_nofence(pfull_bar(s), kStrConsumers);
-            mbar_init_nofence(pempty_bar(s), kStrConsumers);
-        }
         mbar_init_fence();
+    }
+    __syncthreads();  // barriers initialised
+    pdl_launch_dependents();
+    // the first stages leave after the CTA barrier: the consumers start on
+    // their x digits meanwhile instead of waiting for the copies' issue
+    if (producer) {
         pol = l2_policy_evict_first();  // weights are read once
         if (p.weights_after_wait) pdl_wait();
         const int first = min(min(R, kMtEarlyStages), n_stages);
         for (int i = 0; i < first; i++) issue_stage();
     }
-    __syncthreads();  // barriers initialised
-    pdl_launch_dependents();
 
     bool ok = true;
     if (warp == kStrConsumers) {
@@ -513,47 +645,47 @@ __global__ void __launch_bounds__(kStrThreads, 1)
     } else {
         // ---- consumers (warps 0-15)
         constexpr int T = mt_tokens(CT), NS = T / 4;
+        constexpr bool kReg = mt_reg(CT);
         pdl_wait();  // x, norm weights, residual and the outputs follow the previous kernel
         if (!p.x_bf16 && p.norm_w) mt_norm_factors(p, red, nf, warp, lane);
-        mt_build<CT>(p, img, c0, nch, nf, warp, lane);
+        uint4 Breg[CT][4];
+        float2 Mreg[NS][4];
+        if (kReg)
+            mt_build_reg<CT>(p, c0, nch, nf, warp, lane, Breg, Mreg);
+        else
+            mt_build<CT>(p, img, c0, nch, nf, warp, lane);
         __syncwarp();
         if (lane == 0) mbar_arrive(images_bar);
         const MtLane ML = mt_lane(warp, lane, p.sg_shift, sb_row, sb_mask);
         int slot = 0;
         uint32_t phase = 0;
         const int g = lane >> 2, t = lane & 3;
-        // every warp sums a share of strip si's partial slot over the 16 warps:
-        // rows (warp % 8, warp % 8 + 8) x the T/2 tokens of half warp / 8, T
-        // values.  Lane l takes value l % T of the warps l / T + 32 / T * i
-        // (i < T / 2, in order), then a fixed xor tree over the lane groups;
-        // lanes 0..T/2-1 end with (row warp % 8, row + 8) of one token each.
-        // The slot's barriers are polled, not slept on: they complete within
-        // a stage.
-        const int rg = warp & 7, th = warp >> 3;
-        const int lv = lane % T, lw = lane / T;
-        const int lrow = rg + 8 * (lv / (T / 2)), ltok = th * (T / 2) + lv % (T / 2);
-        auto reduce = [&](int si) {
-            const int ps = si % kMtPartSlots;
-            const uint32_t use = (uint32_t)(si / kMtPartSlots);
-            if (ok && !mbar_wait_spin(pfull_bar(ps), use & 1u, kStrWaitNs)) ok = false;
-            float y = 0.0f;
-            if (ok) {
-                const float* src = part + (size_t)ps * kStrConsumers * 16 * T + lrow * T + ltok;
+        constexpr int NB = mt_batch(T);
+        // a batch of strips' per-warp sums [strip % NB][warp][16 rows][T] is
+        // added over the 16 warps in warp order by all consumer threads, one
+        // (strip, row pair, token) each; named barrier 1 before (every warp
+        // has parked its sums) and after (the slots may be reused)
+        auto flush = [&](int si_last, int nb) {
+            asm volatile("bar.sync 1, 512;" ::: "memory");
+            const int tid = warp * 32 + lane;
+            for (int u = tid; u < nb * 8 * T; u += kStrConsumers * 32) {
+                const int bi = u / (8 * T), gg = (u / T) % 8, j = u % T;
+                const float* src = part + (size_t)bi * kStrConsumers * 16 * T + gg * T + j;
+                float y0 = 0.0f, y1 = 0.0f;
 #pragma unroll
-                for (int i = 0; i < T / 2; i++) y += src[(size_t)(lw + (32 / T) * i) * 16 * T];
+                for (int w = 0; w < kStrConsumers; w++) {
+                    y0 += src[(size_t)w * 16 * T];
+                    y1 += src[(size_t)w * 16 * T + 8 * T];
+                }
+                const int si = si_last - (nb - 1) + bi;
+                if (ks == 1) {
+                    if (ok && j < p.m) mt_store(p, s0 + si, gg, j, y0, y1);
+                } else {
+                    res[((size_t)si * 16 + gg) * T + j] = y0;
+                    res[((size_t)si * 16 + gg + 8) * T + j] = y1;
+                }
             }
-#pragma unroll
-            for (int o = T; o < 32; o <<= 1) y += __shfl_xor_sync(0xffffffffu, y, o);
-            __syncwarp();
-            if (ok && lane == 0) mbar_arrive(pempty_bar(ps));
-            const float y1 = __shfl_down_sync(0xffffffffu, y, T / 2);  // row + 8 of the same token
-            const bool mine = lane < T / 2;
-            if (ks == 1) {
-                if (ok && mine && ltok < p.m) mt_store(p, s0 + si, rg, ltok, y, y1);
-            } else if (mine) {
-                res[((size_t)si * 16 + rg) * T + ltok] = y;
-                res[((size_t)si * 16 + rg + 8) * T + ltok] = y1;
-            }
+            asm volatile("bar.sync 1, 512;" ::: "memory");
         };
         for (int si = 0; si < ns; si++) {
             float acc[NS][2];
@@ -563,8 +695,8 @@ __global__ void __launch_bounds__(kStrThreads, 1)
                 if (ok && !mbar_wait_tries(full_bar(slot), phase, kStrTryHintNs, kStrTries)) ok = false;
                 const int lc = kb * kStrKc + warp;
                 if (ok && lc < nch)
-                    mt_tile<CT>(base + (size_t)slot * kStrStageBytes, img + (size_t)lc * mt_img_bytes(CT), warp,
-                                lane, ML, acc);
+                    mt_tile<CT, kReg>(base + (size_t)slot * kStrStageBytes, img + (size_t)lc * mt_img_bytes(CT),
+                                      Breg, Mreg, warp, lane, ML, acc);
                 __syncwarp();
                 // a slot whose copy never arrived is not handed back
                 if (ok && lane == 0) mbar_arrive(empty_bar(slot));
@@ -573,24 +705,15 @@ __global__ void __launch_bounds__(kStrThreads, 1)
                     phase ^= 1u;
                 }
             }
-            // park the strip's tile in its partial slot once the strip that
-            // used the slot before has been summed
-            const int ps = si % kMtPartSlots;
-            const uint32_t use = (uint32_t)(si / kMtPartSlots);
-            if (ok && use > 0 && !mbar_wait_spin(pempty_bar(ps), (use - 1) & 1u, kStrWaitNs)) ok = false;
-            if (ok) {
-                float* dst = part + ((size_t)ps * kStrConsumers + warp) * 16 * T;
+            // park the strip's sums; every NB strips (and at the end) the batch is added up
+            float* dst = part + ((size_t)(si % NB) * kStrConsumers + warp) * 16 * T;
 #pragma unroll
-                for (int sg = 0; sg < NS; sg++) {
-                    dst[g * T + t + 4 * sg] = acc[sg][0];
-                    dst[(g + 8) * T + t + 4 * sg] = acc[sg][1];
-                }
+            for (int sg = 0; sg < NS; sg++) {
+                dst[g * T + t + 4 * sg] = acc[sg][0];
+                dst[(g + 8) * T + t + 4 * sg] = acc[sg][1];
             }
-            __syncwarp();
-            if (ok && lane == 0) mbar_arrive(pfull_bar(ps));
-            if (si > 0) reduce(si - 1);
+            if (si % NB == NB - 1 || si == ns - 1) flush(si, si % NB + 1);
         }
-        if (ns > 0) reduce(ns - 1);
         if (!ok && lane == 0 && p.status) atomicOr(p.status, 1);
     }
 
@@ -718,6 +841,7 @@ static bool mt_plan(int n_out, int n_in, int m, int sg_shift, MtPlan& pl) {
         L.ring = kMtMaxRing;
         while (L.ring > 3 && L.bytes() > kMtSmemTarget) L.ring--;
         if (L.bytes() > kMtSmemTarget) continue;
+        if (mt_reg(pl.ct) && L.nch_max > kStrKc) continue;  // one chunk per warp
         if (ks > 1) {
             const int cap = caps.capacity(kern, kStrThreads, L.bytes(), (int)kMtSmemTarget, ks);
             if (cap <= 0) continue;

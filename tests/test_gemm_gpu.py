@@ -77,7 +77,8 @@ SHAPES = [
     (3584, 18944, 4, 64, "bf16"),
     (4608, 3584, 48, 256, "f32"),
     (3584, 3584, 128, 64, "f32"),
-    (1024, 2048, 6, 64, "f32"),           # register path, hi/lo tokens
+    (1024, 2048, 6, 64, "f32"),           # multi-token kernel, fp32 x
+    (1024, 2048, 12, 64, "bf16"),         # register path
     (2048, 4096, 32, 64, "bf16"),         # tcgen05 path, 32 tokens
     (3584, 18944, 7, 128, "f32"),         # register path, K split, gs 128
     (18944, 3584, 1, 64, "bf16"),         # one token: the streaming GEMV

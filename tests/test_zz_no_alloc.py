@@ -38,7 +38,7 @@ def _static(lib, dw, ds, db, x, gs, out, row_add=None, residual=None):
 CASES = [
     # n_out, n_in, m, gs, x dtype, fused epilogue
     (2048, 1024, 200, 64, "bf16", False),    # tcgen05 kernel
-    (1024, 2048, 6, 64, "f32", True),        # register-path kernel, bias + residual
+    (1024, 2048, 12, 64, "bf16", True),      # register-path kernel, bias + residual
     (3584, 18944, 256, 64, "bf16", False),   # down shape, K split, 9.25 MiB of scratch
     (640, 1536, 24, 128, "bf16", True),
 ]
