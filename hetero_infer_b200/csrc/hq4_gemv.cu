@@ -861,7 +861,7 @@ int gemv_launch_stage(const uint32_t* w, const uint16_t* scales, const uint16_t*
 int check_device_cap() { return check_device(); }
 
 // Two or more fp32 tokens through the multi-token streaming kernel (passes
-// of up to 8 tokens); *used is false when the shape or pointers do not suit
+// of up to 4 tokens); *used is false when the shape or pointers do not suit
 // it.
 static int gemv_tokens_mt(const uint32_t* w, const uint16_t* sc, const uint16_t* bi, const float* x, float* out,
                           int n_out, int n_in, int gs, int m, const float* row_add, const float* residual,

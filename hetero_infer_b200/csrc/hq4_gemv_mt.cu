@@ -930,13 +930,17 @@ bool gemv_mt_fits(int n_out, int n_in, int gs, int m) {
     return m > 0 && m <= kMtMaxTok && mt_shape_ok(n_out, n_in, gs, &sgs) && mt_plan(n_out, n_in, m, sgs, pl);
 }
 
+// Passes of 4 tokens (the register path): a prompt's passes read the
+// weights more often than 8-token passes would, but each runs faster
+// (measured 16.7 against 17.8 ms time to first token on the 7B-shape model).
 int gemv_mt_tokens(MtParams prm, int gs, int m_total, cudaStream_t st, bool* used) {
     *used = false;
-    if (m_total <= 0 || !gemv_mt_fits(prm.n_out, prm.n_in, gs, std::min(m_total, kMtMaxTok))) return HQ4_OK;
+    constexpr int per = mt_tokens(2);
+    if (m_total <= 0 || !gemv_mt_fits(prm.n_out, prm.n_in, gs, std::min(m_total, per))) return HQ4_OK;
     const size_t xe = prm.x_bf16 ? 2 : 4;  // bytes per x element
-    for (int t0 = 0; t0 < m_total; t0 += kMtMaxTok) {
+    for (int t0 = 0; t0 < m_total; t0 += per) {
         MtParams q = prm;
-        q.m = std::min(kMtMaxTok, m_total - t0);
+        q.m = std::min(per, m_total - t0);
         q.x = static_cast<const unsigned char*>(prm.x) + (size_t)t0 * prm.x_stride * xe;
         q.out = prm.out ? prm.out + (size_t)t0 * prm.out_stride : nullptr;
         q.residual = prm.residual ? prm.residual + (size_t)t0 * prm.out_stride : nullptr;

@@ -53,8 +53,8 @@ __host__ __device__ inline int mt_chunk_start(int r, int ks, int n_chunks, int a
 // One pass of up to kMtMaxTok tokens; *used is false when the shape or
 // pointers do not suit it (nothing was launched).
 int gemv_mt_pass(MtParams prm, int gs, cudaStream_t st, bool* used);
-// All m_total tokens in passes of up to kMtMaxTok; *used false when the shape
-// does not suit.
+// All m_total tokens in passes of up to 4; *used false when the shape does
+// not suit.
 int gemv_mt_tokens(MtParams prm, int gs, int m_total, cudaStream_t st, bool* used);
 // Whether a pass of m tokens of this shape runs on the multi-token kernel.
 bool gemv_mt_fits(int n_out, int n_in, int gs, int m);

@@ -739,7 +739,7 @@ extern "C" int hq4_gemv_norm(const uint32_t* w, const uint16_t* scales, const ui
     if (m <= 0 || (silu_mul && n_out % 16)) return HQ4_ERR_SHAPE;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     const int n_store = silu_mul ? n_out / 2 : n_out;
-    if (m >= 2) {  // a prompt: the multi-token kernel, passes of up to 8 tokens
+    if (m >= 2) {  // a prompt: the multi-token kernel, passes of up to 4 tokens
         MtParams mp = {};
         mp.w = w;
         mp.sc = scales;
@@ -781,7 +781,7 @@ extern "C" int hq4_qkv_rope(const uint32_t* w, const uint16_t* scales, const uin
     const int half = head_dim / 2;
     const int q_strips = n_heads * half / 8, k_strips = n_kv * half / 8;
     const int n_out = (n_heads + 2 * n_kv) * head_dim;
-    if (m >= 2) {  // a prompt: the multi-token kernel, passes of up to 8 tokens
+    if (m >= 2) {  // a prompt: the multi-token kernel, passes of up to 4 tokens
         MtParams mp = {};
         mp.w = w;
         mp.sc = scales;
