@@ -16,7 +16,11 @@ and the transport is NCCL over NVLink:
 * the vocabulary projection is row-sharded over all stages: the last stage's
   fp32 hidden state is broadcast, every rank computes V/N logits and their
   (max, first index), and an 8-byte-per-rank all-gather picks the token with
-  numpy's argmax rule (largest value, lowest index);
+  numpy's argmax rule (largest value, lowest index).  On GPUs these run on a
+  side stream over a second communicator, so the collectives join the ranks
+  off the layers' critical path: the next tick's send/recv and layers go
+  ahead, and only rank 0, when it feeds a stream's token back in (one tick
+  later at the earliest), waits for that stream's head;
 * microbatches are independent requests with their own KV caches.  Rank 0
   admits, each tick, the next microbatch (round robin) whose previous token is
   known; stage i works on what rank 0 admitted i ticks earlier.  The schedule
@@ -61,11 +65,24 @@ def admission_schedule(n_micro: int, n_steps: int, n_stages: int) -> List[int]:
     return out
 
 
+_SIDE_GROUPS: Dict[int, object] = {}
+
+
 class Comm:
     """The few torch.distributed operations the pipeline uses."""
 
     def __init__(self, rank: int, world: int, device: torch.device, group=None):
         self.rank, self.world, self.device, self.group = rank, world, device, group
+
+    def side(self) -> "Comm":
+        """The same ranks over a second communicator (created once per base
+        group, on every rank in the same order), for collectives issued on
+        another CUDA stream: NCCL orders the operations of one communicator,
+        so two streams must not share one."""
+        key = id(self.group)
+        if key not in _SIDE_GROUPS:
+            _SIDE_GROUPS[key] = dist.new_group(list(range(self.world)))
+        return Comm(self.rank, self.world, self.device, group=_SIDE_GROUPS[key])
 
     def exchange(self, send: Optional[torch.Tensor], recv: Optional[torch.Tensor]) -> None:
         """Send to rank+1 and/or receive from rank-1 as one group."""
@@ -129,10 +146,20 @@ class PipelineRank:
             self.count = [0] * n_micro
         else:
             self._tokens: List[List[int]] = [[] for _ in range(n_micro)]
+        # device compute over several GPUs: the head on a side stream and
+        # communicator; tok_ev[m] marks stream m's latest token in the history
+        self.async_head = self.on_device and comm.world > 1
+        if self.async_head:
+            self.hcomm = comm.side()
+            self.hstream = torch.cuda.Stream(comm.device)
+            self.hbuf = torch.empty((n_micro, compute.hidden_dim), dtype=torch.float32, device=comm.device)
+            self.tok_ev: List[Optional[torch.cuda.Event]] = [None] * n_micro
 
     @property
     def tokens(self) -> List[List[int]]:
         if self.on_device:
+            if self.async_head:
+                torch.cuda.current_stream(self.comm.device).wait_stream(self.hstream)
             h = self.hist.cpu().numpy()
             return [[int(v) for v in h[m, :self.count[m]]] for m in range(self.n_micro)]
         return self._tokens
@@ -161,6 +188,8 @@ class PipelineRank:
         all-gather of (max, index) -> the token of microbatch m (identical on
         every rank).  Device compute: the token goes straight into the device
         history; host compute: returned as an int."""
+        if self.async_head:
+            return self._head_side(h_last, m)
         H = self.c.hidden_dim
         buf = self.c.to_comm32(h_last) if self.last else torch.empty(H, dtype=torch.float32,
                                                                         device=self.comm.device)
@@ -172,6 +201,29 @@ class PipelineRank:
         val, idx = self.c.head(buf)
         pair = torch.tensor([val, float(idx)], dtype=torch.float64, device=self.comm.device)
         return pick_token(self.comm.all_gather(pair))
+
+    def _head_side(self, h_last, m: int) -> None:
+        """_head on the side stream: after this rank's work so far on the main
+        stream (the last stage's final hidden row), the broadcast, this rank's
+        shard and its pick, the all-gather, and the token into the history;
+        tok_ev[m] records its completion.  hbuf[m] is stream m's own buffer and
+        the side stream runs the heads in order, so no head overwrites what an
+        earlier one still reads."""
+        main = torch.cuda.current_stream(self.comm.device)
+        ready = torch.cuda.Event()
+        ready.record(main)
+        buf = self.hbuf[m]
+        with torch.cuda.stream(self.hstream):
+            self.hstream.wait_event(ready)
+            if self.last:
+                buf.copy_(self.c.to_comm32(h_last))
+            self.hcomm.broadcast(buf, self.comm.world - 1)
+            pairs = self.hcomm.all_gather(self.c.head_pair(buf))
+            self.c.pick_into(pairs, self.comm.world, self.hist[m], self.count[m])
+            done = torch.cuda.Event()
+            done.record(self.hstream)
+        self.tok_ev[m] = done
+        return None
 
     def prefill(self, prompts: Sequence[np.ndarray]) -> None:
         """Each prompt [1, P] through the stages one after another; the first
@@ -211,6 +263,8 @@ class PipelineRank:
             out_prev = None
             h = None
             if mine >= 0:
+                if self.first and self.async_head and self.tok_ev[mine] is not None:
+                    torch.cuda.current_stream(self.comm.device).wait_event(self.tok_ev[mine])
                 src = self._last_token(mine) if self.first else recv
                 wire, h = self.c.decode_tick(mine, self.caches[mine], src, self.first, self.last)
                 if not self.last:
