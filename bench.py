@@ -744,9 +744,9 @@ def profile_case(which: str) -> None:
       layer   the four GEMV launches of a Qwen2-7B-shape layer at batch 1
               (q|k|v 4608x3584, o 3584x3584, gate|up 37888x3584, down
               3584x18944), three rounds over two weight copies;
-      gemm    hq4_gemm_w4a16 on 18944x3584 at 16 tokens (register-path
-              kernel) and 256 tokens (tcgen05 kernel), bf16 activations,
-              three calls each;
+      gemm    hq4_gemm_w4a16 on 18944x3584 at 4 tokens (multi-token
+              streaming kernel), 16 tokens (register-path kernel) and 256
+              tokens (tcgen05 kernel), bf16 activations, three calls each;
       decode  the 7B-shape stage's decode step, per-layer launches, 4 steps
               after a 4-token prompt.
 
@@ -775,7 +775,7 @@ def profile_case(which: str) -> None:
     elif which == "gemm":
         n, k = 18944, 3584
         w, s_, b = q4(n, k)
-        for m in (16, 256):
+        for m in (4, 16, 256):
             x = torch.randn(m, k, device=dev, generator=g).to(torch.bfloat16)
             for _ in range(3):
                 ops.q4_gemm(w, s_, b, x, GS)
