@@ -545,9 +545,11 @@ def cpu_decode_baseline(cfg, w, budget_s: float, prompt_len: int = 4):
 def pipeline_suite(rank: int, world: int, dev, n_tokens: int = 256, prompt_len: int = 32):
     """Benchmark config 5: the 7B-shape random model split by the planner over
     the `world` GPUs, hidden states handed on by NCCL send/recv, the lm_head
-    row-sharded over all ranks, 4 and 8 independent streams in flight,
-    `n_tokens` per stream; the reference's fp16 wire (4 and 8 streams) and its
-    int8 codec (8 streams).  Aggregate decode tok/s: wall clock between two
+    row-sharded over all ranks (on a side stream), 4 and 8 independent
+    streams in flight, `n_tokens` per stream; the reference's fp16 wire (4 and
+    8 streams) and its int8 codec (8 streams).  Every decode tick is a CUDA-
+    graph replay per rank (send/recv and the stage's layers) plus one per
+    finished stream's head.  Aggregate decode tok/s: wall clock between two
     device synchronisations around the decode, max over ranks.
 
     Roofline: every generated token streams the whole model's weights once
@@ -582,6 +584,7 @@ def pipeline_suite(rank: int, world: int, dev, n_tokens: int = 256, prompt_len: 
         pr.decode(n_tok - 1)
         torch.cuda.synchronize(dev)
         dt = time.perf_counter() - t0
+        pr.close()  # its graphs hold NCCL calls: released before the process group goes
         t = torch.tensor([dt], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return pr, float(t.item())

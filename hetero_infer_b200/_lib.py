@@ -46,6 +46,7 @@ SIGNATURES = {
     "hq4_synth_embed_f16": (_I, [ctypes.c_longlong, _I, _I, _F, _P, _P]),
     "hq4_argmax_pair": (_I, [_P, _I, _I, _P, _P]),
     "hq4_pick_token": (_I, [_P, _I, _P, _P, _I, _P]),
+    "hq4_pick_token_next": (_I, [_P, _I, _P, _P, _P, _I, _P]),
     "hq4_advance_position": (_I, [_P, _I, _P]),
     "hq4_decode_plan_create": (_I, [_P] + [_I] * 7 + [_F, _F, _P, _P, _I] + [_P] * 6),
     "hq4_decode_plan_run": (_I, [_P, _P]),

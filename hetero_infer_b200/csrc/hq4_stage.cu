@@ -368,7 +368,7 @@ __global__ void __launch_bounds__(kArgmaxThreads) argmax_cluster_kernel(
 // value, lowest index among equals).  Optionally also recorded in
 // history[slot].
 __global__ void pick_token_kernel(const int* __restrict__ pairs, int world, int* __restrict__ tok,
-                                  int* __restrict__ history, int slot) {
+                                  int* __restrict__ history, int slot, int* __restrict__ count, int hist_len) {
     pdl_launch_dependents();
     pdl_wait();
     if (threadIdx.x != 0) return;
@@ -383,7 +383,13 @@ __global__ void pick_token_kernel(const int* __restrict__ pairs, int world, int*
         }
     }
     *tok = bidx;
-    if (history) history[slot] = bidx;
+    if (count) {  // the slot is the device counter, which advances (a full history drops the token)
+        const int s = *count;
+        if (history && s >= 0 && s < hist_len) history[s] = bidx;
+        *count = s + 1;
+    } else if (history) {
+        history[slot] = bidx;
+    }
 }
 
 __global__ void advance_kernel(int* pos, int delta) {
@@ -723,7 +729,15 @@ extern "C" int hq4_pick_token(const int* pairs, int world, int* tok, int* histor
     if (int rc = check_device_cap()) return rc;
     if (world <= 0 || !tok || (history && slot < 0)) return HQ4_ERR_SHAPE;
     return launch_pdl(pick_token_kernel, dim3(1), dim3(32), 0, static_cast<cudaStream_t>(stream), pairs, world, tok,
-                      history, slot);
+                      history, slot, (int*)nullptr, 0);
+}
+
+extern "C" int hq4_pick_token_next(const int* pairs, int world, int* tok, int* history, int* count, int hist_len,
+                                   void* stream) {
+    if (int rc = check_device_cap()) return rc;
+    if (world <= 0 || !tok || !count || hist_len < 0) return HQ4_ERR_SHAPE;
+    return launch_pdl(pick_token_kernel, dim3(1), dim3(32), 0, static_cast<cudaStream_t>(stream), pairs, world, tok,
+                      history, 0, count, hist_len);
 }
 
 extern "C" int hq4_advance_position(int* pos, int delta, void* stream) {

@@ -98,6 +98,10 @@ class Comm:
     def broadcast(self, t: torch.Tensor, src: int) -> None:
         dist.broadcast(t, src, group=self.group)
 
+    def all_gather_into(self, out: torch.Tensor, t: torch.Tensor) -> None:
+        """all_gather into a caller buffer [world, *t.shape] (NCCL)."""
+        dist.all_gather_into_tensor(out, t, group=self.group)
+
     def all_gather(self, t: torch.Tensor) -> torch.Tensor:
         if dist.get_backend(self.group) == "nccl":
             out = torch.empty((self.world,) + tuple(t.shape), dtype=t.dtype, device=t.device)
@@ -134,7 +138,7 @@ class PipelineRank:
       head(h32) -> (max value, global index) of this rank's vocabulary shard.
     """
 
-    def __init__(self, comm: Comm, compute, n_micro: int, max_tokens: int = 4096):
+    def __init__(self, comm: Comm, compute, n_micro: int, max_tokens: int = 4096, graphs: bool = True):
         self.comm, self.c, self.n_micro = comm, compute, n_micro
         self.caches = [compute.new_cache() for _ in range(n_micro)]
         self.ticks = 0
@@ -150,10 +154,21 @@ class PipelineRank:
         # communicator; tok_ev[m] marks stream m's latest token in the history
         self.async_head = self.on_device and comm.world > 1
         if self.async_head:
+            dev = comm.device
             self.hcomm = comm.side()
-            self.hstream = torch.cuda.Stream(comm.device)
-            self.hbuf = torch.empty((n_micro, compute.hidden_dim), dtype=torch.float32, device=comm.device)
+            self.hstream = torch.cuda.Stream(dev)
+            self.hbuf = torch.empty((n_micro, compute.hidden_dim), dtype=torch.float32, device=dev)
             self.tok_ev: List[Optional[torch.cuda.Event]] = [None] * n_micro
+            # the token of stream m goes to tokdst[m] (on rank 0 the input
+            # buffer of m's step) and to hist[m][cnt[m]] (device counter)
+            self.cnt = torch.zeros(n_micro, dtype=torch.int32, device=dev)
+            self.gat = torch.empty((comm.world, 2), dtype=torch.int32, device=dev)
+            self.tokdst = ([compute.statics(m, True, self.last)[0] for m in range(n_micro)] if self.first else
+                           [t for t in torch.zeros((n_micro, 1), dtype=torch.int32, device=dev)])
+        # decode ticks replayed from CUDA graphs (device compute, several GPUs)
+        self.graphs = graphs and self.async_head
+        self._tick_g: Dict[tuple, torch.cuda.CUDAGraph] = {}
+        self._head_g: Dict[int, torch.cuda.CUDAGraph] = {}
 
     @property
     def tokens(self) -> List[List[int]]:
@@ -202,28 +217,111 @@ class PipelineRank:
         pair = torch.tensor([val, float(idx)], dtype=torch.float64, device=self.comm.device)
         return pick_token(self.comm.all_gather(pair))
 
+    def close(self) -> None:
+        """Drop the CUDA graphs that hold NCCL calls (before the process group
+        is destroyed, which would otherwise wait for them)."""
+        self._tick_g = {}
+        self._head_g = {}
+
+    def _head_ops(self, m: int, h_last=None) -> None:
+        """The head of stream m on the current (side) stream: the final row
+        into hbuf[m] (last rank), broadcast, this rank's shard and its pick,
+        all-gather, the global pick into tokdst[m] and hist[m][cnt[m]]."""
+        buf = self.hbuf[m]
+        if self.last:
+            src = h_last if h_last is not None else self.c.statics(m, self.first, True)[2]
+            buf.copy_(self.c.to_comm32(src))
+        self.hcomm.broadcast(buf, self.comm.world - 1)
+        self.hcomm.all_gather_into(self.gat, self.c.head_pair(buf))
+        self.c.pick_next(self.gat, self.comm.world, self.tokdst[m], self.hist[m], self.cnt[m:m + 1])
+
     def _head_side(self, h_last, m: int) -> None:
         """_head on the side stream: after this rank's work so far on the main
-        stream (the last stage's final hidden row), the broadcast, this rank's
-        shard and its pick, the all-gather, and the token into the history;
+        stream (the last stage's final hidden row), the head of stream m;
         tok_ev[m] records its completion.  hbuf[m] is stream m's own buffer and
         the side stream runs the heads in order, so no head overwrites what an
-        earlier one still reads."""
+        earlier one still reads.  Within graph-replayed decode the head is a
+        graph of its own per stream, captured on its first use."""
         main = torch.cuda.current_stream(self.comm.device)
         ready = torch.cuda.Event()
         ready.record(main)
-        buf = self.hbuf[m]
         with torch.cuda.stream(self.hstream):
             self.hstream.wait_event(ready)
-            if self.last:
-                buf.copy_(self.c.to_comm32(h_last))
-            self.hcomm.broadcast(buf, self.comm.world - 1)
-            pairs = self.hcomm.all_gather(self.c.head_pair(buf))
-            self.c.pick_into(pairs, self.comm.world, self.hist[m], self.count[m])
+            if h_last is None and self.graphs:
+                g = self._head_g.get(m)
+                if g is None:
+                    g = torch.cuda.CUDAGraph()
+                    with torch.cuda.graph(g, stream=self.hstream, capture_error_mode="thread_local"):
+                        self._head_ops(m)
+                    self._head_g[m] = g
+                g.replay()
+            else:
+                self._head_ops(m, h_last)
             done = torch.cuda.Event()
             done.record(self.hstream)
         self.tok_ev[m] = done
         return None
+
+    def _tick_ops(self, send: int, mine: int) -> None:
+        """One tick of this rank on the current stream: send stream `send`'s
+        wire output to rank+1 and receive stream `mine`'s input from rank-1 (one
+        group), then `mine`'s step."""
+        c, r = self.c, self.comm.rank
+        ops = []
+        if send >= 0:
+            ops.append(dist.P2POp(dist.isend, c.statics(send, self.first, self.last)[1], r + 1,
+                                  group=self.comm.group))
+        if mine >= 0 and r > 0:
+            ops.append(dist.P2POp(dist.irecv, c.statics(mine, self.first, self.last)[0], r - 1,
+                                  group=self.comm.group))
+        if ops:
+            for w in dist.batch_isend_irecv(ops):
+                w.wait()
+        if mine >= 0:
+            c.record_step(mine, self.caches[mine], self.first, self.last)
+
+    def _decode_graphed(self, n_steps: int) -> None:
+        """decode() with every tick one CUDA-graph replay per rank (its
+        send/recv and step, captured the first time each (send, receive)
+        pair occurs) and each finished stream's head one more on the side
+        stream: the host issues a few graph launches per tick instead of the
+        tick's dozens of launches and NCCL calls.  Rank 0 waits for a
+        stream's head (its token is written into the step's input buffer)
+        before that stream's next step."""
+        W, r = self.comm.world, self.comm.rank
+        main = torch.cuda.current_stream(self.comm.device)
+        adm = admission_schedule(self.n_micro, n_steps, W)
+        n_ticks = len(adm) + W - 1
+        prev = -1
+        for t in range(n_ticks):
+            mine = adm[t - r] if 0 <= t - r < len(adm) else -1
+            send = -1 if self.last else prev
+            if mine >= 0:
+                cache = self.caches[mine]
+                if cache.offset + 1 > cache.max_ctx:
+                    raise ValueError(f"context {cache.offset + 1} exceeds max_ctx {cache.max_ctx}")
+                if self.first and self.tok_ev[mine] is not None:
+                    main.wait_event(self.tok_ev[mine])
+            if mine >= 0 or send >= 0:
+                key = (send, mine)
+                g = self._tick_g.get(key)
+                if g is None:  # captured on a side stream (the default stream cannot capture)
+                    cap = torch.cuda.Stream(self.comm.device)
+                    cap.wait_stream(main)
+                    g = torch.cuda.CUDAGraph()
+                    with torch.cuda.graph(g, stream=cap, capture_error_mode="thread_local"):
+                        self._tick_ops(send, mine)
+                    main.wait_stream(cap)
+                    self._tick_g[key] = g
+                g.replay()
+                if mine >= 0:
+                    self.caches[mine].offset += 1  # the graph advanced the device position
+            done = adm[t - (W - 1)] if 0 <= t - (W - 1) < len(adm) else -1
+            if done >= 0:
+                self._head_side(None, done)
+                self._record(done, None)
+            prev = mine
+        self.ticks += n_ticks
 
     def prefill(self, prompts: Sequence[np.ndarray]) -> None:
         """Each prompt [1, P] through the stages one after another; the first
@@ -247,6 +345,8 @@ class PipelineRank:
 
     def decode(self, n_steps: int) -> None:
         """n_steps more tokens for every microbatch, pipelined."""
+        if self.graphs:
+            return self._decode_graphed(n_steps)
         W, r = self.comm.world, self.comm.rank
         adm = admission_schedule(self.n_micro, n_steps, W)
         n_ticks = len(adm) + W - 1
@@ -319,6 +419,7 @@ class DeviceCompute:
         self.pair = torch.empty(2, dtype=torch.int32, device=device)
         self.tok = torch.empty(1, dtype=torch.int32, device=device)
         self._graphs = {}
+        self._static = {}
         self.lib = _lib.load()
         self._check = _lib.check
 
@@ -326,9 +427,41 @@ class DeviceCompute:
         return self.stage.new_caches()
 
     def release_graphs(self) -> None:
-        """Drop the per-microbatch decode graphs (they are bound to the caches
-        of the runner that captured them); a new runner captures its own."""
+        """Drop the per-microbatch decode graphs and their buffers (they are
+        bound to the caches of the runner that captured them); a new runner
+        captures its own."""
         self._graphs = {}
+        self._static = {}
+
+    def statics(self, m, first: bool, last: bool):
+        """Microbatch m's fixed step buffers on this stage, created once: the
+        input (a token id on the first stage, else a wire frame), the wire
+        output (none on the last stage) and the final hidden row."""
+        sb = self._static.get(m)
+        if sb is None:
+            static_in = (torch.zeros((1, 1), dtype=torch.int32, device=self.device) if first
+                         else self.wire_empty(1).zero_())
+            static_wire = None if last else self.wire_empty(1)
+            static_h = torch.empty((1, 1, self.hidden_dim), dtype=torch.float32, device=self.device)
+            sb = self._static[m] = (static_in, static_wire, static_h)
+        return sb
+
+    def record_step(self, m, cache, first: bool, last: bool) -> None:
+        """Microbatch m's decode step on the current stream, from its input
+        buffer to its wire output and final row (eagerly or into a capture):
+        embedding or wire decode, the stage's layers, the position advance."""
+        st = self.stage
+        H = self.hidden_dim
+        static_in, static_wire, static_h = self.statics(m, first, last)
+        h = st.embed(static_in) if first else self.from_wire(static_in)
+        h = h.reshape(1, H).contiguous()
+        for i in range(len(st.layers)):
+            st.layer_forward(i, h, cache, 1)
+        if len(st.layers):
+            st._check(st.lib.hq4_advance_position(cache.pos.data_ptr(), 1, st._stream()), "hq4_advance_position")
+        if static_wire is not None:
+            self._encode_into(h, static_wire)
+        static_h.copy_(h.view(1, 1, H))
 
     def embed_forward(self, ids, cache):
         return self.stage(ids, cache, apply_head=False)
@@ -346,7 +479,7 @@ class DeviceCompute:
         g = self._graphs.get(m)
         if g is None:
             h = self.embed_forward(src, cache) if first else self.forward(self.from_wire(src), cache)
-            self._graphs[m] = self._capture(cache, first, last)
+            self._graphs[m] = self._capture(m, cache, first, last)
             return (None if last else self.to_wire(h)), h
         static_in, static_wire, static_h, graph = g
         if cache.offset + 1 > cache.max_ctx:
@@ -356,27 +489,13 @@ class DeviceCompute:
         cache.offset += 1  # the graph advanced the device position
         return static_wire, static_h
 
-    def _capture(self, cache, first: bool, last: bool):
-        st = self.stage
-        H = self.hidden_dim
-        static_in = (torch.zeros((1, 1), dtype=torch.int32, device=self.device) if first
-                     else self.wire_empty(1).zero_())
-        static_wire = None if last else self.wire_empty(1)
-        static_h = torch.empty((1, 1, H), dtype=torch.float32, device=self.device)
+    def _capture(self, m, cache, first: bool, last: bool):
+        static_in, static_wire, static_h = self.statics(m, first, last)
         side = torch.cuda.Stream(self.device)
         side.wait_stream(torch.cuda.current_stream(self.device))
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph, stream=side, capture_error_mode="thread_local"):
-            h = st.embed(static_in) if first else self.from_wire(static_in)
-            h = h.reshape(1, H).contiguous()
-            for i in range(len(st.layers)):
-                st.layer_forward(i, h, cache, 1)
-            if len(st.layers):
-                st._check(st.lib.hq4_advance_position(cache.pos.data_ptr(), 1, st._stream()),
-                          "hq4_advance_position")
-            if static_wire is not None:
-                self._encode_into(h, static_wire)
-            static_h.copy_(h.view(1, 1, H))
+            self.record_step(m, cache, first, last)
         torch.cuda.current_stream(self.device).wait_stream(side)
         return static_in, static_wire, static_h, graph
 
@@ -423,6 +542,13 @@ class DeviceCompute:
         self._check(self.lib.hq4_argmax_pair(self.logits.data_ptr(), self.hi - self.lo, self.lo,
                                              self.pair.data_ptr(), st), "argmax_pair")
         return self.pair
+
+    def pick_next(self, pairs, world: int, tok, history_row, count) -> None:
+        """Global token from the gathered pairs into tok[0] and
+        history_row[count[0]]; count[0] advances (device counter)."""
+        st = torch.cuda.current_stream(self.device).cuda_stream
+        self._check(self.lib.hq4_pick_token_next(pairs.data_ptr(), world, tok.data_ptr(), history_row.data_ptr(),
+                                                 count.data_ptr(), history_row.numel(), st), "pick_token_next")
 
     def pick_into(self, pairs, world: int, history_row, slot: int):
         """Global token from the gathered pairs, written to history_row[slot]."""

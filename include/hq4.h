@@ -264,6 +264,13 @@ int hq4_argmax_pair(const float* x, int n, int offset, int* pair, void* stream);
  * unsharded logits vector on the host). */
 int hq4_pick_token(const int* pairs, int world, int* tok, int* history, int slot, void* stream);
 
+/* hq4_pick_token whose history slot is a device counter: writes the token to
+ * *tok and to history[*count] (when *count < hist_len), then advances
+ * *count, so a CUDA graph that holds the call appends one token per replay.
+ * No reference counterpart (the reference appends on the host). */
+int hq4_pick_token_next(const int* pairs, int world, int* tok, int* history, int* count, int hist_len,
+                        void* stream);
+
 /* *pos += delta on the device (advances the decode position inside a graph). */
 int hq4_advance_position(int* pos, int delta, void* stream);
 

@@ -55,6 +55,7 @@ def _rank_main(rank, world, port, case, q):
         pr.prefill(prompts)
         pr.decode(case["steps"])
         torch.cuda.synchronize()
+        pr.close()  # its graphs hold NCCL calls: release them before the process group goes
         q.put((rank, pr.tokens))
     finally:
         dist.destroy_process_group()
