@@ -346,7 +346,7 @@ decode_kernel(const DecPhase* __restrict__ phases, const CUtensorMap* __restrict
             str_epi_prefetch_late(p, ns, s0, warp, lane, epi_pos);
             asm volatile("bar.sync 1, 512;" ::: "memory");  // slots cleared before any warp adds into them
             StrAcc acc = {0.0f, 0.0f, 0.0f, 0.0f};
-            str_consume(p, base, full_bar(0), empty_bar(0), R, slot, phase, ok, ns, nkb, nk, img_w, zero_blk,
+            str_consume<false>(p, base, full_bar(0), empty_bar(0), R, slot, phase, ok, ns, nkb, nk, img_w, zero_blk,
                         partials, ns_max, warp, lane, acc);
             if (!ok && lane == 0 && status) atomicOr(status, 1);
             str_finish(p, partials, ns, ns_max, s0, ok, acc, warp, lane);

@@ -526,7 +526,7 @@ gemv_stream_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_consta
     int slot = 0;
     uint32_t phase = 0;
     StrAcc acc = {0.0f, 0.0f, 0.0f, 0.0f};
-    str_consume(p, base, full_bar(0), empty_bar(0), R, slot, phase, ok, ns, nkb, nk, img_w, base + L.zero_off(),
+    str_consume<true>(p, base, full_bar(0), empty_bar(0), R, slot, phase, ok, ns, nkb, nk, img_w, base + L.zero_off(),
                 partials, L.ns_max, warp, lane, acc);
     if (!ok && lane == 0 && p.status) atomicOr(p.status, 1);
     str_finish(p, partials, ns, L.ns_max, s0, ok, acc, warp, lane);

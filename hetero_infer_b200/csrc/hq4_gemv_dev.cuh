@@ -225,7 +225,8 @@ __device__ __forceinline__ void str_load_nw(const GemvM1Params& p, int kc, int n
 
 // Digit image of chunk kc (k-block kb of this warp) from its x values
 // (normalised first when `norm`).  Image format: per lane-group the digit
-// blocks d2, d1, d0 of 64 bytes in k-step order, then (2^(E-22), xsum).
+// blocks d2, d1, d0 of 64 bytes (four 16-byte units, one per word pair),
+// then (2^(E-22), xsum).
 __device__ __forceinline__ void str_build_chunk(const GemvM1Params& p, unsigned char* img_w, int kb, int kc,
                                                 int lane, const float (&xin)[8], const float (&n8)[8], bool norm,
                                                 float norm_r) {
@@ -261,9 +262,18 @@ __device__ __forceinline__ void str_build_chunk(const GemvM1Params& p, unsigned 
     const uint32_t o11 = prmt(prmt(r[1], r[3], 0x5140), prmt(r[5], r[7], 0x5140), 0x7632);
     const uint32_t o21 = prmt(prmt(r[1], r[3], 0x0062), prmt(r[5], r[7], 0x0062), 0x5410);
     unsigned char* gb = img_w + (size_t)kb * kStrImgBytes + bq * C::kImgStride;
-    *reinterpret_cast<uint2*>(gb + 0 * 64 + bp * 8) = make_uint2(e21, o21);
-    *reinterpret_cast<uint2*>(gb + 1 * 64 + bp * 8) = make_uint2(e11, o11);
-    *reinterpret_cast<uint2*>(gb + 2 * 64 + bp * 8) = make_uint2(e01, o01);
+    // Each 16-byte unit of a digit block holds words 2i and 2i+1 of the
+    // group as (even digits of 2i, even of 2i+1, odd of 2i, odd of 2i+1): the
+    // B register pairs of the even-nibble and the odd-nibble MMA.  Neighbour
+    // lanes (words 2i, 2i+1) swap halves so each stores 8 contiguous bytes.
+    const bool odd_w = bp & 1;
+    unsigned char* u = gb + (bp >> 1) * 16 + (odd_w ? 8 : 0);
+    const uint32_t x2 = __shfl_xor_sync(0xffffffffu, odd_w ? e21 : o21, 1);
+    const uint32_t x1 = __shfl_xor_sync(0xffffffffu, odd_w ? e11 : o11, 1);
+    const uint32_t x0 = __shfl_xor_sync(0xffffffffu, odd_w ? e01 : o01, 1);
+    *reinterpret_cast<uint2*>(u + 0 * 64) = odd_w ? make_uint2(x2, o21) : make_uint2(e21, x2);
+    *reinterpret_cast<uint2*>(u + 1 * 64) = odd_w ? make_uint2(x1, o11) : make_uint2(e11, x1);
+    *reinterpret_cast<uint2*>(u + 2 * 64) = odd_w ? make_uint2(x0, o01) : make_uint2(e01, x0);
     if (bp == 0) *reinterpret_cast<float2*>(gb + C::kMetaOff) = make_float2(exp2i(E - kXBits), s);
 }
 
@@ -378,19 +388,43 @@ __device__ __forceinline__ StrLane str_lane(const GemvM1Params& p, int warp, int
     return L;
 }
 
-// One stage's tile for this warp (k-chunk `warp` of the stage, image `img`
+// The x side of a warp's tiles for one k-chunk: the lane's B fragments of
+// the three digit blocks (zero where its column belongs to another lane-group
+// or digit) and the group's (2^(E-22), xsum).  Loaded once per k-block and
+// kept in registers across every strip of that k-block.
+struct StrB {
+    uint4 q0[4], q1[4];  // c0 columns (d2 | d1) and c1 columns (d0 | 0), word pairs 0..3
+    float2 meta;
+};
+
+__device__ __forceinline__ void str_load_b(const StrLane& L, const unsigned char* img,
+                                           const unsigned char* zero_blk, StrB& B) {
+    using C = M1<64>;
+    const unsigned char* gb = img + L.t * C::kImgStride;
+    const uint4* src0 = reinterpret_cast<const uint4*>(L.role ? gb + L.off0 : zero_blk);
+    const uint4* src1 = reinterpret_cast<const uint4*>(L.role == 1 ? gb + 128 : zero_blk);
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        B.q0[i] = src0[i];
+        B.q1[i] = src1[i];
+    }
+    B.meta = *reinterpret_cast<const float2*>(gb + C::kMetaOff);
+}
+
+// One stage's tile for this warp (k-chunk `warp` of the stage, x fragments B
 // of that chunk): the lane's shares of rows g and g+8, zero when its
 // lane-group lies past the row end (gok false).  Exact digit dots on the
 // integer tensor cores, then scale * dot * 2^(E-22) + bias * xsum in fp32.
-__device__ __forceinline__ void str_tile(const StrLane& L, const unsigned char* st, const unsigned char* img,
-                                         const unsigned char* zero_blk, bool gok, int warp, float& a0f,
-                                         float& a1f) {
-    using C = M1<64>;
+//
+// A packed word gives two A registers with one mask each: the even nibbles
+// (w & 0x0F0F0F0F) and the odd nibbles left in place, i.e. 16 x their value
+// (w & 0xF0F0F0F0).  One MMA takes the even nibbles of words ks and ks+1
+// against their x digits, another the odd ones; the odd chain's sums are
+// exact multiples of 16 (|sum| < 2^20), so (odd >> 4) + even is the exact
+// integer column dot, identical to unpacking both nibbles to 0..15.
+__device__ __forceinline__ void str_tile(const StrLane& L, const unsigned char* st, const StrB& B, bool gok,
+                                         int warp, float& a0f, float& a1f) {
     const int g = L.g, t = L.t;
-    const unsigned char* gb = img + t * C::kImgStride;
-    const uint4* src0 = reinterpret_cast<const uint4*>(L.role ? gb + L.off0 : zero_blk);
-    const uint4* src1 = reinterpret_cast<const uint4*>(L.role == 1 ? gb + 128 : zero_blk);
-    const float2 meta = *reinterpret_cast<const float2*>(gb + C::kMetaOff);
     const unsigned char* wt = st + warp * kStrTileBytes;
     // rows g and g+8; 16-byte chunks 2t and 2t+1 of the row, swizzled
     const int c0 = ((2 * t) ^ g) << 4, c1 = ((2 * t + 1) ^ g) << 4;
@@ -398,37 +432,43 @@ __device__ __forceinline__ void str_tile(const StrLane& L, const unsigned char* 
     const uint4 rc = lds128(wt + (g + 8) * 128 + c0), rd = lds128(wt + (g + 8) * 128 + c1);
     const uint32_t w0[8] = {ra.x, ra.y, ra.z, ra.w, rb.x, rb.y, rb.z, rb.w};
     const uint32_t w1[8] = {rc.x, rc.y, rc.z, rc.w, rd.x, rd.y, rd.z, rd.w};
-    int c0e[4] = {0, 0, 0, 0}, c0o[4] = {0, 0, 0, 0}, c1e[4] = {0, 0, 0, 0}, c1o[4] = {0, 0, 0, 0};
+    constexpr uint32_t kLo = 0x0F0F0F0Fu, kHi = 0xF0F0F0F0u;
+    int c0l[4], c1l[4], c0h[4], c1h[4];
 #pragma unroll
-    for (int ks = 0; ks < C::kKSteps; ks += 2) {
-        const uint4 q0 = src0[ks >> 1], q1 = src1[ks >> 1];
-        uint32_t a0, a1, a2, a3;
-        unpack_u8(w0[ks], a0, a2);
-        unpack_u8(w1[ks], a1, a3);
-        mma_u8s8_16832(c0e, a0, a1, a2, a3, q0.x, q0.y);
-        mma_u8s8_16832(c1e, a0, a1, a2, a3, q1.x, q1.y);
-        unpack_u8(w0[ks + 1], a0, a2);
-        unpack_u8(w1[ks + 1], a1, a3);
-        mma_u8s8_16832(c0o, a0, a1, a2, a3, q0.z, q0.w);
-        mma_u8s8_16832(c1o, a0, a1, a2, a3, q1.z, q1.w);
+    for (int ks = 0; ks < M1<64>::kKSteps; ks += 2) {
+        const uint4 q0 = B.q0[ks >> 1], q1 = B.q1[ks >> 1];
+        const uint32_t l0 = w0[ks] & kLo, l1 = w1[ks] & kLo, l2 = w0[ks + 1] & kLo, l3 = w1[ks + 1] & kLo;
+        const uint32_t h0 = w0[ks] & kHi, h1 = w1[ks] & kHi, h2 = w0[ks + 1] & kHi, h3 = w1[ks + 1] & kHi;
+        if (ks == 0) {
+            mma_u8s8_16832_first(c0l, l0, l1, l2, l3, q0.x, q0.y);
+            mma_u8s8_16832_first(c1l, l0, l1, l2, l3, q1.x, q1.y);
+            mma_u8s8_16832_first(c0h, h0, h1, h2, h3, q0.z, q0.w);
+            mma_u8s8_16832_first(c1h, h0, h1, h2, h3, q1.z, q1.w);
+        } else {
+            mma_u8s8_16832(c0l, l0, l1, l2, l3, q0.x, q0.y);
+            mma_u8s8_16832(c1l, l0, l1, l2, l3, q1.x, q1.y);
+            mma_u8s8_16832(c0h, h0, h1, h2, h3, q0.z, q0.w);
+            mma_u8s8_16832(c1h, h0, h1, h2, h3, q1.z, q1.w);
+        }
     }
     const unsigned char* ss = st + kStrWBytes;
     const unsigned char* sbi = st + kStrWBytes + kStrSBBytes;
     a0f = 0.0f;
     a1f = 0.0f;
     if (gok) {
-        const float dot0 = fmaf((float)(c0e[0] + c0o[0]), 65536.0f,
-                                fmaf((float)(c0e[1] + c0o[1]), 256.0f, (float)(c1e[0] + c1o[0])));
-        const float dot1 = fmaf((float)(c0e[2] + c0o[2]), 65536.0f,
-                                fmaf((float)(c0e[3] + c0o[3]), 256.0f, (float)(c1e[2] + c1o[2])));
+        // column dots (d2, d1, d0) of rows g and g+8
+        const int d2a = c0l[0] + (c0h[0] >> 4), d1a = c0l[1] + (c0h[1] >> 4), d0a = c1l[0] + (c1h[0] >> 4);
+        const int d2b = c0l[2] + (c0h[2] >> 4), d1b = c0l[3] + (c0h[3] >> 4), d0b = c1l[2] + (c1h[2] >> 4);
+        const float dot0 = fmaf((float)d2a, 65536.0f, fmaf((float)d1a, 256.0f, (float)d0a));
+        const float dot1 = fmaf((float)d2b, 65536.0f, fmaf((float)d1b, 256.0f, (float)d0b));
         const float s0 = h2f(*reinterpret_cast<const uint16_t*>(ss + L.sbo0));
         const float b0 = h2f(*reinterpret_cast<const uint16_t*>(sbi + L.sbo0));
         const float s1 = h2f(*reinterpret_cast<const uint16_t*>(ss + L.sbo1));
         const float b1 = h2f(*reinterpret_cast<const uint16_t*>(sbi + L.sbo1));
-        a0f = fmaf(s0 * meta.x, dot0, 0.0f);
-        a0f = fmaf(b0, meta.y, a0f);
-        a1f = fmaf(s1 * meta.x, dot1, 0.0f);
-        a1f = fmaf(b1, meta.y, a1f);
+        a0f = fmaf(s0 * B.meta.x, dot0, 0.0f);
+        a0f = fmaf(b0, B.meta.y, a0f);
+        a1f = fmaf(s1 * B.meta.x, dot1, 0.0f);
+        a1f = fmaf(b1, B.meta.y, a1f);
     }
 }
 
@@ -437,6 +477,10 @@ __device__ __forceinline__ void str_tile(const StrLane& L, const unsigned char* 
 // phase), which it advances.  `stages` is the ring's first stage, `full` /
 // `empty` the barrier addresses of slot 0 (8 bytes apart).  A wait that
 // runs out clears ok; a slot whose copy never arrived is not handed back.
+// kHoistB keeps the x fragments of a k-block in registers across its strips
+// (34 registers); without it they are reloaded per tile, for kernels with
+// less register room.
+template <bool kHoistB>
 __device__ __forceinline__ void str_consume(const GemvM1Params& p, const unsigned char* stages, uint32_t full,
                                             uint32_t empty, int R, int& slot, uint32_t& phase, bool& ok, int ns,
                                             int nkb, int nk, const unsigned char* img_w,
@@ -450,13 +494,16 @@ __device__ __forceinline__ void str_consume(const GemvM1Params& p, const unsigne
     for (int kb = 0; kb < nkb; kb++) {
         const int kc = kb * kStrKc + warp;
         const bool active = kc < nk;
-        const unsigned char* img = img_w + (size_t)kb * kStrImgBytes;
         const bool gok = kc * 4 + t < p.ng;
+        const unsigned char* img = img_w + (size_t)kb * kStrImgBytes;
+        StrB B;
+        if (kHoistB && active) str_load_b(L, img, zero_blk, B);
         for (int j = 0; j < ns; j++) {
             if (ok && !mbar_wait_tries(full + 8u * slot, phase, kStrTryHintNs, kStrTries)) ok = false;
             if (ok && active) {
                 float a0f, a1f;
-                str_tile(L, stages + (size_t)slot * kStrStageBytes, img, zero_blk, gok, warp, a0f, a1f);
+                if (!kHoistB) str_load_b(L, img, zero_blk, B);
+                str_tile(L, stages + (size_t)slot * kStrStageBytes, B, gok, warp, a0f, a1f);
                 if (regacc) {
                     if (j == 0) {
                         acc.r00 += a0f;
@@ -466,15 +513,16 @@ __device__ __forceinline__ void str_consume(const GemvM1Params& p, const unsigne
                         acc.r11 += a1f;
                     }
                 } else {
-                    a0f += __shfl_xor_sync(0xffffffffu, a0f, 1);
-                    a0f += __shfl_xor_sync(0xffffffffu, a0f, 2);
-                    a1f += __shfl_xor_sync(0xffffffffu, a1f, 1);
-                    a1f += __shfl_xor_sync(0xffffffffu, a1f, 2);
-                    if (t == 0) {
-                        float* slotp = partials + ((size_t)warp * ns_max + j) * 16;
-                        slotp[g] += a0f;
-                        slotp[g + 8] += a1f;
-                    }
+                    // sums over the 4 lanes t of rows g and g+8 in three steps:
+                    // even t keeps row g, odd t row g+8, each taking its partner's
+                    // share of that row, then the pair two lanes away; lane t=0
+                    // ends with row g, t=1 with row g+8 (the additions of the
+                    // plain xor tree, in the same order)
+                    const bool odd = t & 1;
+                    float keep = odd ? a1f : a0f;
+                    keep += __shfl_xor_sync(0xffffffffu, odd ? a0f : a1f, 1);
+                    keep += __shfl_xor_sync(0xffffffffu, keep, 2);
+                    if (t < 2) partials[((size_t)warp * ns_max + j) * 16 + g + 8 * t] += keep;
                 }
             }
             __syncwarp();
