@@ -162,99 +162,134 @@ def _stage_time(node: NodeProfile, spec: ShardSpec, head_share: float = 0.0) -> 
 def plan_pipeline(index, nodes: List[NodeProfile], link: LinkSpec, objective: str = "throughput",
                   max_ctx: int = 4096, batch: int = 1, codec: str = "fp16",
                   kv_dtype_bytes: int = 2) -> Plan:
-    """Head on stage N-1 or 0, whichever predicts faster (planner.py:118-140)."""
-    best, best_cost, err = None, float("inf"), None
-    for head_at in ({len(nodes) - 1, 0} if len(nodes) > 1 else {len(nodes) - 1}):
+    """Head on the last stage or on stage 0, whichever predicts faster
+    (planner.py:118-140); the placements are tried in the reference's order
+    and the first of two equal predictions is kept."""
+    best, err = None, None
+    for head_at in _head_placements(len(nodes)):
         try:
             p = _plan(index, nodes, link, head_at, objective, max_ctx, batch, codec, kv_dtype_bytes)
         except MemoryError as e:
             err = e
             continue
-        if p.predicted_decode_s < best_cost:
-            best, best_cost = p, p.predicted_decode_s
+        if best is None or p.predicted_decode_s < best.predicted_decode_s:
+            best = p
     if best is None:
         raise err
     return best
 
 
+def _head_placements(n: int) -> List[int]:
+    # the reference iterates the set {n - 1, 0}; keep its iteration order
+    return list({n - 1, 0}) if n > 1 else [n - 1]
+
+
+class _StageCosts:
+    """Every per-stage term of one head placement, shared by the cut search
+    and by the finished plan: head_at is the stage owning the vocabulary
+    projection, or -1 when it is row-sharded over all N stages (each then
+    pays head_s / N, holds 1/N of its bytes and joins two collectives per
+    token: the broadcast of the last stage's fp32 hidden state and the
+    all-gather of the N (value, index) pairs)."""
+
+    def __init__(self, index, nodes, link, head_at, max_ctx, batch, codec, kv_dtype_bytes, sharded):
+        cfg = index.config
+        self.index, self.nodes, self.head_at, self.sharded = index, nodes, head_at, sharded
+        self.n = len(nodes)
+        self.kv = kv_bytes_per_layer(cfg, max_ctx, batch, kv_dtype_bytes)
+        self.hand_off = link.seconds_for(hidden_bytes(cfg, tokens=1, batch=batch, codec=codec) + 96)
+        self.token_back = link.seconds_for(96)
+        self.head_part = index.head_bytes() // self.n if sharded else 0
+        self.head_coll = (link.seconds_for(int(cfg["hidden_size"]) * 4) + link.seconds_for(8 * self.n)
+                          if sharded else 0.0)
+
+    def spec(self, i: int, start: int, end: int) -> ShardSpec:
+        return ShardSpec(start, end, i == 0, i == self.head_at)
+
+    def mem(self, i: int, spec: ShardSpec) -> int:
+        return _resident(self.index, spec, self.nodes[i].weight_expansion) + spec.n_layers * self.kv + self.head_part
+
+    def compute(self, i: int, spec: ShardSpec) -> float:
+        share = self.nodes[i].head_s / self.n + self.head_coll if self.sharded else 0.0
+        return _stage_time(self.nodes[i], spec, share)
+
+    def send(self, i: int) -> float:
+        """What stage i ships on: a hidden state to the next stage; the last
+        stage returns a token id, or a hidden state when stage 0 owns the head."""
+        if i < self.n - 1 or self.head_at == 0:
+            return self.hand_off
+        return self.token_back
+
+
+def _cut_search(costs: _StageCosts, n_layers: int, objective: str) -> List[int]:
+    """Cut points [0, c1, ..., L] of the cheapest feasible split.
+
+    A backward pass over the stages keeps, for every first layer c of the
+    stages i.., the best (cost, sum of squared stage times, next cut).  A
+    stage's cost is its time plus what it sends, combined with the rest by max
+    (throughput) or sum (latency), plus 1e-12 (mem / budget)^8 so that equal
+    costs go to the split with the most memory headroom; the first cut
+    reaching the minimum wins, as in the reference (planner.py:180-205).  With
+    a sharded head a near-tie is broken by the smaller sum of squared stage
+    times, so identical GPUs get balanced stages."""
+    join = max if objective == "throughput" else (lambda a, b: a + b)
+    INF = float("inf")
+    rest = {n_layers: (0.0, 0.0, None)}  # nothing left for the stages after the last
+    tables = []
+    for i in range(costs.n - 1, -1, -1):
+        budget = costs.nodes[i].mem_bytes
+        here = {}
+        for c in range(n_layers + 1):
+            cost_b, sq_b, cut_b = INF, INF, -1
+            for c2 in range(c, n_layers + 1):
+                after = rest.get(c2)
+                if after is None:
+                    continue
+                spec = costs.spec(i, c, c2)
+                m = costs.mem(i, spec)
+                if m > budget:
+                    continue
+                t = costs.compute(i, spec) + costs.send(i)
+                cost = join(t, after[0])
+                cost += 1e-12 * (m / budget) ** 8
+                if costs.sharded:
+                    sq = after[1] + t * t
+                    near = abs(cost - cost_b) <= 1e-9 * max(cost, 1e-30)
+                    take = (cost < cost_b and not near) or (near and sq < sq_b)
+                else:
+                    sq, take = 0.0, cost < cost_b
+                if take:
+                    cost_b, sq_b, cut_b = cost, sq, c2
+            if cut_b >= 0:
+                here[c] = (cost_b, sq_b, cut_b)
+        tables.append(here)
+        rest = here
+    if 0 not in rest:
+        raise MemoryError(f"no feasible split of {costs.index.total_bytes() / 2**30:.2f} GiB over {costs.n} nodes")
+    cuts = [0]
+    for here in reversed(tables):  # stage 0 first
+        cuts.append(here[cuts[-1]][2])
+    return cuts
+
+
 def _plan(index, nodes, link, head_at, objective, max_ctx, batch, codec, kv_dtype_bytes,
           sharded_head: bool = False) -> Plan:
-    """The DP over cut points for one head placement (planner.py:143-217).
+    """The cut search for one head placement (planner.py:143-217).
 
     head_at = -1 with sharded_head: no stage owns the whole head; every stage
     pays head_s / N and holds 1/N of its bytes."""
-    cfg = index.config
-    L = int(cfg["num_hidden_layers"])
-    N = len(nodes)
-    if N < 2:
+    if len(nodes) < 2:
         raise ValueError("need at least two nodes to split a model")
-    kv = kv_bytes_per_layer(cfg, max_ctx, batch, kv_dtype_bytes)
-    act = hidden_bytes(cfg, tokens=1, batch=batch, codec=codec)
-    comm = link.seconds_for(act + 96)
-    ret_comm = link.seconds_for(96)
-    head_share_bytes = index.head_bytes() // N if sharded_head else 0
-    INF = float("inf")
-    best = [[INF] * (L + 1) for _ in range(N + 1)]
-    # secondary key for the sharded-head GPU plan: sum of squared stage times,
-    # so that among splits with the same slowest stage the balanced one wins
-    # (identical GPUs tie on the throughput objective alone)
-    sq = [[INF] * (L + 1) for _ in range(N + 1)]
-    choice = [[-1] * (L + 1) for _ in range(N + 1)]
-    best[N][L] = 0.0
-    sq[N][L] = 0.0
-
-    def combine(a, b):
-        return max(a, b) if objective == "throughput" else a + b
-
-    def mem(i, spec):
-        return _resident(index, spec, nodes[i].weight_expansion) + spec.n_layers * kv + head_share_bytes
-
-    # a row-sharded head costs every stage, every token, its share of the
-    # head GEMV plus the two collectives that join the shards: the broadcast
-    # of the last stage's fp32 hidden state and the all-gather of the N
-    # (value, index) pairs
-    head_coll = (link.seconds_for(int(cfg["hidden_size"]) * 4) + link.seconds_for(8 * N)) if sharded_head else 0.0
-
-    def share(i):
-        return nodes[i].head_s / N + head_coll if sharded_head else 0.0
-
-    for i in range(N - 1, -1, -1):
-        node = nodes[i]
-        for c in range(L + 1):
-            for c2 in range(c, L + 1):
-                if best[i + 1][c2] == INF:
-                    continue
-                spec = ShardSpec(c, c2, i == 0, i == head_at)
-                m = mem(i, spec)
-                if m > node.mem_bytes:
-                    continue
-                out = (comm if head_at == 0 else ret_comm) if i == N - 1 else comm
-                t = _stage_time(node, spec, share(i)) + out
-                cost = combine(t, best[i + 1][c2])
-                cost += 1e-12 * (m / node.mem_bytes) ** 8
-                if sharded_head:
-                    s2 = sq[i + 1][c2] + t * t
-                    close = abs(cost - best[i][c]) <= 1e-9 * max(cost, 1e-30)
-                    if cost < best[i][c] and not close or (close and s2 < sq[i][c]):
-                        best[i][c], sq[i][c], choice[i][c] = cost, s2, c2
-                elif cost < best[i][c]:
-                    best[i][c] = cost
-                    choice[i][c] = c2
-    if best[0][0] == INF:
-        raise MemoryError(f"no feasible split of {index.total_bytes() / 2**30:.2f} GiB over {N} nodes")
-    cuts, c = [0], 0
-    for i in range(N):
-        c = choice[i][c]
-        cuts.append(c)
-    specs = [ShardSpec(cuts[i], cuts[i + 1], i == 0, i == head_at) for i in range(N)]
+    costs = _StageCosts(index, nodes, link, head_at, max_ctx, batch, codec, kv_dtype_bytes, sharded_head)
+    cuts = _cut_search(costs, int(index.config["num_hidden_layers"]), objective)
+    specs = [costs.spec(i, cuts[i], cuts[i + 1]) for i in range(len(nodes))]
     plan = Plan(cuts=cuts, nodes=nodes, specs=specs, objective=objective, head_node=head_at)
-    plan.stage_compute_s = [_stage_time(n, s, share(i)) for i, (n, s) in enumerate(zip(nodes, specs))]
-    plan.stage_comm_s = [(comm if head_at == 0 else ret_comm) if i == N - 1 else comm for i in range(N)]
-    plan.stage_mem_bytes = [mem(i, s) for i, s in enumerate(specs)]
-    if objective == "throughput":
-        plan.predicted_decode_s = max(a + b for a, b in zip(plan.stage_compute_s, plan.stage_comm_s))
-    else:
-        plan.predicted_decode_s = sum(plan.stage_compute_s) + sum(plan.stage_comm_s)
+    plan.stage_compute_s = [costs.compute(i, s) for i, s in enumerate(specs)]
+    plan.stage_comm_s = [costs.send(i) for i in range(len(nodes))]
+    plan.stage_mem_bytes = [costs.mem(i, s) for i, s in enumerate(specs)]
+    totals = [a + b for a, b in zip(plan.stage_compute_s, plan.stage_comm_s)]
+    plan.predicted_decode_s = max(totals) if objective == "throughput" else (
+        sum(plan.stage_compute_s) + sum(plan.stage_comm_s))
     return plan
 
 
