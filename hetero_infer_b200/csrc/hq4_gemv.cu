@@ -959,6 +959,18 @@ extern "C" int hq4_gemv_ex(const uint32_t* w, const uint16_t* scales, const uint
     return HQ4_OK;
 }
 
+// x rows from pinned, device-mapped host memory into the device staging
+// buffer, one float4 per thread.  It triggers its dependents at once, so the
+// GEMV launched after it (PDL) starts its CTAs and streams its first weight
+// stages while x crosses the host link; the GEMV reads x only after this
+// kernel completes (its dependency wait).
+__global__ void __launch_bounds__(256) host_x_kernel(const float4* __restrict__ src, float4* __restrict__ dst,
+                                                     int n4) {
+    pdl_launch_dependents();
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n4) dst[i] = src[i];
+}
+
 extern "C" int hq4_gemv_host(const uint32_t* w, const uint16_t* scales, const uint16_t* biases,
                              const float* row_add, const float* x_host, float* out_host, int n_out, int n_in,
                              int gs, int m, float* x_dev, float* out_dev, void* stream) {
@@ -977,7 +989,22 @@ extern "C" int hq4_gemv_host(const uint32_t* w, const uint16_t* scales, const ui
         out_direct = static_cast<float*>(pa.devicePointer);
     else
         (void)cudaGetLastError();  // an unregistered pointer is not an error here
-    if (cudaMemcpyAsync(x_dev, x_host, in_bytes, cudaMemcpyHostToDevice, st) != cudaSuccess) return HQ4_ERR_LAUNCH;
+    // A pinned, device-mapped x is fetched by a small kernel instead of a copy,
+    // so the GEMV's weight stream starts while x is in flight (a copy would
+    // have to finish before the GEMV could start).  Other host memory is copied.
+    const float4* x_direct = nullptr;
+    if ((in_bytes & 15) == 0 && ((uintptr_t)x_dev & 15) == 0 && cudaPointerGetAttributes(&pa, x_host) == cudaSuccess &&
+        pa.type == cudaMemoryTypeHost && pa.devicePointer && ((uintptr_t)pa.devicePointer & 15) == 0)
+        x_direct = static_cast<const float4*>(pa.devicePointer);
+    else
+        (void)cudaGetLastError();
+    if (x_direct) {
+        const int n4 = (int)(in_bytes / 16);
+        host_x_kernel<<<(n4 + 255) / 256, 256, 0, st>>>(x_direct, reinterpret_cast<float4*>(x_dev), n4);
+        if (cudaGetLastError() != cudaSuccess) return HQ4_ERR_LAUNCH;
+    } else if (cudaMemcpyAsync(x_dev, x_host, in_bytes, cudaMemcpyHostToDevice, st) != cudaSuccess) {
+        return HQ4_ERR_LAUNCH;
+    }
     if (int rc = hq4_gemv_fused(w, scales, biases, x_dev, out_direct ? out_direct : out_dev, n_out, n_in, gs, m,
                                 row_add, nullptr, stream))
         return rc;

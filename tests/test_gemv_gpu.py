@@ -224,8 +224,10 @@ def test_gemv_ex_weights_written_by_the_preceding_kernel(cuda, oracle, n_out, n_
 @pytest.mark.gpu
 def test_gemv_host_pinned_output_written_by_the_kernel(cuda, oracle):
     """hq4_gemv_host writes a pinned (device-mapped) output straight from the
-    GEMV's epilogue and copies into any other host buffer: both give the same
-    bits, equal to the device path, for several calls in a row."""
+    GEMV's epilogue and copies into any other host buffer, and fetches a
+    pinned x with a kernel ahead of the GEMV but copies any other x: every
+    combination gives the same bits, equal to the device path, for several
+    calls in a row."""
     import torch
     from hetero_infer_b200 import _lib
     lib = _lib.load()
@@ -251,4 +253,8 @@ def test_gemv_host_pinned_output_written_by_the_kernel(cuda, oracle):
         assert lib.hq4_gemv_host(wd.data_ptr(), sd.data_ptr(), bd.data_ptr(), None, xh.data_ptr(),
                                  pageable.ctypes.data, n_out, n_in, gs, 1, dx.data_ptr(), dy.data_ptr(), st) == 0
         assert np.array_equal(pageable, ref)
+        pinned.fill_(float("nan"))
+        assert lib.hq4_gemv_host(wd.data_ptr(), sd.data_ptr(), bd.data_ptr(), None, x.ctypes.data, pinned.data_ptr(),
+                                 n_out, n_in, gs, 1, dx.data_ptr(), dy.data_ptr(), st) == 0  # pageable x
+        assert np.array_equal(pinned.numpy(), ref)
     assert rel_l2(ref, oracle.gemv_f32(w, s, b, x, gs)) <= OUR_TOL
