@@ -87,7 +87,10 @@ int hq4_gemv_ex(const uint32_t* w, const uint16_t* scales, const uint16_t* biase
  * out_dev are caller-owned device buffers of at least m*n_in and m*n_out
  * floats; pinned host buffers keep the copies at full speed.  When out_host
  * is pinned and mapped for the device (cudaHostAlloc / pinned tensors), the
- * kernel writes the products into it directly and out_dev is not used. */
+ * kernel writes the products into it directly and out_dev is not used; when
+ * x_host is pinned and mapped (and 16-byte aligned), a small kernel fetches
+ * it into x_dev instead of a copy, and the GEMV streams its first weights
+ * while that kernel runs. */
 int hq4_gemv_host(const uint32_t* w, const uint16_t* scales, const uint16_t* biases,
                   const float* row_add, const float* x_host, float* out_host, int n_out, int n_in,
                   int gs, int m, float* x_dev, float* out_dev, void* stream);
