@@ -759,6 +759,7 @@ def profile_case(which: str) -> None:
       gemm    hq4_gemm_w4a16 on 18944x3584 at 4 tokens (multi-token
               streaming kernel), 16 tokens (register-path kernel) and 256
               tokens (tcgen05 kernel), bf16 activations, three calls each;
+      gemm_down  the same on the down shape, 3584x18944;
       decode  the 7B-shape stage's decode step, per-layer launches, 4 steps
               after a 4-token prompt.
 
@@ -784,8 +785,8 @@ def profile_case(which: str) -> None:
             for (w, s_, b), x, y, n, k in mats[r % 2]:
                 _lib.check(lib.hq4_gemv(w.data_ptr(), s_.data_ptr(), b.data_ptr(), x.data_ptr(), y.data_ptr(),
                                         n, k, GS, 1, st), "hq4_gemv")
-    elif which == "gemm":
-        n, k = 18944, 3584
+    elif which in ("gemm", "gemm_down"):
+        n, k = (18944, 3584) if which == "gemm" else (3584, 18944)
         w, s_, b = q4(n, k)
         for m in (4, 16, 256):
             x = torch.randn(m, k, device=dev, generator=g).to(torch.bfloat16)
@@ -819,7 +820,7 @@ def main():
                     help="N>1: only run the config-5 pipeline (TOKENS per stream, 4 and 8 streams)")
     ap.add_argument("--decode-only", type=int, default=0, metavar="TOKENS",
                     help="only run the config-4 decode (TOKENS generated) and print its JSON")
-    ap.add_argument("--case", choices=["layer", "gemm", "decode"], default=None,
+    ap.add_argument("--case", choices=["layer", "gemm", "gemm_down", "decode"], default=None,
                     help="run one short fixed case for a profiler capture and exit")
     args = ap.parse_args()
     if args.case:
