@@ -78,6 +78,7 @@ class QLinear:
         self._ptrs = (self.w.data_ptr(), self.scales.data_ptr(), self.biases.data_ptr(),
                       None if self.bias is None else self.bias.data_ptr())
         self._stage = None  # (rows, pinned x, pinned y, device x, device y, x view, y view)
+        self._calls = {}    # rows -> (pinned x view, pinned y view, C-call arguments)
         self._dev_idx = None
         self._host_fn = _lib.load().hq4_gemv_host
 
@@ -108,10 +109,15 @@ class QLinear:
         # host-buffer contract
         xa = np.asarray(x, dtype=np.float32)
         lead = xa.shape[:-1]
-        flat = xa.reshape(-1, self.n_in)
+        flat = xa if xa.ndim == 2 else xa.reshape(-1, self.n_in)
+        if flat.shape[-1] != self.n_in:
+            raise ValueError(f"x has {flat.shape[-1]} features, the layer takes {self.n_in}")
         m = flat.shape[0]
-        *_, hxn, hyn, (hxp, hyp, dxp, dyp) = self._staging(m)
-        np.copyto(hxn[:m], flat)
+        call = self._calls.get(m)
+        if call is None:
+            call = self._host_call(m)
+        hx, hy, args = call
+        np.copyto(hx, flat)
         idx = self._dev_idx
         if idx is None:
             idx = self._dev_idx = (self.device.index if self.device.index is not None
@@ -119,12 +125,23 @@ class QLinear:
         if torch.cuda.current_device() != idx:
             with torch.cuda.device(idx):
                 return self.__call__(x)
-        w, s, b, bias = self._ptrs
-        rc = self._host_fn(w, s, b, bias, hxp, hyp, self.n_out, self.n_in, self.group_size, m, dxp, dyp,
-                           _raw_stream(idx))
+        rc = self._host_fn(*args, _raw_stream(idx))
         if rc:
             _lib.check(rc, "hq4_gemv_host")
-        return hyn[:m].copy().reshape(*lead, self.n_out)
+        y = hy.copy()
+        return y if len(lead) == 1 else y.reshape(*lead, self.n_out)
+
+    def _host_call(self, m: int):
+        """(pinned x view, pinned y view, hq4_gemv_host arguments but the
+        stream) for m rows, kept per row count."""
+        before = self._stage
+        *_, hxn, hyn, (hxp, hyp, dxp, dyp) = self._staging(m)
+        if self._stage is not before:
+            self._calls.clear()  # the staging grew: calls cached on the old buffers are stale
+        w, s, b, bias = self._ptrs
+        call = (hxn[:m], hyn[:m], (w, s, b, bias, hxp, hyp, self.n_out, self.n_in, self.group_size, m, dxp, dyp))
+        self._calls[m] = call
+        return call
 
 
 # ---------------------------------------------------------------------------

@@ -175,6 +175,13 @@ def test_qlinear_host_path_matches_oracle(oracle, cuda, m, with_bias):
     y2 = q(x[0]) if m == 1 else None          # a 1-D activation keeps its shape
     if y2 is not None:
         assert y2.shape == (n_out,) and np.array_equal(y2, y[0])
+    if m == 3:
+        # one row after three (the pinned staging was sized for three), then
+        # four rows (it grows), then one row again: each call as on its own
+        y1 = q(x[:1])
+        y4 = q(np.concatenate([x, x[:1]]))
+        assert np.array_equal(q(x[:1]), y1) and y4.shape == (4, n_out)
+        assert rel_l2(y1, oracle.gemv_f32(w, s, b, x[:1], gs) + (0 if bias is None else bias)) <= OUR_TOL
 
 
 @pytest.mark.gpu
