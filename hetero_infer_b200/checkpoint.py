@@ -8,8 +8,10 @@ of the files (no intermediate copy) and uploaded by `cuda_model.Stage`;
 `stage_from_snapshot` does both.
 
 The ownership rules and the dtype size table are the reference's (they
-define the checkpoint format and the planner's accounting, so they are kept
-alike); the reading is this module's own.
+define the checkpoint format and the planner's accounting, so the results
+are kept alike; here each tensor is classified once into a part of the
+model and the byte counts are sums over parts); the reading is this
+module's own.
 """
 from __future__ import annotations
 
@@ -47,6 +49,18 @@ def read_header(path: str) -> Tuple[Dict[str, dict], int]:
     return head, 8 + n
 
 
+def _part(name: str):
+    """The part of the model a tensor name belongs to: its decoder layer's
+    index, "embed", "head", or None for a name outside the format."""
+    if name.startswith("model.layers."):
+        return int(name.split(".")[2])
+    if name.startswith("model.embed_tokens"):
+        return "embed"
+    if name.startswith("lm_head") or name == "model.norm.weight":
+        return "head"
+    return None
+
+
 class WeightIndex:
     """name -> (file, dtype, shape, bytes) across a snapshot directory, plus the
     snapshot's config.json (hetero/shard.py:72-158)."""
@@ -58,6 +72,7 @@ class WeightIndex:
             raise FileNotFoundError(f"no safetensors in {model_dir}")
         self.entries: Dict[str, Tuple[str, str, List[int], int]] = {}
         self._where: Dict[str, Tuple[int, int]] = {}  # name -> (absolute begin, end) in its file
+        self._parts: Dict[str, object] = {}  # name -> layer index, "embed", "head" or None
         for path in files:
             head, data0 = read_header(path)
             for name, meta in head.items():
@@ -68,6 +83,7 @@ class WeightIndex:
                     raise ValueError(f"{path}: {name} holds {e - b} bytes, its shape needs {nb}")
                 self.entries[name] = (path, meta["dtype"], shape, nb)
                 self._where[name] = (data0 + int(b), data0 + int(e))
+                self._parts[name] = _part(name)
         with open(os.path.join(model_dir, "config.json")) as f:
             self.config = json.load(f)
 
@@ -76,14 +92,26 @@ class WeightIndex:
         """Tied embeddings: the head stage reuses the embedding matrix."""
         return bool(self.config.get("tie_word_embeddings", False))
 
-    def owns(self, name: str, spec) -> bool:
-        if name.startswith("model.layers."):
-            return spec.start <= int(name.split(".")[2]) < spec.end
-        if name.startswith("model.embed_tokens"):
-            return spec.embed or (self.tied and spec.head)  # a tied head keeps its own copy
-        if name.startswith("lm_head") or name == "model.norm.weight":
+    # Every tensor belongs to one part of the model: a decoder layer (its
+    # index), the embedding table, or the head (lm_head and the final norm).
+    # A stage owns its layers' range, the embedding when it embeds, the head
+    # when it samples -- and, with tied embeddings, the head stage also holds
+    # its own copy of the table.  Byte counts are sums over parts.
+    def _part_of(self, name: str):
+        part = self._parts.get(name, _part(name))
+        if part is None:
+            raise KeyError(f"unclassified tensor {name}")
+        return part
+
+    def _owns_part(self, part, spec) -> bool:
+        if part == "embed":
+            return spec.embed or (self.tied and spec.head)
+        if part == "head":
             return spec.head
-        raise KeyError(f"unclassified tensor {name}")
+        return spec.start <= part < spec.end
+
+    def owns(self, name: str, spec) -> bool:
+        return self._owns_part(self._part_of(name), spec)
 
     def names(self) -> List[str]:
         return list(self.entries)
@@ -91,26 +119,32 @@ class WeightIndex:
     def nbytes(self, name: str) -> int:
         return self.entries[name][3]
 
-    def layer_bytes(self) -> List[int]:
-        out = [0] * int(self.config["num_hidden_layers"])
+    def _part_bytes(self) -> Dict[object, int]:
+        tot: Dict[object, int] = {}
         for name, (_, _, _, nb) in self.entries.items():
-            if name.startswith("model.layers."):
-                out[int(name.split(".")[2])] += nb
-        return out
+            part = self._parts[name]
+            tot[part] = tot.get(part, 0) + nb
+        return tot
+
+    def layer_bytes(self) -> List[int]:
+        tot = self._part_bytes()
+        return [tot.get(i, 0) for i in range(int(self.config["num_hidden_layers"]))]
 
     def embed_bytes(self) -> int:
-        return sum(nb for n, (_, _, _, nb) in self.entries.items() if n.startswith("model.embed_tokens"))
+        return self._part_bytes().get("embed", 0)
 
     def head_bytes(self) -> int:
-        b = sum(nb for n, (_, _, _, nb) in self.entries.items()
-                if n.startswith("lm_head") or n == "model.norm.weight")
-        return b + (self.embed_bytes() if self.tied else 0)
+        tot = self._part_bytes()
+        return tot.get("head", 0) + (tot.get("embed", 0) if self.tied else 0)
 
     def total_bytes(self) -> int:
         return sum(nb for _, _, _, nb in self.entries.values())
 
     def shard_bytes(self, spec) -> int:
-        return sum(nb for n, (_, _, _, nb) in self.entries.items() if self.owns(n, spec))
+        tot = self._part_bytes()
+        if None in tot:
+            self._part_of(next(n for n, p in self._parts.items() if p is None))  # raises
+        return sum(nb for part, nb in tot.items() if self._owns_part(part, spec))
 
     def load_shard(self, spec) -> Dict[str, np.ndarray]:
         """This stage's tensors only, as arrays mapped from the files."""
