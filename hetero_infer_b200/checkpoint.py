@@ -73,6 +73,7 @@ class WeightIndex:
         self.entries: Dict[str, Tuple[str, str, List[int], int]] = {}
         self._where: Dict[str, Tuple[int, int]] = {}  # name -> (absolute begin, end) in its file
         self._parts: Dict[str, object] = {}  # name -> layer index, "embed", "head" or None
+        self._tot = None                     # part -> bytes, built on first use
         for path in files:
             head, data0 = read_header(path)
             for name, meta in head.items():
@@ -120,11 +121,13 @@ class WeightIndex:
         return self.entries[name][3]
 
     def _part_bytes(self) -> Dict[object, int]:
-        tot: Dict[object, int] = {}
-        for name, (_, _, _, nb) in self.entries.items():
-            part = self._parts[name]
-            tot[part] = tot.get(part, 0) + nb
-        return tot
+        if self._tot is None:  # the index does not change after construction
+            tot: Dict[object, int] = {}
+            for name, (_, _, _, nb) in self.entries.items():
+                part = self._parts[name]
+                tot[part] = tot.get(part, 0) + nb
+            self._tot = tot
+        return self._tot
 
     def layer_bytes(self) -> List[int]:
         tot = self._part_bytes()
