@@ -242,6 +242,8 @@ def test_gemv_host_pinned_output_written_by_the_kernel(cuda, oracle):
     w, s, b, x = make_case(n_out, n_in, gs, seed=77)
     wd, sd, bd = to_dev(w), to_dev(s), to_dev(b)
     xh = torch.from_numpy(x).pin_memory()
+    xh_odd = torch.empty(n_in + 1).pin_memory()  # x at a 4-byte offset into a pinned buffer
+    xh_odd[1:] = torch.from_numpy(x.reshape(-1))
     dx = torch.empty(1, n_in, device="cuda")
     dy = torch.empty(1, n_out, device="cuda")
     st = torch.cuda.current_stream().cuda_stream
@@ -263,5 +265,10 @@ def test_gemv_host_pinned_output_written_by_the_kernel(cuda, oracle):
         pinned.fill_(float("nan"))
         assert lib.hq4_gemv_host(wd.data_ptr(), sd.data_ptr(), bd.data_ptr(), None, x.ctypes.data, pinned.data_ptr(),
                                  n_out, n_in, gs, 1, dx.data_ptr(), dy.data_ptr(), st) == 0  # pageable x
+        assert np.array_equal(pinned.numpy(), ref)
+        pinned.fill_(float("nan"))
+        assert lib.hq4_gemv_host(wd.data_ptr(), sd.data_ptr(), bd.data_ptr(), None, xh_odd[1:].data_ptr(),
+                                 pinned.data_ptr(), n_out, n_in, gs, 1, dx.data_ptr(), dy.data_ptr(),
+                                 st) == 0  # pinned x off a 16-byte boundary: copied
         assert np.array_equal(pinned.numpy(), ref)
     assert rel_l2(ref, oracle.gemv_f32(w, s, b, x, gs)) <= OUR_TOL
