@@ -172,8 +172,7 @@ decode_kernel(const DecPhase* __restrict__ phases, const CUtensorMap* __restrict
                 pns = 0;
                 if (d.kind == kPhGemv) {
                     const int n = d.p.n_strips;
-                    ps0 = (int)(blockIdx.x * (uint32_t)n / G);
-                    pns = (int)((blockIdx.x + 1) * (uint32_t)n / G) - ps0;
+                    str_strips((int)blockIdx.x, n, (int)G, ps0, pns);
                     pnkb = d.nkb;
                     pshift = d.p.sg_shift;
                     if (pns > 0) {
@@ -333,8 +332,8 @@ decode_kernel(const DecPhase* __restrict__ phases, const CUtensorMap* __restrict
             }
             const GemvM1Params& p = d.p;
             const int n = p.n_strips;
-            const int s0 = (int)(blockIdx.x * (uint32_t)n / G);
-            const int ns = (int)((blockIdx.x + 1) * (uint32_t)n / G) - s0;
+            int s0, ns;
+            str_strips((int)blockIdx.x, n, (int)G, s0, ns);
             if (ns == 0) continue;
             const int ns_max = (int)((n + G - 1) / G);
             const int nk = (p.ng + 3) >> 2, nkb = d.nkb;

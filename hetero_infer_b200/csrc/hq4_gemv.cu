@@ -435,9 +435,8 @@ gemv_stream_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_consta
     const uint32_t images_bar = bars + 8u * (2 * R);  // every consumer warp's x images are built
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int s0 = (int)(blockIdx.x * (uint32_t)p.n_strips / gridDim.x);
-    const int s1 = (int)((blockIdx.x + 1) * (uint32_t)p.n_strips / gridDim.x);
-    const int ns = s1 - s0;
+    int s0, ns;
+    str_strips((int)blockIdx.x, p.n_strips, (int)gridDim.x, s0, ns);
     const int nk = (p.ng + 3) >> 2;              // k-chunks of 4 lane-groups
     const int nkb = (nk + kStrKc - 1) / kStrKc;  // stages per strip
     const int n_stages = nkb * ns;

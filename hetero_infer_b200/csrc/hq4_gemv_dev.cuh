@@ -158,6 +158,17 @@ __device__ __forceinline__ void store_pair(const GemvM1Params& p, int s, int g, 
 }
 
 
+// Strips [s0, s0 + ns) of CTA b when n strips are split over G CTAs: every
+// CTA takes n / G, and the first n % G take one more.  A launch's CTAs start
+// in index order as the previous kernel's CTAs leave their SMs (the last ones
+// also behind a short kernel such as attention), so the extra strips go to
+// the CTAs that start first.
+__host__ __device__ __forceinline__ void str_strips(int b, int n, int G, int& s0, int& ns) {
+    const int q = n / G, extra = n - q * G;
+    s0 = b * q + (b < extra ? b : extra);
+    ns = q + (b < extra ? 1 : 0);
+}
+
 constexpr int kStrConsumers = 16;
 constexpr int kStrThreads = (kStrConsumers + 1) * kWarp;  // + one producer warp
 constexpr int kStrKc = kStrConsumers;                      // k-chunks per stage (one per consumer warp)
